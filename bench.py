@@ -1,0 +1,316 @@
+"""Benchmark: batch-1 decode through every packed linear of a Llama-3-8B-shaped model.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step is one decode token: all 32 x 7 codebook-quantized linears of the
+Llama-3-8B shapes (indices u8 per 4-weight vector, 256x4 fp16 codebook, fp16
+scale per row per 128 weights; 1.85 GB of indices), visited in layer order
+with each launch reading the previous one's output.  The packed weights
+(1.9 GB) are far larger than the 126 MB L2, so every step streams them from
+HBM; no L2 flush is needed.  Attention, norms and the bf16 lm_head are not
+part of the packed-linear path and are not in the step.
+
+Our arm replays the step as a CUDA graph of libepq.so launches (value), and
+separately through the public runner with host buffers (e2e: pinned H2D copy
+of the token input, replay, D2H copy of the output, every step).  At N > 1
+each rank runs an independent replica on its own GPU (weak scaling; the 8B
+model fits one GPU, so there is no collective on the data path); the time is
+the max over ranks.
+
+The reference arm (--impl reference) runs the reference's fused CPU kernel
+(kernel/src/lib.rs, restated in C under oracle/) on the host cores: each step
+is one layer's 7 linears with f32 activations, and tokens/s is scaled by the
+32 layers.  Rank 0 alone runs it.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "epure-runtime_b200"))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode tok/s bs1 @8B; dequant-GEMV HBM GB/s as % of B200 peak"
+UNIT = "tok/s"
+WORKLOAD = "llama3-8b packed linears, batch-1 decode token (224 linears, 128 launches)"
+
+# dram__bytes_read.sum + dram__bytes_write.sum per gemv_lut_kernel launch, from
+# the ncu capture summarised in profiles/gemv_lut_kernel_llama3-8b_decode.md
+# (None until a capture exists).
+NCU_TRAFFIC_PER_STEP = None
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples for one GPU during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out = ""
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": ["no samples"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# CPU reference arm / CPU baseline
+# ---------------------------------------------------------------------------
+def cpu_reference_sample(seconds=10.0, threads=0, steps=None, warmup=1):
+    """Time the lib.rs restatement on one 8B layer; returns (tok/s, info)."""
+    import numpy as np
+    from oracle import oracle as O
+    from epure import synthetic
+
+    O.build_c_oracle()
+    rng = np.random.default_rng(0)
+    layer = []
+    for name, n, k in synthetic.LLAMA3_8B.linears():
+        idx = rng.integers(0, 256, (n, k // 4), dtype=np.uint8)
+        cb = rng.standard_normal((256, 4)).astype(np.float16).astype(np.float32)
+        sc = np.abs(rng.normal(0, 0.02, (n, k // 128))).astype(np.float16).astype(np.float32)
+        x = rng.standard_normal((1, k)).astype(np.float32)
+        layer.append((x, idx, sc, cb, n, k))
+
+    def one_layer():
+        for x, idx, sc, cb, n, k in layer:
+            O.c_dequant_matmul(x, idx, sc, cb, n, k, 4, 128, 256, threads=threads)
+
+    for _ in range(warmup):
+        one_layer()
+    times = []
+    t_total = time.perf_counter()
+    while True:
+        t0 = time.perf_counter()
+        one_layer()
+        times.append(time.perf_counter() - t0)
+        if steps is not None:
+            if len(times) >= steps:
+                break
+        elif time.perf_counter() - t_total >= seconds:
+            break
+    per_layer = statistics.median(times)
+    tok_s = 1.0 / (per_layer * synthetic.LLAMA3_8B.layers)
+    used = threads if threads > 0 else O.c_threads()
+    info = {"cores": used, "kind": "port",
+            "sample": f"1 of 32 layers (7 linears, f32 activations), {len(times)} timed "
+                      f"repetitions, median {per_layer*1e3:.1f} ms/layer; tok/s = 1/(32 x layer)"}
+    return tok_s, info
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return 0
+    tok_s, info = cpu_reference_sample(steps=args.steps, warmup=args.warmup)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(tok_s, 4), "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1000.0 / tok_s, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "global_batch": 1, "parallelism": "host threads",
+                   "l2": "n/a (CPU)"},
+        "cpu_baseline": {"value": round(tok_s, 4), "unit": UNIT, **info},
+        "e2e": {"value": round(tok_s, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    from epure import synthetic
+    from epure.decode import GraphedLinearStack
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    shapes = synthetic.LLAMA3_8B
+    stack = synthetic.LinearStack(shapes, device=dev, seed=1000 * rank)
+    runner = GraphedLinearStack(stack, m=1, dtype=torch.bfloat16, device=dev).capture()
+    g = torch.Generator(device=dev).manual_seed(rank)
+    runner.x.copy_(torch.randn(runner.x.shape, generator=g, device=dev).to(torch.bfloat16))
+    step_bytes = stack.algorithmic_bytes(m=1, act_bytes=2)
+    launches = runner.launches_per_step
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        runner.replay()
+    torch.cuda.synchronize(dev)
+
+    # device-resident: K graph replays between two events on the replay stream
+    barrier()
+    torch.cuda.synchronize(dev)
+    stream = torch.cuda.current_stream(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            runner.replay()
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    ms = max_over_ranks(ev0.elapsed_time(ev1)) / args.steps
+
+    # end to end through the public runner with host buffers
+    x_host = torch.empty(runner.x.shape, dtype=runner.x.dtype, pin_memory=True)
+    x_host.copy_(runner.x.cpu())
+    out_host = torch.empty(runner.out.shape, dtype=runner.out.dtype, pin_memory=True)
+    for _ in range(args.warmup):
+        runner(x_host, out_host)
+    torch.cuda.synchronize(dev)
+    barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    e0.record(stream)
+    for _ in range(args.steps):
+        runner(x_host, out_host)
+        stream.synchronize()            # the host reads each token's output
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    wall_ms = (time.perf_counter() - t0) * 1e3 / args.steps
+    barrier()
+    e2e_ms = max_over_ranks(max(e0.elapsed_time(e1) / args.steps, wall_ms))
+
+    hbm_peak, peak_kind = _peaks()
+    achieved_gbs = step_bytes / (ms * 1e-3) / 1e9
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": round(world * 1000.0 / ms, 2),
+            "unit": UNIT,
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms, 5),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": WORKLOAD, "global_batch": world, "seq_len": 1,
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "l2": "inputs larger than L2 (1.9 GB of packed weights per step)",
+                       "bytes_per_step": step_bytes},
+            "roofline": {"bound": "hbm", "achieved": round(achieved_gbs, 1),
+                         "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(achieved_gbs / hbm_peak, 4),
+                         "peak_kind": peak_kind,
+                         "kernel": "gemv_lut_kernel (all launches of the step)",
+                         "launch_avg_us": round(ms * 1e3 / launches, 3),
+                         "traffic": NCU_TRAFFIC_PER_STEP},
+            "e2e": {"value": round(world * 1000.0 / e2e_ms, 2), "unit": UNIT,
+                    "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
+                    "d2h_bytes_per_step": out_host.numel() * out_host.element_size()},
+            "gpu_launches": launches * args.steps,
+            "clocks": clocks.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            tok_s, info = cpu_reference_sample(seconds=args.cpu_seconds)
+            line["cpu_baseline"] = {"value": round(tok_s, 4), "unit": UNIT, **info}
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        from datetime import timedelta
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        return run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    sys.exit(main())

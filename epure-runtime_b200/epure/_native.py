@@ -1,0 +1,260 @@
+"""ctypes binding of libepq.so, the C-ABI CUDA library (include/epq.h).
+
+This is the only module that touches the native library.  It turns torch
+tensors into the plain pointers and sizes of the C ABI, owns the per-stream
+workspaces the batch-1 kernel needs, and raises ``RuntimeError`` with the
+library's own message whenever a call returns a non-zero status.  There is no
+fallback: if the library is missing, every GPU call raises.
+"""
+import ctypes
+import os
+import threading
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libepq.so")
+
+EPQ_F32, EPQ_F16, EPQ_BF16 = 0, 1, 2
+LAYOUT_ROWS, LAYOUT_TILED = 0, 1
+
+_DT = {torch.float32: EPQ_F32, torch.float16: EPQ_F16, torch.bfloat16: EPQ_BF16}
+
+
+class EpqStore(ctypes.Structure):
+    _fields_ = [
+        ("idx", ctypes.c_void_p),
+        ("layout", ctypes.c_int32),
+        ("bits", ctypes.c_int32),
+        ("vec", ctypes.c_int32),
+        ("levels", ctypes.c_int32),
+        ("group", ctypes.c_int32),
+        ("cb_dtype", ctypes.c_int32),
+        ("cb", ctypes.c_void_p),
+        ("scale_dtype", ctypes.c_int32),
+        ("reserved0", ctypes.c_int32),
+        ("scale", ctypes.c_void_p),
+        ("scale_stride_n", ctypes.c_int64),
+        ("scale_stride_g", ctypes.c_int64),
+        ("n", ctypes.c_int64),
+        ("k", ctypes.c_int64),
+    ]
+
+
+EXPORTS = (
+    "epq_abi_version", "epq_last_error", "epq_device_error", "epq_tiled_bytes",
+    "epq_relayout_tiled", "epq_linear_workspace_bytes", "epq_linear_multi", "epq_linear",
+    "epq_linear_bwd", "epq_materialize",
+)
+
+_lib = None
+_lock = threading.Lock()
+
+
+def load_library(path=None):
+    """Load libepq.so (once) and declare its signatures.  Raises if it is absent."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        path = path or LIB_PATH
+        if not os.path.exists(path):
+            raise RuntimeError(
+                f"epure: the CUDA library {path} is not built; run "
+                "`python epure-runtime_b200/build_native.py` (or __graft_entry__.build()).")
+        lib = ctypes.CDLL(path)
+        P, I32, I64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64
+        SP = ctypes.POINTER(EpqStore)
+        lib.epq_abi_version.restype = ctypes.c_int
+        lib.epq_last_error.restype = ctypes.c_char_p
+        lib.epq_device_error.argtypes = [ctypes.POINTER(ctypes.c_int)]
+        lib.epq_tiled_bytes.restype = I64
+        lib.epq_tiled_bytes.argtypes = [I64, I64, I32, I32]
+        lib.epq_relayout_tiled.argtypes = [P, I64, I64, I32, I32, P, P]
+        lib.epq_linear_workspace_bytes.argtypes = [SP, I32, I64, ctypes.POINTER(I64)]
+        lib.epq_linear_multi.argtypes = [SP, I32, P, I32, I64, I64, P, P, I32, P, I64, P]
+        lib.epq_linear.argtypes = [SP, P, I32, I64, I64, P, I64, I32, P, I64, P]
+        lib.epq_linear_bwd.argtypes = [SP, P, I64, P, I64, I32, I64, P, I64, I32, P, P, P]
+        lib.epq_materialize.argtypes = [SP, P, I64, I32, P]
+        for name in EXPORTS:
+            getattr(lib, name)          # every declared entry point must be exported
+        if lib.epq_abi_version() != 1:
+            raise RuntimeError(f"epure: {path} has ABI {lib.epq_abi_version()}, expected 1")
+        _lib = lib
+        return lib
+
+
+def _check(rc, what):
+    if rc != 0:
+        msg = _lib.epq_last_error().decode(errors="replace")
+        raise RuntimeError(f"epure: {what} failed (status {rc}): {msg}")
+
+
+def dtype_code(dt):
+    try:
+        return _DT[dt]
+    except KeyError:
+        raise TypeError(f"epure: dtype {dt} is not supported by the CUDA kernels") from None
+
+
+def _stream_ptr(device):
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+# ---------------------------------------------------------------------------
+# store description
+# ---------------------------------------------------------------------------
+def describe_store(store):
+    """The C ``epq_store`` for a PackedWeight (cached until a buffer changes)."""
+    packed, scale, cb = store.packed, store.scale, store.cb
+    key = (id(packed), packed.data_ptr(), id(scale), scale.data_ptr(), scale.dtype,
+           id(cb), cb.data_ptr(), cb.dtype, store.layout)
+    hit = store.__dict__.get("_epq_desc")
+    if hit is not None and hit[0] == key:
+        return hit[1]
+    if scale.dim() != 2:
+        raise RuntimeError("epure: scale must be 2-D [rows, groups]")
+    d = EpqStore()
+    d.idx = packed.data_ptr()
+    d.layout = LAYOUT_TILED if store.layout == "tiled" else LAYOUT_ROWS
+    d.bits = 4 if (store.vec == 1 and store.levels <= 16) else 8
+    d.vec = store.vec
+    d.levels = store.levels
+    d.group = store.group
+    d.cb_dtype = dtype_code(cb.dtype)
+    d.cb = cb.data_ptr()
+    d.scale_dtype = dtype_code(scale.dtype)
+    d.scale = scale.data_ptr()
+    d.scale_stride_n = scale.stride(0)
+    d.scale_stride_g = scale.stride(1)
+    d.n = store.out_features
+    d.k = store.in_features
+    if not cb.is_contiguous():
+        raise RuntimeError("epure: codebook must be contiguous")
+    store.__dict__["_epq_desc"] = (key, d, (packed, scale, cb))
+    return d
+
+
+# ---------------------------------------------------------------------------
+# workspaces: one zero-filled buffer per (device, stream), grown on demand
+# ---------------------------------------------------------------------------
+_workspaces = {}
+
+
+def workspace(device, stream_ptr, nbytes):
+    if nbytes <= 0:
+        return None, 0
+    key = (device.index if device.index is not None else torch.cuda.current_device(), stream_ptr)
+    buf = _workspaces.get(key)
+    if buf is None or buf.numel() < nbytes:
+        size = max(nbytes, 1 << 20)
+        buf = torch.zeros(size, dtype=torch.uint8, device=device)
+        _workspaces[key] = buf
+    return buf, buf.numel()
+
+
+def reserve_workspace(stores, m=1, device=None):
+    """Allocate the workspace a later call will need (before CUDA graph capture)."""
+    lib = load_library()
+    descs = (EpqStore * len(stores))(*[describe_store(s) for s in stores])
+    need = ctypes.c_int64(0)
+    _check(lib.epq_linear_workspace_bytes(descs, len(stores), m, ctypes.byref(need)),
+           "epq_linear_workspace_bytes")
+    device = device or stores[0].packed.device
+    workspace(device, _stream_ptr(device), need.value)
+    return need.value
+
+
+# ---------------------------------------------------------------------------
+# calls
+# ---------------------------------------------------------------------------
+def linear_multi(x, stores, out_dtype=None, outs=None):
+    """``[x @ W_i^T for each store]`` in one launch; all stores share x (same k)."""
+    lib = load_library()
+    if not x.is_cuda:
+        raise RuntimeError("epure: linear_multi needs a CUDA activation")
+    k = stores[0].in_features
+    shape = x.shape
+    x2 = x.reshape(-1, shape[-1])
+    if x2.shape[-1] != k:
+        raise RuntimeError(f"epure: activation has {x2.shape[-1]} features, store expects {k}")
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    m = x2.shape[0]
+    out_dtype = out_dtype or x.dtype
+    count = len(stores)
+    descs = (EpqStore * count)(*[describe_store(s) for s in stores])
+    if outs is None:
+        outs = [torch.empty((m, s.out_features), dtype=out_dtype, device=x.device) for s in stores]
+    out_ptrs = (ctypes.c_void_p * count)(*[o.data_ptr() for o in outs])
+    ldo = (ctypes.c_int64 * count)(*[o.stride(0) if o.dim() == 2 else s.out_features
+                                     for o, s in zip(outs, stores)])
+    stream = _stream_ptr(x.device)
+    need = ctypes.c_int64(0)
+    _check(lib.epq_linear_workspace_bytes(descs, count, m, ctypes.byref(need)),
+           "epq_linear_workspace_bytes")
+    ws, ws_bytes = workspace(x.device, stream, need.value)
+    rc = lib.epq_linear_multi(descs, count, x2.data_ptr(), dtype_code(x2.dtype), m,
+                              x2.stride(0), out_ptrs, ldo, dtype_code(out_dtype),
+                              ws.data_ptr() if ws is not None else None, ws_bytes, stream)
+    _check(rc, "epq_linear_multi")
+    return [o.reshape(*shape[:-1], s.out_features) for o, s in zip(outs, stores)]
+
+
+def linear(x, store, out_dtype=None):
+    return linear_multi(x, [store], out_dtype)[0]
+
+
+def linear_bwd(x, dy, store, need_dx=True, need_dscale=True, need_dcb=True):
+    """(dx, dscale [n, ng] f32, dcb [levels*vec] f32) of ``sum(dy * (x @ W^T))``."""
+    lib = load_library()
+    k, n = store.in_features, store.out_features
+    x2 = x.reshape(-1, k).contiguous()
+    dy2 = dy.reshape(-1, n).to(x2.dtype).contiguous()
+    m = x2.shape[0]
+    dev = x.device
+    d = describe_store(store)
+    dx = torch.empty((m, k), dtype=x.dtype, device=dev) if need_dx else None
+    ng = -(-k // store.group)
+    dscale = torch.empty((n, ng), dtype=torch.float32, device=dev) if need_dscale else None
+    dcb = torch.empty(store.levels * store.vec, dtype=torch.float32, device=dev) \
+        if need_dcb else None
+    rc = lib.epq_linear_bwd(
+        ctypes.byref(d), x2.data_ptr(), x2.stride(0), dy2.data_ptr(), dy2.stride(0),
+        dtype_code(x2.dtype), m, dx.data_ptr() if dx is not None else None, k,
+        dtype_code(x.dtype), dscale.data_ptr() if dscale is not None else None,
+        dcb.data_ptr() if dcb is not None else None, _stream_ptr(dev))
+    _check(rc, "epq_linear_bwd")
+    return (dx.reshape(*x.shape[:-1], k) if dx is not None else None), dscale, dcb
+
+
+def materialize(store, dtype):
+    lib = load_library()
+    d = describe_store(store)
+    w = torch.empty((store.out_features, store.in_features), dtype=dtype,
+                    device=store.packed.device)
+    _check(lib.epq_materialize(ctypes.byref(d), w.data_ptr(), w.stride(0), dtype_code(dtype),
+                               _stream_ptr(w.device)), "epq_materialize")
+    return w
+
+
+def tiled_bytes(n, k, vec, group):
+    return int(load_library().epq_tiled_bytes(n, k, vec, group))
+
+
+def relayout_tiled(idx_rows, n, k, vec, group):
+    """Row-layout u8 indices on the GPU -> a new EPQ_LAYOUT_TILED buffer."""
+    lib = load_library()
+    src = idx_rows.contiguous()
+    nbytes = tiled_bytes(n, k, vec, group)
+    dst = torch.empty(nbytes, dtype=torch.uint8, device=src.device)
+    _check(lib.epq_relayout_tiled(src.data_ptr(), n, k, vec, group, dst.data_ptr(),
+                                  _stream_ptr(src.device)), "epq_relayout_tiled")
+    return dst
+
+
+def device_error():
+    lib = load_library()
+    flag = ctypes.c_int(0)
+    _check(lib.epq_device_error(ctypes.byref(flag)), "epq_device_error")
+    return flag.value

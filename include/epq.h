@@ -1,0 +1,171 @@
+/*
+ * epq.h -- C ABI of the B200 fused codebook dequant-matmul library (libepq.so).
+ *
+ * A packed weight ("store") is W[n, k] = cb[idx(n, k)] * scale[n, k / group]:
+ *   idx    uint8 codebook indices; one index per `vec` consecutive weights
+ *          along k (vec = 1: the reference's scalar codebook; vec = 4: a
+ *          4-weight vector codebook).  bits = 4 packs two scalar indices per
+ *          byte (even k in the low nibble), bits = 8 is one index per byte.
+ *   cb     `levels` entries of `vec` values (f32, f16 or bf16).
+ *   scale  one value per output row per group of `group` weights along k
+ *          (f16, f32 or bf16), addressed as scale[n * scale_stride_n +
+ *          g * scale_stride_g] (element strides).
+ *
+ * Everything here takes plain device pointers and sizes.  Nothing allocates
+ * or frees memory: callers pass output buffers and, where a kernel needs
+ * scratch, a workspace sized by the matching *_workspace_bytes query.  Every
+ * call is asynchronous on the given stream (a cudaStream_t passed as void*;
+ * NULL is the legacy default stream) and returns EPQ_OK or a negative
+ * epq_status; epq_last_error() then describes the failure.  The calls are
+ * safe to capture in a CUDA graph.
+ *
+ * Reference interfaces replaced (epure-runtime v0.2.4, paths in that project):
+ *   epq_linear / epq_linear_multi
+ *       epure/kernels/_triton.py:477  dequant_matmul(x, packed, scale, cb,
+ *                                     group, bits, n_out, k_in)  (GPU)
+ *       kernel/src/lib.rs:96          dequant_matmul(x, packed, scales, cb,
+ *                                     group, four_bit)            (CPU)
+ *       epure/kernels/cuda.py:88      linear(x, store)  -- the backend
+ *                                     contract; the ABI never declines, it
+ *                                     returns an error instead
+ *   epq_linear_bwd
+ *       the autograd of epure/runtime.py:78-89 (materialize) + F.linear used
+ *       by epure/finetune.py:49-102 (make_trainable) -- the reference has no
+ *       backward kernel
+ *   epq_materialize
+ *       epure/runtime.py:78-89        PackedWeight.materialize(dtype)
+ *   epq_relayout_tiled / epq_tiled_bytes
+ *       the re-layout step of epure/runtime.py:243-249 (apply_to builds the
+ *       store from the container's index stream)
+ */
+#ifndef EPQ_H
+#define EPQ_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define EPQ_ABI_VERSION 1
+
+/* Status codes.  0 is success; every failure is negative. */
+enum epq_status {
+    EPQ_OK = 0,
+    EPQ_EINVAL = -1,        /* null pointer, negative size, bad enum value   */
+    EPQ_ESHAPE = -2,        /* sizes inconsistent with each other            */
+    EPQ_EDTYPE = -3,        /* dtype not supported for this argument         */
+    EPQ_EALIGN = -4,        /* pointer or stride alignment not met           */
+    EPQ_ELAYOUT = -5,       /* index layout not supported for this call      */
+    EPQ_EWORKSPACE = -6,    /* workspace missing or smaller than required    */
+    EPQ_ELAUNCH = -7,       /* the CUDA launch failed                        */
+    EPQ_EUNSUPPORTED = -8,  /* combination of parameters not implemented     */
+    EPQ_ETIMEOUT = -9       /* a bounded device-side wait gave up            */
+};
+
+/* Element types. */
+enum epq_dtype { EPQ_F32 = 0, EPQ_F16 = 1, EPQ_BF16 = 2 };
+
+/* Index layouts.
+ *   EPQ_LAYOUT_ROWS   the reference's layout: the flat stream of runtime.py
+ *                     _pack4 over [n, k] (bits = 4: two per byte, even flat
+ *                     position low nibble; bits = 8: one per byte), or for
+ *                     vec = 4 one byte per vector, [n, k / 4] row-major.
+ *   EPQ_LAYOUT_TILED  the kernel-native layout for bits = 8.  With
+ *                     P = group / vec index positions per group, RB =
+ *                     ceil(n / 16) row blocks and NG = ceil(k / group) groups,
+ *                     the index of row r, position j lives at byte
+ *                       ((g * RB + rb) * P + l) * 16 + rr,
+ *                     g = j / P, l = j % P, rb = r / 16, rr = r % 16.  A
+ *                     16-row x P-position tile is contiguous, tiles run
+ *                     row-block fastest within a group.  Padding (rows >= n,
+ *                     positions >= k / vec) holds index 0.            */
+enum epq_layout { EPQ_LAYOUT_ROWS = 0, EPQ_LAYOUT_TILED = 1 };
+
+/* A packed weight, described by plain pointers (all device memory). */
+typedef struct epq_store {
+    const uint8_t* idx;       /* packed indices, `layout`                      */
+    int32_t layout;           /* enum epq_layout                               */
+    int32_t bits;             /* 4 or 8                                        */
+    int32_t vec;              /* weights per index: 1 or 4                     */
+    int32_t levels;           /* codebook entries (<= 16 for bits = 4, <= 256) */
+    int32_t group;            /* weights per scale along k (> 0)               */
+    int32_t cb_dtype;         /* enum epq_dtype                                */
+    const void* cb;           /* [levels * vec]                                */
+    int32_t scale_dtype;      /* enum epq_dtype                                */
+    int32_t reserved0;
+    const void* scale;        /* [n, ceil(k / group)] with the strides below   */
+    int64_t scale_stride_n;   /* element stride between rows                   */
+    int64_t scale_stride_g;   /* element stride between groups                 */
+    int64_t n;                /* output features (rows)                        */
+    int64_t k;                /* input features                                */
+} epq_store;
+
+/* ABI version of the loaded library (EPQ_ABI_VERSION it was built with). */
+int epq_abi_version(void);
+
+/* Human-readable description of the last failure on the calling host thread. */
+const char* epq_last_error(void);
+
+/* Reads (synchronously, on the current device) the flag a kernel sets when
+ * one of its in-kernel checks fails and it returns without writing output.
+ * *flag = 0 means no kernel has reported a failure. */
+int epq_device_error(int* flag);
+
+/* Bytes of an EPQ_LAYOUT_TILED index buffer for the given shape. */
+int64_t epq_tiled_bytes(int64_t n, int64_t k, int32_t vec, int32_t group);
+
+/* Re-lay an EPQ_LAYOUT_ROWS index buffer (bits = 8) into EPQ_LAYOUT_TILED.
+ * `dst` must hold epq_tiled_bytes(n, k, vec, group) bytes; padding is zeroed. */
+int epq_relayout_tiled(const uint8_t* src_rows, int64_t n, int64_t k, int32_t vec,
+                       int32_t group, uint8_t* dst_tiled, void* stream);
+
+/* Scratch needed by epq_linear_multi for these stores at `m` activation rows.
+ * The workspace must be zero-filled once after it is allocated; every call
+ * leaves its counter region zero again when it completes, so a workspace can
+ * be reused by later calls that are ordered after it (same stream, or a
+ * dependency).  Calls that overlap on the GPU need separate workspaces. */
+int epq_linear_workspace_bytes(const epq_store* stores, int32_t count, int64_t m,
+                               int64_t* bytes);
+
+/* out[i][m, n_i] = x[m, k] @ W_i[n_i, k]^T for `count` (1..4) stores that share
+ * the activation x (same k).  x: [m, k] with row stride ldx (elements),
+ * x_dtype f32/f16/bf16; outs[i]: [m, n_i] with row stride ldo[i], out_dtype
+ * f32/f16/bf16.  fp32 accumulation.  Batch-1 calls on EPQ_LAYOUT_TILED vector
+ * stores use the bandwidth-bound LUT kernel and need the workspace above. */
+int epq_linear_multi(const epq_store* stores, int32_t count, const void* x,
+                     int32_t x_dtype, int64_t m, int64_t ldx, void* const* outs,
+                     const int64_t* ldo, int32_t out_dtype, void* workspace,
+                     int64_t workspace_bytes, void* stream);
+
+/* Single-store form of epq_linear_multi. */
+int epq_linear(const epq_store* store, const void* x, int32_t x_dtype, int64_t m,
+               int64_t ldx, void* out, int64_t ldo, int32_t out_dtype, void* workspace,
+               int64_t workspace_bytes, void* stream);
+
+/* Backward of out = x @ W^T with the indices frozen.
+ *   dy [m, n] (ldy), x [m, k] (ldx): same dtype, f32/f16/bf16.
+ *   dx [m, k] (lddx, dx_dtype) = dy @ W        (skipped when dx is NULL)
+ *   dscale [n, ceil(k / group)] f32, dense row-major:
+ *       dscale[r, g] = sum_{k in g} dW[r, k] * cb[idx(r, k)]
+ *   dcb [levels * vec] f32:
+ *       dcb[e * vec + p] = sum over weights with index e, sub-position p of
+ *                          dW[r, k] * scale[r, k / group]
+ *   with dW = dy^T x never stored.  dscale / dcb are overwritten (skipped
+ *   when NULL).  They are reduced with float atomics, so their last bits can
+ *   vary from run to run. */
+int epq_linear_bwd(const epq_store* store, const void* x, int64_t ldx, const void* dy,
+                   int64_t ldy, int32_t act_dtype, int64_t m, void* dx, int64_t lddx,
+                   int32_t dx_dtype, float* dscale, float* dcb, void* stream);
+
+/* Dense W [n, k] (row stride ldw) in out_dtype with PackedWeight.materialize's
+ * rounding: cb and scale are first rounded to out_dtype, their product is
+ * rounded to out_dtype (runtime.py:85-88). */
+int epq_materialize(const epq_store* store, void* w, int64_t ldw, int32_t out_dtype,
+                    void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EPQ_H */
