@@ -45,10 +45,13 @@ int make_store(const epq_store* in, StoreD* s, const char* who) {
         return set_error(EPQ_ESHAPE, "%s: group=%d not a multiple of vec=%d", who, in->group, in->vec);
     if (!dtype_ok(in->cb_dtype) || !dtype_ok(in->scale_dtype))
         return set_error(EPQ_EDTYPE, "%s: cb/scale dtype must be f32, f16 or bf16", who);
-    if (in->layout != EPQ_LAYOUT_ROWS && in->layout != EPQ_LAYOUT_TILED)
+    if (in->layout != EPQ_LAYOUT_ROWS && in->layout != EPQ_LAYOUT_TILED &&
+        in->layout != EPQ_LAYOUT_MMA16)
         return set_error(EPQ_EINVAL, "%s: layout=%d", who, in->layout);
-    if (in->layout == EPQ_LAYOUT_TILED && in->bits != 8)
-        return set_error(EPQ_ELAYOUT, "%s: the tiled layout holds 8-bit indices only", who);
+    if (in->layout != EPQ_LAYOUT_ROWS && in->bits != 8)
+        return set_error(EPQ_ELAYOUT, "%s: tiled layouts hold 8-bit indices only", who);
+    if (in->layout == EPQ_LAYOUT_MMA16 && in->group / in->vec != 32)
+        return set_error(EPQ_ELAYOUT, "%s: EPQ_LAYOUT_MMA16 needs group / vec = 32", who);
     if (in->n > 0 && in->k > 0 && (!in->idx || !in->cb || !in->scale))
         return set_error(EPQ_EINVAL, "%s: idx, cb and scale must be non-NULL", who);
     s->idx = in->idx;
@@ -73,6 +76,7 @@ int make_store(const epq_store* in, StoreD* s, const char* who) {
 }
 
 int lut_read_device_error(int* flag);
+int mma_read_device_error(int* flag);
 
 static bool x_ok(const void* x, int64_t m, int64_t k, int64_t ldx) {
     return (m == 0 || k == 0) || (x != nullptr && ldx >= k);
@@ -90,25 +94,37 @@ const char* epq_last_error(void) { return g_err; }
 
 int epq_device_error(int* flag) {
     if (!flag) return set_error(EPQ_EINVAL, "epq_device_error: flag is NULL");
-    return lut_read_device_error(flag);
+    int lut = 0, mma = 0;
+    int rc = lut_read_device_error(&lut);
+    if (rc) return rc;
+    rc = mma_read_device_error(&mma);
+    if (rc) return rc;
+    *flag = (lut ? 1 : 0) | (mma ? 2 : 0);   // bit 0: LUT placement check, bit 1: a bounded wait gave up
+    return EPQ_OK;
 }
 
-int64_t epq_tiled_bytes(int64_t n, int64_t k, int32_t vec, int32_t group) {
-    if (n < 0 || k < 0 || (vec != 1 && vec != 4) || group <= 0 || group % vec) return -1;
-    return cdiv(k, group) * cdiv(n, 16) * (group / vec) * 16;
+int64_t epq_layout_bytes(int32_t layout, int64_t n, int64_t k, int32_t vec, int32_t group) {
+    if (n < 0 || k < 0 || (vec != 1 && vec != 4) || group <= 0 || group % vec || k % vec) return -1;
+    if (layout == EPQ_LAYOUT_MMA16 && group / vec != 32) return -1;
+    if (layout != EPQ_LAYOUT_TILED && layout != EPQ_LAYOUT_MMA16) return -1;
+    return layout_bytes(layout, n, k, vec, group);
 }
 
-int epq_relayout_tiled(const uint8_t* src_rows, int64_t n, int64_t k, int32_t vec, int32_t group,
-                       uint8_t* dst_tiled, void* stream) {
+int epq_relayout(const uint8_t* src_rows, int32_t layout, int64_t n, int64_t k, int32_t vec,
+                 int32_t group, uint8_t* dst, void* stream) {
     if (n < 0 || k < 0) return set_error(EPQ_EINVAL, "relayout: negative shape");
     if (vec != 1 && vec != 4) return set_error(EPQ_EUNSUPPORTED, "relayout: vec=%d", vec);
     if (group <= 0 || group % vec) return set_error(EPQ_ESHAPE, "relayout: group=%d vec=%d", group, vec);
     if (k % vec) return set_error(EPQ_ESHAPE, "relayout: k=%lld not a multiple of vec", (long long)k);
+    if (layout != EPQ_LAYOUT_TILED && layout != EPQ_LAYOUT_MMA16)
+        return set_error(EPQ_ELAYOUT, "relayout: target layout %d", layout);
+    if (layout == EPQ_LAYOUT_MMA16 && group / vec != 32)
+        return set_error(EPQ_ESHAPE, "relayout: EPQ_LAYOUT_MMA16 needs group / vec = 32");
     if (n * k == 0) return EPQ_OK;
-    if (!src_rows || !dst_tiled) return set_error(EPQ_EINVAL, "relayout: NULL buffer");
-    if (reinterpret_cast<uintptr_t>(dst_tiled) & 15)
+    if (!src_rows || !dst) return set_error(EPQ_EINVAL, "relayout: NULL buffer");
+    if (reinterpret_cast<uintptr_t>(dst) & 15)
         return set_error(EPQ_EALIGN, "relayout: destination must be 16-byte aligned");
-    return launch_relayout(src_rows, n, k, vec, group, dst_tiled, static_cast<cudaStream_t>(stream));
+    return launch_relayout(src_rows, layout, n, k, vec, group, dst, static_cast<cudaStream_t>(stream));
 }
 
 int epq_linear_workspace_bytes(const epq_store* stores, int32_t count, int64_t m, int64_t* bytes) {
@@ -123,6 +139,7 @@ int epq_linear_workspace_bytes(const epq_store* stores, int32_t count, int64_t m
         if (rc) return rc;
         all_lut = all_lut && lut_eligible(s[i]);
     }
+    all_lut = all_lut && lut_counters_fit(s, count);
     *bytes = all_lut ? lut_workspace_bytes(s, count) : 0;
     return EPQ_OK;
 }
@@ -146,8 +163,12 @@ int epq_linear_multi(const epq_store* stores, int32_t count, const void* x, int3
         if (ldo && ldo[i] < s[i].n) return set_error(EPQ_ESHAPE, "linear: ldo[%d] < n", i);
         all_lut = all_lut && lut_eligible(s[i]);
     }
+    all_lut = all_lut && lut_counters_fit(s, count);
     if (!x_ok(x, m, s[0].k, ldx)) return set_error(EPQ_EINVAL, "linear: x is NULL or ldx < k");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    bool all_mma = true;
+    for (int i = 0; i < count; ++i) all_mma = all_mma && mma_eligible(s[i], m, x_dtype);
+    if (all_mma) return launch_linear_mma(s, count, x, x_dtype, m, ldx, outs, ldo, out_dtype, st);
     if (all_lut) {
         if (reinterpret_cast<uintptr_t>(x) % dtype_size(x_dtype))
             return set_error(EPQ_EALIGN, "linear: x misaligned");

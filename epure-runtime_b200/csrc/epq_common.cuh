@@ -63,6 +63,12 @@ __device__ __forceinline__ int index_at(const StoreD& s, int64_t r, int64_t c) {
         const int64_t b = r >> 4, rr = r & 15;
         return s.idx[((g * s.rb + b) * s.p + l) * 16 + rr];
     }
+    if (s.layout == EPQ_LAYOUT_MMA16) {   // P = 32: lane 4*(r%8) + j%4, byte 8*((r%16)/8) + (j%32)/4
+        const int64_t j = c / s.vec;
+        const int64_t g = j >> 5, jj = j & 31;
+        const int64_t b = r >> 4, lane = 4 * (r & 7) + (jj & 3);
+        return s.idx[((b * s.ng + g) * 32 + lane) * 16 + 8 * ((r >> 3) & 1) + (jj >> 2)];
+    }
     if (s.vec == 4) return s.idx[r * s.kpos + (c >> 2)];
     const int64_t f = r * s.k + c;  // flat position in the _pack4 stream
     if (s.bits == 4) {
@@ -98,12 +104,19 @@ int launch_bwd_generic(const StoreD& s, const void* x, int64_t ldx, const void* 
                        int act_dtype, int64_t m, void* dx, int64_t lddx, int dx_dtype,
                        float* dscale, float* dcb, cudaStream_t st);
 int launch_materialize(const StoreD& s, void* w, int64_t ldw, int out_dtype, cudaStream_t st);
-int launch_relayout(const uint8_t* src, int64_t n, int64_t k, int vec, int group, uint8_t* dst,
-                    cudaStream_t st);
+int64_t layout_bytes(int layout, int64_t n, int64_t k, int vec, int group);
+int launch_relayout(const uint8_t* src, int layout, int64_t n, int64_t k, int vec, int group,
+                    uint8_t* dst, cudaStream_t st);
+
+// Small-batch tensor-core GEMV over EPQ_LAYOUT_MMA16 stores (k_gemv_mma.cu).
+bool mma_eligible(const StoreD& s, int64_t m, int x_dtype);
+int launch_linear_mma(const StoreD* s, int count, const void* x, int x_dtype, int64_t m, int64_t ldx,
+                      void* const* outs, const int64_t* ldo, int out_dtype, cudaStream_t st);
 
 // Batch-1 LUT kernel over up to 4 stores sharing x.
 constexpr int kLutMaxStores = 4;
 bool lut_eligible(const StoreD& s);
+bool lut_counters_fit(const StoreD* s, int count);
 int64_t lut_workspace_bytes(const StoreD* s, int count);
 int launch_linear_lut(const StoreD* s, int count, const void* x, int x_dtype, void* const* outs,
                       int out_dtype, void* ws, int64_t ws_bytes, cudaStream_t st);

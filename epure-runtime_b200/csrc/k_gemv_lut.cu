@@ -39,6 +39,8 @@ constexpr int kWarps = kThreads / 32;
 constexpr uint32_t kTBase = 65536;   // shared-window offset of T: low 16 bits must be 0
 constexpr uint32_t kTBytes = 65536;  // 256 entries x 256 B
 constexpr int kDynSmem = 131072;     // covers [dynamic base, kTBase + kTBytes)
+constexpr int kListOffset = 8192;    // finished-row-block list (below T, after the codebook)
+constexpr int kListCap = 8192;       // entries (32 KB)
 
 struct LutStore {
     const uint8_t* idx;
@@ -95,7 +97,8 @@ __device__ __forceinline__ void lookup16(const uint4 v, uint32_t base, float (&a
 __global__ void __launch_bounds__(kThreads, 1) gemv_lut_kernel(const __grid_constant__ LutParams P) {
     extern __shared__ __align__(16) uint8_t smem[];
     const uint32_t smem_base = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
-    if (smem_base + 4096u > kTBase || smem_base + (uint32_t)P.dyn_smem < kTBase + kTBytes) {
+    if (smem_base + kListOffset + 4u * kListCap > kTBase ||
+        smem_base + (uint32_t)P.dyn_smem < kTBase + kTBytes) {
         if (threadIdx.x == 0) atomicExch(&g_lut_layout_error, 1);
         return;
     }
@@ -105,9 +108,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_lut_kernel(const __grid_cons
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int team = lane >> 3, tl = lane & 7;
 
-    int t = blockIdx.x * P.tiles_per_cta;
+    const int t_begin = blockIdx.x * P.tiles_per_cta;
+    int t = t_begin;
     const int t_end = min(t + P.tiles_per_cta, P.total_tiles);
     int cur_store = -1, slot = 0;
+    bool wrote = false;
 
     while (t < t_end) {
         int si = 0;
@@ -139,6 +144,18 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_lut_kernel(const __grid_cons
             }
         };
         load_quad(q, cur);
+        auto load_scales = [&](int qq, float& s0, float& s1) {
+            const int tile = 4 * qq + team;
+            s0 = s1 = 0.f;
+            if (qq < n_quads && tile < seg_tiles) {
+                const int row = (rb0 + tile) * 16 + 2 * tl;
+                if (row < S.n) s0 = load_f(S.scale, S.scale_dtype, row * S.s_n + (int64_t)g * S.s_g);
+                if (row + 1 < S.n)
+                    s1 = load_f(S.scale, S.scale_dtype, (row + 1) * S.s_n + (int64_t)g * S.s_g);
+            }
+        };
+        float cs0, cs1;
+        load_scales(q, cs0, cs1);
 
         if (si != cur_store) {
             // Codebook -> fp32 shared, zero-padded to 256 entries.
@@ -180,7 +197,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_lut_kernel(const __grid_cons
         const int n16 = S.rb * 16;
         for (; q < n_quads; q += kWarps) {
             uint4 nxt[4];
+            float ns0, ns1;
             load_quad(q + kWarps, nxt);
+            load_scales(q + kWarps, ns0, ns1);
             float acc[16];
 #pragma unroll
             for (int r = 0; r < 16; ++r) acc[r] = 0.f;
@@ -209,40 +228,63 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_lut_kernel(const __grid_cons
                 a3[i] = keep + __shfl_xor_sync(0xffffffffu, send, 1);
             }
 
+            // Scaled group sums of this tile -> partials[g][row]; nothing waits here.
             const int tile = 4 * q + team;
-            const bool active = tile < seg_tiles;
-            const int rb = rb0 + tile;
-            const int row = rb * 16 + 2 * tl;
-            bool last = false;
-            if (active) {
-                const float s0 = row < S.n ? load_f(S.scale, S.scale_dtype, row * S.s_n + (int64_t)g * S.s_g) : 0.f;
-                const float s1 = row + 1 < S.n ? load_f(S.scale, S.scale_dtype, (row + 1) * S.s_n + (int64_t)g * S.s_g) : 0.f;
-                float2* pp = reinterpret_cast<float2*>(S.partials + (int64_t)g * n16 + row);
-                *pp = make_float2(a3[0] * s0, a3[1] * s1);
-                __threadfence();
+            if (tile < seg_tiles) {
+                const int row = (rb0 + tile) * 16 + 2 * tl;
+                *reinterpret_cast<float2*>(S.partials + (int64_t)g * n16 + row) =
+                    make_float2(a3[0] * cs0, a3[1] * cs1);
+                wrote = true;
             }
-            __syncwarp();
-            if (active && tl == 0) last = atomicAdd(&S.counters[rb], 1u) == (unsigned)(S.ng - 1);
-            last = __shfl_sync(0xffffffffu, last, team * 8);
-            if (active && last) {
-                __threadfence();
-                float sum0 = 0.f, sum1 = 0.f;
-                const float* pcol = S.partials + row;
-#pragma unroll 8
-                for (int gg = 0; gg < S.ng; ++gg) {
-                    const float2 v = __ldcg(reinterpret_cast<const float2*>(pcol + (int64_t)gg * n16));
-                    sum0 += v.x;
-                    sum1 += v.y;
-                }
-                if (row < S.n) store_f(S.out, P.out_dtype, row, sum0);
-                if (row + 1 < S.n) store_f(S.out, P.out_dtype, row + 1, sum1);
-                if (tl == 0) S.counters[rb] = 0u;
-            }
+            cs0 = ns0;
+            cs1 = ns1;
 #pragma unroll
             for (int i = 0; i < 4; ++i) cur[i] = nxt[i];
         }
         slot ^= 1;
         t = seg_end;
+    }
+
+    // Completion: one counter increment per tile of this CTA; the CTA whose
+    // increment completes a row block (all ng groups written) reduces it.
+    if (wrote) __threadfence();
+    int* finish = reinterpret_cast<int*>(smem + kListOffset);   // (store << 24) | rb
+    int* n_finish = reinterpret_cast<int*>(smem + kListOffset - 16);
+    if (threadIdx.x == 0) *n_finish = 0;
+    __syncthreads();
+    for (int tt = t_begin + threadIdx.x; tt < t_end; tt += kThreads) {
+        int si = 0;
+        while (si + 1 < P.count && tt >= P.st[si + 1].tile0) ++si;
+        const LutStore& S = P.st[si];
+        const int rb = (tt - S.tile0) % S.rb;
+        if (atomicAdd(&S.counters[rb], 1u) == (unsigned)(S.ng - 1)) {
+            __threadfence();
+            const int slot_i = atomicAdd(n_finish, 1);
+            if (slot_i < kListCap) {
+                finish[slot_i] = (si << 24) | rb;
+            } else {  // list full: reduce this row block here (rare, correct)
+                for (int r = 0; r < 16; ++r) {
+                    const int row = rb * 16 + r;
+                    float sum = 0.f;
+                    for (int gg = 0; gg < S.ng; ++gg) sum += __ldcg(S.partials + (int64_t)gg * S.rb * 16 + row);
+                    if (row < S.n) store_f(S.out, P.out_dtype, row, sum);
+                }
+                S.counters[rb] = 0u;
+            }
+        }
+    }
+    __syncthreads();
+    const int nf = min(*n_finish, kListCap);
+    for (int f = warp; f < nf; f += kWarps) {
+        const int si = finish[f] >> 24, rb = finish[f] & 0xFFFFFF;
+        const LutStore& S = P.st[si];
+        const int row = rb * 16 + (lane & 15);
+        const int64_t n16 = (int64_t)S.rb * 16;
+        float sum = 0.f;
+        for (int gg = lane >> 4; gg < S.ng; gg += 2) sum += __ldcg(S.partials + gg * n16 + row);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 16);
+        if (lane < 16 && row < S.n) store_f(S.out, P.out_dtype, row, sum);
+        if (lane == 0) S.counters[rb] = 0u;
     }
 }
 
@@ -272,9 +314,17 @@ bool lut_eligible(const StoreD& s) {
 
 static int64_t align256(int64_t v) { return (v + 255) & ~int64_t(255); }
 
+// Per-row-block completion counters (u32) at the start of the workspace.
+constexpr int64_t kCounterRegionBytes = 65536;
+
+bool lut_counters_fit(const StoreD* s, int count) {
+    int64_t n = 0;
+    for (int i = 0; i < count; ++i) n += s[i].rb;
+    return n * 4 <= kCounterRegionBytes;
+}
+
 int64_t lut_workspace_bytes(const StoreD* s, int count) {
-    int64_t b = 0;
-    for (int i = 0; i < count; ++i) b += align256(s[i].rb * 4);
+    int64_t b = kCounterRegionBytes;
     for (int i = 0; i < count; ++i) b += align256(s[i].ng * s[i].rb * 16 * 4);
     return b;
 }
@@ -302,7 +352,16 @@ int launch_linear_lut(const StoreD* s, int count, const void* x, int x_dtype, vo
     P.x_dtype = x_dtype;
     P.out_dtype = out_dtype;
     P.dyn_smem = kDynSmem;
-    uint8_t* wp = static_cast<uint8_t*>(ws);
+    // Counters live in a fixed region at the start of every workspace, so no
+    // call ever uses bytes another call wrote partial sums into as counters.
+    int64_t n_counters = 0;
+    for (int i = 0; i < count; ++i) n_counters += s[i].rb;
+    if (n_counters * 4 > kCounterRegionBytes)
+        return set_error(EPQ_EUNSUPPORTED, "linear: %lld row blocks exceed the %lld counters of "
+                         "the batch-1 kernel", (long long)n_counters,
+                         (long long)(kCounterRegionBytes / 4));
+    unsigned* counters = static_cast<unsigned*>(ws);
+    uint8_t* wp = static_cast<uint8_t*>(ws) + kCounterRegionBytes;
     int64_t total = 0;
     for (int i = 0; i < count; ++i) {
         LutStore& L = P.st[i];
@@ -320,8 +379,8 @@ int launch_linear_lut(const StoreD* s, int count, const void* x, int x_dtype, vo
         L.ng = (int)s[i].ng;
         L.kpos = (int)s[i].kpos;
         L.tile0 = (int)total;
-        L.counters = reinterpret_cast<unsigned*>(wp);
-        wp += align256(s[i].rb * 4);
+        L.counters = counters;
+        counters += s[i].rb;
         total += s[i].ng * s[i].rb;
     }
     for (int i = 0; i < count; ++i) {

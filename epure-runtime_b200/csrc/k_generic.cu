@@ -200,9 +200,10 @@ __global__ void materialize_kernel(StoreD s, void* __restrict__ w, int64_t ldw, 
     }
 }
 
-// One thread per 16-byte tiled chunk (16 rows of one index position).
-__global__ void relayout_kernel(const uint8_t* __restrict__ src, int64_t n, int64_t kpos,
-                                int64_t p, int64_t rb, int64_t chunks, uint8_t* __restrict__ dst) {
+// EPQ_LAYOUT_TILED: one thread per 16-byte chunk (16 rows of one index position).
+__global__ void relayout_tiled_kernel(const uint8_t* __restrict__ src, int64_t n, int64_t kpos,
+                                      int64_t p, int64_t rb, int64_t chunks,
+                                      uint8_t* __restrict__ dst) {
     for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < chunks;
          t += (int64_t)gridDim.x * blockDim.x) {
         const int64_t l = t % p, gb = t / p;
@@ -213,6 +214,27 @@ __global__ void relayout_kernel(const uint8_t* __restrict__ src, int64_t n, int6
             const int64_t r = b * 16 + rr;
             const uint32_t v = (r < n && j < kpos) ? src[r * kpos + j] : 0u;
             words[rr >> 2] |= v << (8 * (rr & 3));
+        }
+        reinterpret_cast<uint4*>(dst)[t] = make_uint4(words[0], words[1], words[2], words[3]);
+    }
+}
+
+// EPQ_LAYOUT_MMA16: one thread per 16-byte chunk (lane t of a tile: rows
+// rb*16 + t/4 and + 8, positions t%4 + 4s of its group, s = 0..7).
+__global__ void relayout_mma16_kernel(const uint8_t* __restrict__ src, int64_t n, int64_t kpos,
+                                      int64_t ng, int64_t chunks, uint8_t* __restrict__ dst) {
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < chunks;
+         t += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t lane = t & 31, bg = t >> 5;
+        const int64_t g = bg % ng, b = bg / ng;
+        uint32_t words[4] = {0, 0, 0, 0};
+        for (int h = 0; h < 2; ++h) {
+            const int64_t r = b * 16 + 8 * h + (lane >> 2);
+            for (int s = 0; s < 8; ++s) {
+                const int64_t j = g * 32 + 4 * s + (lane & 3);
+                const uint32_t v = (r < n && j < kpos) ? src[r * kpos + j] : 0u;
+                words[2 * h + (s >> 2)] |= v << (8 * (s & 3));
+            }
         }
         reinterpret_cast<uint4*>(dst)[t] = make_uint4(words[0], words[1], words[2], words[3]);
     }
@@ -264,14 +286,26 @@ int launch_materialize(const StoreD& s, void* w, int64_t ldw, int out_dtype, cud
     return check_launch("materialize_kernel");
 }
 
-int launch_relayout(const uint8_t* src, int64_t n, int64_t k, int vec, int group, uint8_t* dst,
-                    cudaStream_t st) {
-    const int64_t p = group / vec, kpos = k / vec;
-    const int64_t rb = cdiv(n, 16), ng = cdiv(k, group);
-    const int64_t chunks = ng * rb * p;
+int64_t layout_bytes(int layout, int64_t n, int64_t k, int vec, int group) {
+    if (layout == EPQ_LAYOUT_TILED) return cdiv(k, group) * cdiv(n, 16) * (group / vec) * 16;
+    if (layout == EPQ_LAYOUT_MMA16) return cdiv(k, group) * cdiv(n, 16) * 512;
+    return -1;
+}
+
+int launch_relayout(const uint8_t* src, int layout, int64_t n, int64_t k, int vec, int group,
+                    uint8_t* dst, cudaStream_t st) {
+    const int64_t kpos = k / vec, ng = cdiv(k, group);
+    if (layout == EPQ_LAYOUT_TILED) {
+        const int64_t p = group / vec, rb = cdiv(n, 16);
+        const int64_t chunks = ng * rb * p;
+        if (chunks == 0) return EPQ_OK;
+        relayout_tiled_kernel<<<grid_1d(chunks, 256), 256, 0, st>>>(src, n, kpos, p, rb, chunks, dst);
+        return check_launch("relayout_tiled_kernel");
+    }
+    const int64_t rb = cdiv(n, 16), chunks = ng * rb * 32;
     if (chunks == 0) return EPQ_OK;
-    relayout_kernel<<<grid_1d(chunks, 256), 256, 0, st>>>(src, n, kpos, p, rb, chunks, dst);
-    return check_launch("relayout_kernel");
+    relayout_mma16_kernel<<<grid_1d(chunks, 256), 256, 0, st>>>(src, n, kpos, ng, chunks, dst);
+    return check_launch("relayout_mma16_kernel");
 }
 
 }  // namespace epq

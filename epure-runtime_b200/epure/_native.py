@@ -16,7 +16,8 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libepq.so")
 
 EPQ_F32, EPQ_F16, EPQ_BF16 = 0, 1, 2
-LAYOUT_ROWS, LAYOUT_TILED = 0, 1
+LAYOUT_ROWS, LAYOUT_TILED, LAYOUT_MMA16 = 0, 1, 2
+LAYOUT_CODES = {"rows": LAYOUT_ROWS, "tiled": LAYOUT_TILED, "mma16": LAYOUT_MMA16}
 
 _DT = {torch.float32: EPQ_F32, torch.float16: EPQ_F16, torch.bfloat16: EPQ_BF16}
 
@@ -42,8 +43,8 @@ class EpqStore(ctypes.Structure):
 
 
 EXPORTS = (
-    "epq_abi_version", "epq_last_error", "epq_device_error", "epq_tiled_bytes",
-    "epq_relayout_tiled", "epq_linear_workspace_bytes", "epq_linear_multi", "epq_linear",
+    "epq_abi_version", "epq_last_error", "epq_device_error", "epq_layout_bytes",
+    "epq_relayout", "epq_linear_workspace_bytes", "epq_linear_multi", "epq_linear",
     "epq_linear_bwd", "epq_materialize",
 )
 
@@ -68,9 +69,9 @@ def load_library(path=None):
         lib.epq_abi_version.restype = ctypes.c_int
         lib.epq_last_error.restype = ctypes.c_char_p
         lib.epq_device_error.argtypes = [ctypes.POINTER(ctypes.c_int)]
-        lib.epq_tiled_bytes.restype = I64
-        lib.epq_tiled_bytes.argtypes = [I64, I64, I32, I32]
-        lib.epq_relayout_tiled.argtypes = [P, I64, I64, I32, I32, P, P]
+        lib.epq_layout_bytes.restype = I64
+        lib.epq_layout_bytes.argtypes = [I32, I64, I64, I32, I32]
+        lib.epq_relayout.argtypes = [P, I32, I64, I64, I32, I32, P, P]
         lib.epq_linear_workspace_bytes.argtypes = [SP, I32, I64, ctypes.POINTER(I64)]
         lib.epq_linear_multi.argtypes = [SP, I32, P, I32, I64, I64, P, P, I32, P, I64, P]
         lib.epq_linear.argtypes = [SP, P, I32, I64, I64, P, I64, I32, P, I64, P]
@@ -116,7 +117,7 @@ def describe_store(store):
         raise RuntimeError("epure: scale must be 2-D [rows, groups]")
     d = EpqStore()
     d.idx = packed.data_ptr()
-    d.layout = LAYOUT_TILED if store.layout == "tiled" else LAYOUT_ROWS
+    d.layout = LAYOUT_CODES[store.layout]
     d.bits = 4 if (store.vec == 1 and store.levels <= 16) else 8
     d.vec = store.vec
     d.levels = store.levels
@@ -238,18 +239,21 @@ def materialize(store, dtype):
     return w
 
 
-def tiled_bytes(n, k, vec, group):
-    return int(load_library().epq_tiled_bytes(n, k, vec, group))
+def layout_bytes(layout, n, k, vec, group):
+    return int(load_library().epq_layout_bytes(LAYOUT_CODES[layout], n, k, vec, group))
 
 
-def relayout_tiled(idx_rows, n, k, vec, group):
-    """Row-layout u8 indices on the GPU -> a new EPQ_LAYOUT_TILED buffer."""
+def relayout(idx_rows, layout, n, k, vec, group):
+    """Row-layout u8 indices on the GPU -> a new buffer in ``layout`` ("tiled" / "mma16")."""
     lib = load_library()
     src = idx_rows.contiguous()
-    nbytes = tiled_bytes(n, k, vec, group)
+    nbytes = layout_bytes(layout, n, k, vec, group)
+    if nbytes < 0:
+        raise RuntimeError(f"epure: layout {layout} does not support n={n} k={k} vec={vec} "
+                           f"group={group}")
     dst = torch.empty(nbytes, dtype=torch.uint8, device=src.device)
-    _check(lib.epq_relayout_tiled(src.data_ptr(), n, k, vec, group, dst.data_ptr(),
-                                  _stream_ptr(src.device)), "epq_relayout_tiled")
+    _check(lib.epq_relayout(src.data_ptr(), LAYOUT_CODES[layout], n, k, vec, group,
+                            dst.data_ptr(), _stream_ptr(src.device)), "epq_relayout")
     return dst
 
 

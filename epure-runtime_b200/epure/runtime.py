@@ -79,7 +79,10 @@ class PackedWeight(nn.Module):
     row-major [rows, in_features / 4] u8 array and ``cb`` is [levels, 4].
     """
 
-    TILE_GROUP = 128   # the group size the tiled GPU layout serves
+    TILE_GROUP = 128   # the group size the tiled GPU layouts serve
+    # GPU index layout of vector stores: "mma16" (the tensor-core GEMV, any batch
+    # up to 16) or "tiled" (the batch-1 LUT kernel).
+    GPU_LAYOUT = os.environ.get("EPURE_GPU_LAYOUT", "mma16")
 
     def __init__(self, shape, packed, scale, cb, group, levels, vec=1):
         super().__init__()
@@ -108,26 +111,42 @@ class PackedWeight(nn.Module):
     def _sync_layout(self):
         """Keep the index layout matched to the device (tiled on a GPU, rows on CPU)."""
         from . import _native
-        want = "tiled" if self._tiling_wanted() else "rows"
+        want = self.GPU_LAYOUT if self._tiling_wanted() else "rows"
         if want == self.layout:
             return
         n, k = self.out_features, self.in_features
-        if want == "tiled":
+        if want != "rows":
+            if self.layout != "rows":
+                self._buffers["packed"] = self._rows_from_tiled().reshape(-1).contiguous()
             rows = self.packed.reshape(n, k // self.vec)
-            self._buffers["packed"] = _native.relayout_tiled(rows, n, k, self.vec, self.group)
+            self._buffers["packed"] = _native.relayout(rows, want, n, k, self.vec, self.group)
             sc = self.scale
+            gm = self._group_major(sc.data if isinstance(sc, nn.Parameter) else sc)
             if isinstance(sc, nn.Parameter):
-                sc.data = sc.data.t().contiguous().t()
+                sc.data = gm
             else:
-                self._buffers["scale"] = sc.t().contiguous().t()
+                self._buffers["scale"] = gm
         else:
             self._buffers["packed"] = self._rows_from_tiled().reshape(-1).contiguous()
         self.layout = want
         self.__dict__.pop("_epq_desc", None)
         self.__dict__.pop("_hot_cache", None)
 
+    @staticmethod
+    def _group_major(sc):
+        """[rows, groups] scales stored group-major, rows padded to 16 (a strided view).
+
+        The kernels read the 16 scales of a 16-row block at one group as one
+        contiguous run; padded rows hold 0.
+        """
+        n, ng = sc.shape
+        npad = -(-n // 16) * 16
+        store = torch.zeros((ng, npad), dtype=sc.dtype, device=sc.device)
+        store[:, :n] = sc.t()
+        return store[:, :n].t()
+
     def _apply(self, fn, recurse=True):
-        if self.layout == "tiled":
+        if self.layout != "rows":
             # Device moves go through the row layout so the bytes stay meaningful.
             rows = self._rows_from_tiled().reshape(-1).contiguous()
             self._buffers["packed"] = rows
@@ -138,24 +157,31 @@ class PackedWeight(nn.Module):
         return out
 
     def _tiled_view(self):
-        """The tiled bytes as a strided [rows, positions] view (no copy)."""
+        """The tiled bytes as a strided [row block, row in block, ...] view (no copy).
+
+        "tiled": byte ((g*RB + rb)*P + l)*16 + rr  ->  [rb, rr, g, l]
+        "mma16": byte ((rb*NG + g)*32 + 4*rr + q)*16 + 8*h + s  ->  [rb, h, rr, g, s, q]
+        (row = 16*rb + rr or 16*rb + 8*h + rr; position j = g*P + l or g*32 + 4*s + q).
+        """
         n, k, vec, g = self.out_features, self.in_features, self.vec, self.group
-        p, rb, ng = g // vec, -(-n // 16), -(-k // g)
-        t = self.packed.view(ng, rb, p, 16).permute(1, 3, 0, 2)   # [rb, 16, ng, p]
-        return t
+        p, ng = g // vec, -(-k // g)
+        if self.layout == "tiled":
+            return self.packed.view(ng, -(-n // 16), p, 16).permute(1, 3, 0, 2), 16
+        t = self.packed.view(-(-n // 16), ng, 8, 4, 2, 8).permute(0, 4, 2, 1, 5, 3)
+        return t.reshape(-(-n // 16), 16, ng, 8, 4), 16
 
     def _rows_from_tiled(self, rows=None):
         n, kpos = self.out_features, self.in_features // self.vec
-        t = self._tiled_view()
+        t, blk = self._tiled_view()
         if rows is None:
-            full = t.reshape(t.shape[0] * 16, -1)
+            full = t.reshape(t.shape[0] * blk, -1)
             return full[:n, :kpos].contiguous()
-        sel = t[rows // 16, rows % 16]                             # [len, ng, p]
+        sel = t[rows // blk, rows % blk]
         return sel.reshape(rows.numel(), -1)[:, :kpos]
 
     def index_rows(self, rows=None):
         """Per-position indices as [rows, in_features / vec] (u8, row layout)."""
-        if self.layout == "tiled":
+        if self.layout != "rows":
             return self._rows_from_tiled(rows)
         kpos = self.in_features // self.vec
         if self.vec == 4 or self.levels > 16:
@@ -167,7 +193,7 @@ class PackedWeight(nn.Module):
 
     def packed_2d(self):
         """[rows, bytes-per-row] view of the row layout (a copy for tiled stores)."""
-        if self.layout == "tiled":
+        if self.layout != "rows":
             return self._rows_from_tiled()
         cols = (self.in_features // 4 if self.vec == 4 else
                 self.in_features if self.levels > 16 else (self.in_features + 1) // 2)

@@ -34,7 +34,7 @@
  *       backward kernel
  *   epq_materialize
  *       epure/runtime.py:78-89        PackedWeight.materialize(dtype)
- *   epq_relayout_tiled / epq_tiled_bytes
+ *   epq_relayout / epq_layout_bytes
  *       the re-layout step of epure/runtime.py:243-249 (apply_to builds the
  *       store from the container's index stream)
  */
@@ -79,8 +79,18 @@ enum epq_dtype { EPQ_F32 = 0, EPQ_F16 = 1, EPQ_BF16 = 2 };
  *                     g = j / P, l = j % P, rb = r / 16, rr = r % 16.  A
  *                     16-row x P-position tile is contiguous, tiles run
  *                     row-block fastest within a group.  Padding (rows >= n,
- *                     positions >= k / vec) holds index 0.            */
-enum epq_layout { EPQ_LAYOUT_ROWS = 0, EPQ_LAYOUT_TILED = 1 };
+ *                     positions >= k / vec) holds index 0.
+ *   EPQ_LAYOUT_MMA16  the small-batch tensor-core layout for bits = 8 with
+ *                     group / vec = 32 positions per group.  With RB =
+ *                     ceil(n / 16) and NG = ceil(k / group), the index of
+ *                     row r, position j lives at byte
+ *                       ((rb * NG + g) * 32 + t) * 16 + 8 * h + s,
+ *                     g = j / 32, rb = r / 16, h = (r % 16) / 8,
+ *                     t = 4 * (r % 8) + j % 4, s = (j % 32) / 4: a 512-byte
+ *                     tile per (16-row block, group), group fastest, in which
+ *                     each of 32 lanes reads one 16-byte word.  Padding holds
+ *                     index 0.                                          */
+enum epq_layout { EPQ_LAYOUT_ROWS = 0, EPQ_LAYOUT_TILED = 1, EPQ_LAYOUT_MMA16 = 2 };
 
 /* A packed weight, described by plain pointers (all device memory). */
 typedef struct epq_store {
@@ -107,32 +117,42 @@ int epq_abi_version(void);
 /* Human-readable description of the last failure on the calling host thread. */
 const char* epq_last_error(void);
 
-/* Reads (synchronously, on the current device) the flag a kernel sets when
- * one of its in-kernel checks fails and it returns without writing output.
- * *flag = 0 means no kernel has reported a failure. */
+/* Reads (synchronously, on the current device) the flags kernels set when an
+ * in-kernel check fails: bit 0 -- the batch-1 LUT kernel found its shared
+ * memory placement violated and wrote nothing; bit 1 -- a bounded
+ * device-side wait gave up (that call's output is invalid).  *flag = 0
+ * means no kernel has reported a failure. */
 int epq_device_error(int* flag);
 
-/* Bytes of an EPQ_LAYOUT_TILED index buffer for the given shape. */
-int64_t epq_tiled_bytes(int64_t n, int64_t k, int32_t vec, int32_t group);
+/* Bytes of an index buffer in `layout` (EPQ_LAYOUT_TILED or EPQ_LAYOUT_MMA16)
+ * for the given shape, or -1 for an unsupported combination. */
+int64_t epq_layout_bytes(int32_t layout, int64_t n, int64_t k, int32_t vec, int32_t group);
 
-/* Re-lay an EPQ_LAYOUT_ROWS index buffer (bits = 8) into EPQ_LAYOUT_TILED.
- * `dst` must hold epq_tiled_bytes(n, k, vec, group) bytes; padding is zeroed. */
-int epq_relayout_tiled(const uint8_t* src_rows, int64_t n, int64_t k, int32_t vec,
-                       int32_t group, uint8_t* dst_tiled, void* stream);
+/* Re-lay an EPQ_LAYOUT_ROWS index buffer (bits = 8, [n, k / vec] row-major)
+ * into `layout`.  `dst` must hold epq_layout_bytes(...) bytes and be 16-byte
+ * aligned; padding is written as index 0. */
+int epq_relayout(const uint8_t* src_rows, int32_t layout, int64_t n, int64_t k, int32_t vec,
+                 int32_t group, uint8_t* dst, void* stream);
 
-/* Scratch needed by epq_linear_multi for these stores at `m` activation rows.
- * The workspace must be zero-filled once after it is allocated; every call
- * leaves its counter region zero again when it completes, so a workspace can
- * be reused by later calls that are ordered after it (same stream, or a
- * dependency).  Calls that overlap on the GPU need separate workspaces. */
+/* Scratch needed by epq_linear_multi for these stores at `m` activation rows
+ * (0 when the call needs none).  The first 64 KiB of a workspace hold
+ * completion counters and the rest partial sums.  Zero-fill a workspace once
+ * after allocating it; every call leaves the counters zero again when it
+ * completes, so one workspace serves any later call that is ordered after it
+ * (same stream, or a dependency), whatever its shapes.  Calls that overlap on
+ * the GPU need separate workspaces. */
 int epq_linear_workspace_bytes(const epq_store* stores, int32_t count, int64_t m,
                                int64_t* bytes);
 
 /* out[i][m, n_i] = x[m, k] @ W_i[n_i, k]^T for `count` (1..4) stores that share
  * the activation x (same k).  x: [m, k] with row stride ldx (elements),
  * x_dtype f32/f16/bf16; outs[i]: [m, n_i] with row stride ldo[i], out_dtype
- * f32/f16/bf16.  fp32 accumulation.  Batch-1 calls on EPQ_LAYOUT_TILED vector
- * stores use the bandwidth-bound LUT kernel and need the workspace above. */
+ * f32/f16/bf16.  fp32 accumulation.  Calls with 1 <= m <= 16 bf16/f16
+ * activations on EPQ_LAYOUT_MMA16 vector stores run the tensor-core GEMV (no
+ * workspace; it may overlap the previous kernel on the stream through
+ * programmatic dependent launch).  Batch-1 calls on EPQ_LAYOUT_TILED vector
+ * stores run the LUT kernel and need the workspace above.  Every other
+ * combination runs the general kernel. */
 int epq_linear_multi(const epq_store* stores, int32_t count, const void* x,
                      int32_t x_dtype, int64_t m, int64_t ldx, void* const* outs,
                      const int64_t* ldo, int32_t out_dtype, void* workspace,

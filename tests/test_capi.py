@@ -37,11 +37,15 @@ def test_abi_version(lib):
     assert lib.epq_abi_version() == 1
 
 
-def test_tiled_bytes(lib):
-    assert lib.epq_tiled_bytes(6144, 2048, 4, 128) == 16 * 384 * 32 * 16
-    assert lib.epq_tiled_bytes(37, 200, 4, 128) == 2 * 3 * 32 * 16
-    assert lib.epq_tiled_bytes(-1, 8, 4, 128) == -1
-    assert lib.epq_tiled_bytes(8, 8, 3, 128) == -1
+def test_layout_bytes(lib):
+    assert lib.epq_layout_bytes(1, 6144, 2048, 4, 128) == 16 * 384 * 32 * 16
+    assert lib.epq_layout_bytes(1, 37, 200, 4, 128) == 2 * 3 * 32 * 16
+    assert lib.epq_layout_bytes(2, 6144, 2048, 4, 128) == 16 * 384 * 512
+    assert lib.epq_layout_bytes(2, 37, 200, 4, 128) == 2 * 3 * 512
+    assert lib.epq_layout_bytes(2, 64, 256, 4, 64) == -1      # mma16 needs 32 positions per group
+    assert lib.epq_layout_bytes(1, -1, 8, 4, 128) == -1
+    assert lib.epq_layout_bytes(1, 8, 8, 3, 128) == -1
+    assert lib.epq_layout_bytes(0, 8, 8, 4, 128) == -1
 
 
 def _store(**kw):
@@ -91,7 +95,7 @@ def test_workspace_query(lib):
     arr = (EpqStore * 1)(_store(n=64, k=256))
     b = ctypes.c_int64(-1)
     assert lib.epq_linear_workspace_bytes(arr, 1, 1, ctypes.byref(b)) == 0
-    # 4 row blocks of counters (256-aligned) + 2 groups x 64 rows of fp32 partials
-    assert b.value == 256 + 512
+    # the fixed 64 KiB counter region + 2 groups x 64 rows of fp32 partials
+    assert b.value == 65536 + 512
     assert lib.epq_linear_workspace_bytes(arr, 1, 2, ctypes.byref(b)) == 0
     assert b.value == 0          # batch > 1 runs kernels without scratch

@@ -3,9 +3,11 @@
 Tolerances (per layer, max |got - want| / max |want|):
 * vs the reference's bf16 path (materialize(bf16) + F.linear): <= 1e-2, the
   bound the benchmark's north star states.
-* vs the exact float64 product of the stored values: <= 4e-3 for bf16 outputs
-  (the kernels expand cb * scale in fp32 and accumulate in fp32, so the only
-  rounding is bf16 activations/outputs), <= 1e-5 for fp32 outputs.
+* vs the exact float64 product of the stored values: <= 8e-3 for bf16 outputs
+  (the tensor-core kernel rounds the codebook to bf16 as the reference does;
+  scales multiply the fp32 accumulator; accumulation is fp32), <= 1e-5 for
+  fp32 activations and outputs (the general and LUT kernels keep everything
+  in fp32).
 * materialize: bit-exact with the reference (both fp32 and bf16).
 * gradients (fp32 activations): <= 1e-4 vs the reference's autograd.
 Batch-1 vector stores (EPQ_LAYOUT_TILED) run the LUT kernel; everything else
@@ -32,6 +34,18 @@ def _gpu():
     assert _native.device_error() == 0
 
 
+LAYOUTS = ["mma16", "tiled"]
+
+
+@pytest.fixture(params=LAYOUTS)
+def gpu_layout(request):
+    from epure import PackedWeight
+    old = PackedWeight.GPU_LAYOUT
+    PackedWeight.GPU_LAYOUT = request.param
+    yield request.param
+    PackedWeight.GPU_LAYOUT = old
+
+
 def _store(z, device=DEV):
     from epure import PackedWeight
     return PackedWeight((z["n"], z["k"]), z["idx_rows"].ravel().copy(), z["scale"].copy(),
@@ -43,13 +57,13 @@ def _args(z):
 
 
 @pytest.mark.parametrize("case", golden_cases())
-def test_forward_vs_reference(case, oracle_mod):
+def test_forward_vs_reference(case, oracle_mod, gpu_layout):
     from epure import PackedLinear
     O = oracle_mod
     z = load_golden(case)
     st = _store(z)
     if z["vec"] == 4:
-        assert st.layout == "tiled"
+        assert st.layout == gpu_layout
     lin = PackedLinear(st)
     x = torch.from_numpy(z["x"]).to(DEV)
     with torch.no_grad():
@@ -57,12 +71,12 @@ def test_forward_vs_reference(case, oracle_mod):
         out32 = lin(x).cpu().numpy()
     assert O.rel_err(out, z["outbf"]) <= 1e-2
     exact = O.linear_exact(z["x"], *_args(z))
-    assert O.rel_err(out, exact) <= 4e-3
+    assert O.rel_err(out, exact) <= 8e-3
     assert O.rel_err(out32, exact) <= 1e-5
 
 
 @pytest.mark.parametrize("case", golden_cases())
-def test_batch1_rows(case, oracle_mod):
+def test_batch1_rows(case, oracle_mod, gpu_layout):
     """Each activation row alone (batch 1: the LUT kernel for vector stores)."""
     from epure import PackedLinear
     O = oracle_mod
@@ -113,16 +127,16 @@ def test_backward_vs_reference(case):
     verify_frozen(model, snap)
 
 
-def test_relayout_roundtrip():
+def test_relayout_roundtrip(gpu_layout):
     from epure import synthetic
     st = synthetic.make_store(1000, 4096, device=DEV, seed=5)
-    assert st.layout == "tiled"
+    assert st.layout == gpu_layout
     rows = st.index_rows()
     cpu = st.to("cpu")
     assert cpu.layout == "rows"
     assert torch.equal(cpu.index_rows(), rows.cpu())
     back = cpu.to(DEV)
-    assert back.layout == "tiled"
+    assert back.layout == gpu_layout
     assert torch.equal(back.index_rows(), rows)
 
 
@@ -139,8 +153,8 @@ def _oracle_inputs(st):
     return idx, st.scale.float().cpu().numpy(), st.cb.float().cpu().numpy()
 
 
-@pytest.mark.parametrize("m", [1, 8])
-def test_config0_vs_oracle(m, oracle_mod):
+@pytest.mark.parametrize("m", [1, 8, 16])
+def test_config0_vs_oracle(m, oracle_mod, gpu_layout):
     """K=2048, N=6144 (the single-linear benchmark configuration) at batch 1 and 8."""
     from epure.kernels import cuda
     O = oracle_mod
@@ -152,28 +166,47 @@ def test_config0_vs_oracle(m, oracle_mod):
     ref = O.linear_reference(xs, idx, sc, cb, 6144, 2048, 4, 128, 256, dtype="bfloat16")
     exact = O.linear_exact(xs, idx, sc, cb, 6144, 2048, 4, 128, 256)
     assert O.rel_err(out, ref) <= 1e-2
-    assert O.rel_err(out, exact) <= 4e-3
+    assert O.rel_err(out, exact) <= 8e-3
     c = O.c_dequant_matmul(xs, idx, sc, cb, 6144, 2048, 4, 128, 256)
-    assert O.rel_err(out, c) <= 4e-3
+    assert O.rel_err(out, c) <= 8e-3
 
 
 @pytest.mark.parametrize("n,k", [(1, 128), (16, 4096), (17, 132), (4096, 14336), (28672, 4096),
                                  (1024, 8192), (37, 200)])
 def test_lut_shapes_vs_oracle(n, k, oracle_mod):
+    """The batch-1 LUT kernel (fp32 activations) at the 8B/70B shapes and ragged ones."""
+    from epure import PackedWeight
+    old = PackedWeight.GPU_LAYOUT
+    PackedWeight.GPU_LAYOUT = "tiled"
+    try:
+        _shape_check(n, k, oracle_mod, torch.float32, 1e-5, 1)
+    finally:
+        PackedWeight.GPU_LAYOUT = old
+
+
+@pytest.mark.parametrize("m", [1, 3, 8, 16])
+@pytest.mark.parametrize("n,k", [(1, 128), (9, 4096), (17, 132), (4096, 14336), (28672, 4096),
+                                 (1024, 8192), (37, 200)])
+def test_mma_shapes_vs_oracle(n, k, m, oracle_mod):
+    """The tensor-core GEMV (bf16 activations) at batch 1..16, 8B/70B and ragged shapes."""
+    _shape_check(n, k, oracle_mod, torch.bfloat16, 8e-3, m)
+
+
+def _shape_check(n, k, oracle_mod, dtype, tol, m):
     from epure import synthetic
     from epure.kernels import cuda
     O = oracle_mod
     st = synthetic.make_store(n, k, device=DEV, seed=n + k)
     g = torch.Generator(device=DEV).manual_seed(7)
-    x = torch.randn(1, k, generator=g, device=DEV)
+    x = torch.randn(m, k, generator=g, device=DEV).to(dtype)
     with torch.no_grad():
-        out32 = cuda.linear(x, st).cpu().numpy()
+        out = cuda.linear(x, st).float().cpu().numpy()
     idx, sc, cb = _oracle_inputs(st)
-    exact = O.linear_exact(x.cpu().numpy(), idx, sc, cb, n, k, 4, 128, 256)
-    assert O.rel_err(out32, exact) <= 1e-5
+    exact = O.linear_exact(x.float().cpu().numpy(), idx, sc, cb, n, k, 4, 128, 256)
+    assert O.rel_err(out, exact) <= tol
 
 
-def test_fused_multi_matches_separate():
+def test_fused_multi_matches_separate(gpu_layout):
     """q/k/v-style fused launch equals three single-store launches, bit for bit."""
     from epure import synthetic
     from epure.kernels import cuda
@@ -187,7 +220,7 @@ def test_fused_multi_matches_separate():
         assert torch.equal(a, b)
 
 
-def test_lut_deterministic_and_reusable():
+def test_deterministic_and_reusable(gpu_layout):
     """The workspace counters reset after each call; results are bitwise repeatable."""
     from epure import synthetic
     from epure.kernels import cuda
@@ -197,6 +230,24 @@ def test_lut_deterministic_and_reusable():
         outs = [cuda.linear(x, st) for _ in range(5)]
     for o in outs[1:]:
         assert torch.equal(o, outs[0])
+
+
+def test_lut_workspace_reuse_across_shapes(oracle_mod):
+    """One workspace serves calls of growing and shrinking shapes in any order."""
+    from epure import PackedWeight, synthetic
+    from epure.kernels import cuda
+    O = oracle_mod
+    PackedWeight.GPU_LAYOUT, old = "tiled", PackedWeight.GPU_LAYOUT
+    shapes = [(96, 1024), (6144, 2048), (16, 128), (3000, 4096), (6144, 2048)]
+    for i, (n, k) in enumerate(shapes):
+        st = synthetic.make_store(n, k, device=DEV, seed=50 + i)
+        x = torch.randn(1, k, device=DEV)
+        with torch.no_grad():
+            out = cuda.linear(x, st).cpu().numpy()
+        idx, sc, cb = _oracle_inputs(st)
+        exact = O.linear_exact(x.cpu().numpy(), idx, sc, cb, n, k, 4, 128, 256)
+        assert O.rel_err(out, exact) <= 1e-5, (n, k)
+    PackedWeight.GPU_LAYOUT = old
 
 
 def test_full_size_linearity():
@@ -212,15 +263,16 @@ def test_full_size_linearity():
     assert float((lhs - rhs).abs().max() / rhs.abs().max()) < 1e-5
 
 
-def test_batch_rows_agree_with_batch1():
-    """Row i of a batch-8 call equals a batch-1 call on row i (fp32, to rounding)."""
+def test_batch_rows_agree_with_batch1(gpu_layout):
+    """Row i of a batch-8 call equals a batch-1 call on row i (to fp32 rounding)."""
     from epure.kernels import cuda
     st, x = _config0(8, seed=4)
-    x = x.float()
     with torch.no_grad():
-        full = cuda.linear(x, st)
-        rows = torch.cat([cuda.linear(x[i:i + 1], st) for i in range(8)])
-    assert float((full - rows).abs().max() / rows.abs().max()) < 1e-5
+        full = cuda.linear(x, st).float()
+        rows = torch.cat([cuda.linear(x[i:i + 1], st) for i in range(8)]).float()
+    # bf16 outputs: rows may differ by one bf16 rounding step when the batch-1
+    # and batch-8 calls run different kernels
+    assert float((full - rows).abs().max() / rows.abs().max()) < 1e-2
 
 
 def test_bad_inputs_raise():

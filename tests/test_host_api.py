@@ -106,21 +106,31 @@ def test_packed_embedding_rows():
     assert torch.equal(got, want)
 
 
-def test_tiled_view_inverts_tiling():
-    """_rows_from_tiled undoes the EPQ_LAYOUT_TILED byte order (numpy model of the kernel)."""
+@pytest.mark.parametrize("layout", ["tiled", "mma16"])
+def test_tiled_view_inverts_tiling(layout):
+    """index_rows undoes the kernel-native byte orders (numpy model of the relayout kernels)."""
     from epure import PackedWeight
     rng = np.random.default_rng(1)
     n, k, vec, group = 37, 200, 4, 128
     rows = rng.integers(0, 256, (n, k // vec), dtype=np.uint8)
-    p, rb, ng = group // vec, -(-n // 16), -(-k // group)
-    tiled = np.zeros((ng, rb, p, 16), np.uint8)
-    for r in range(n):
-        for j in range(k // vec):
-            tiled[j // p, r // 16, j % p, r % 16] = rows[r, j]
+    p, ng = group // vec, -(-k // group)
+    if layout == "tiled":
+        rb = -(-n // 16)
+        buf = np.zeros((ng, rb, p, 16), np.uint8)
+        for r in range(n):
+            for j in range(k // vec):
+                buf[j // p, r // 16, j % p, r % 16] = rows[r, j]
+    else:
+        rb = -(-n // 16)
+        buf = np.zeros((rb, ng, 32, 16), np.uint8)
+        for r in range(n):
+            for j in range(k // vec):
+                jj = j % 32
+                buf[r // 16, j // 32, 4 * (r % 8) + jj % 4, 8 * ((r % 16) // 8) + jj // 4] = rows[r, j]
     st = PackedWeight((n, k), rows.ravel(), np.zeros((n, ng), np.float16),
                       np.zeros((256, 4), np.float16), group, 256, vec=4)
-    st._buffers["packed"] = torch.from_numpy(tiled.ravel())
-    st.layout = "tiled"
+    st._buffers["packed"] = torch.from_numpy(buf.ravel())
+    st.layout = layout
     assert np.array_equal(st.index_rows().numpy(), rows)
     sel = torch.tensor([0, 17, 36])
     assert np.array_equal(st.index_rows(sel).numpy(), rows[[0, 17, 36]])
