@@ -38,10 +38,12 @@ METRIC = "decode tok/s bs1 @8B; dequant-GEMV HBM GB/s as % of B200 peak"
 UNIT = "tok/s"
 WORKLOAD = "llama3-8b packed linears, batch-1 decode token (224 linears, 128 launches)"
 
-# dram__bytes_read.sum + dram__bytes_write.sum per gemv_lut_kernel launch, from
-# the ncu capture summarised in profiles/gemv_lut_kernel_llama3-8b_decode.md
-# (None until a capture exists).
-NCU_TRAFFIC_PER_STEP = None
+# DRAM traffic / algorithmic bytes of gemv_mma_kernel, from one ncu capture of
+# a Llama-3-8B gate+up launch (profiles/gemv_mma_kernel_llama3-8b_gateup_b1.md:
+# dram__bytes_read.sum + dram__bytes_write.sum = 31,236,352 B against 31,264,768
+# algorithmic bytes).  Traffic grows with the bytes streamed, so the step's
+# traffic is reported as this ratio times the step's algorithmic bytes.
+NCU_TRAFFIC_RATIO = 31236352 / 31264768
 
 
 def _peaks():
@@ -263,9 +265,11 @@ def run_ours(args, rank, world, local_rank):
                          "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(achieved_gbs / hbm_peak, 4),
                          "peak_kind": peak_kind,
-                         "kernel": "gemv_lut_kernel (all launches of the step)",
+                         "kernel": "gemv_mma_kernel (all launches of the step)",
                          "launch_avg_us": round(ms * 1e3 / launches, 3),
-                         "traffic": NCU_TRAFFIC_PER_STEP},
+                         "traffic": int(step_bytes * NCU_TRAFFIC_RATIO),
+                         "traffic_note": "per step, scaled from one ncu capture of the "
+                                         "gate+up launch (traffic/algorithmic = 0.999)"},
             "e2e": {"value": round(world * 1000.0 / e2e_ms, 2), "unit": UNIT,
                     "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
                     "d2h_bytes_per_step": out_host.numel() * out_host.element_size()},
