@@ -191,6 +191,34 @@ int epq_linear(const epq_store* store, const void* x, int32_t x_dtype, int64_t m
                             workspace_bytes, stream);
 }
 
+int epq_linear_noalloc(const epq_store* stores, int32_t count, const void* x, int32_t x_dtype,
+                       void* const* outs, int32_t out_dtype, void* stream) {
+    if (count < 1 || count > kLutMaxStores || !stores || !outs)
+        return set_error(EPQ_EINVAL, "linear_noalloc: count=%d (1..%d) / NULL arrays", count,
+                         kLutMaxStores);
+    if (!dtype_ok(x_dtype) || !dtype_ok(out_dtype))
+        return set_error(EPQ_EDTYPE, "linear_noalloc: x/out dtype must be f32, f16 or bf16");
+    StoreD s[kLutMaxStores];
+    for (int i = 0; i < count; ++i) {
+        int rc = make_store(&stores[i], &s[i], "linear_noalloc");
+        if (rc) return rc;
+        if (s[i].k != s[0].k)
+            return set_error(EPQ_ESHAPE, "linear_noalloc: stores sharing x must have equal k");
+        if (!lut_eligible(s[i]))
+            return set_error(EPQ_EUNSUPPORTED, "linear_noalloc: store %d is not an EPQ_LAYOUT_TILED "
+                             "vector store (vec 4, 8-bit, group 128)", i);
+        if (!outs[i]) return set_error(EPQ_EINVAL, "linear_noalloc: out[%d] is NULL", i);
+    }
+    if (!lut_counters_fit(s, count))
+        return set_error(EPQ_EUNSUPPORTED, "linear_noalloc: too many row blocks");
+    if (!x || reinterpret_cast<uintptr_t>(x) % dtype_size(x_dtype))
+        return set_error(EPQ_EINVAL, "linear_noalloc: x is NULL or misaligned");
+    return launch_linear_lut_static(s, count, x, x_dtype, outs, out_dtype,
+                                    static_cast<cudaStream_t>(stream));
+}
+
+int64_t epq_linear_noalloc_max_scratch(void) { return lut_static_scratch_bytes(); }
+
 int epq_linear_bwd(const epq_store* store, const void* x, int64_t ldx, const void* dy, int64_t ldy,
                    int32_t act_dtype, int64_t m, void* dx, int64_t lddx, int32_t dx_dtype,
                    float* dscale, float* dcb, void* stream) {

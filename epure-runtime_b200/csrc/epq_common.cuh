@@ -120,5 +120,8 @@ bool lut_counters_fit(const StoreD* s, int count);
 int64_t lut_workspace_bytes(const StoreD* s, int count);
 int launch_linear_lut(const StoreD* s, int count, const void* x, int x_dtype, void* const* outs,
                       int out_dtype, void* ws, int64_t ws_bytes, cudaStream_t st);
+int64_t lut_static_scratch_bytes();
+int launch_linear_lut_static(const StoreD* s, int count, const void* x, int x_dtype,
+                             void* const* outs, int out_dtype, cudaStream_t st);
 
 }  // namespace epq

@@ -29,6 +29,8 @@
 //   partials[g][row]; a per-row-block counter picks the last arriving team,
 //   which adds the partials in group order and writes the output row-block,
 //   then resets the counter to zero for the next call.
+#include <mutex>
+
 #include "epq_common.cuh"
 
 namespace epq {
@@ -402,6 +404,62 @@ int lut_read_device_error(int* flag) {
     if (cudaMemcpyFromSymbol(flag, g_lut_layout_error, sizeof(int)) != cudaSuccess)
         return check_launch("read gemv_lut error flag");
     return EPQ_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of the batch-1 LUT GEMV.
+//
+// Some callers cannot call cudaMalloc (or any allocating routine) at the point
+// where they run the op: a plugin loaded into a serving engine whose memory
+// manager reserves the whole device up front and forbids side allocations, or
+// a latency-critical loop where an allocation could block or fail.  For them
+// the workspace of the LUT kernel (completion counters + partial sums) lives
+// in this file-scope device array instead of a caller buffer.  Every GPU that
+// loads the library holds it until the process exits.
+// ---------------------------------------------------------------------------
+constexpr int64_t kStaticScratchBytes = 4 << 20;   // 4 MiB: counters + partial sums
+__device__ __align__(256) unsigned char g_lut_static_scratch[kStaticScratchBytes];
+
+namespace {
+std::mutex g_static_mu;
+void* g_static_ptr[64] = {nullptr};
+}  // namespace
+
+int64_t lut_static_scratch_bytes() { return kStaticScratchBytes; }
+
+int launch_linear_lut_static(const StoreD* s, int count, const void* x, int x_dtype,
+                             void* const* outs, int out_dtype, cudaStream_t st) {
+    const int64_t need = lut_workspace_bytes(s, count);
+    if (need > kStaticScratchBytes)
+        return set_error(EPQ_EWORKSPACE,
+                         "linear_noalloc: these stores need %lld bytes of scratch; the static "
+                         "scratch holds %lld (use epq_linear_multi with a workspace)",
+                         (long long)need, (long long)kStaticScratchBytes);
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+        return set_error(EPQ_EUNSUPPORTED, "linear_noalloc: no usable current device");
+    void* ptr = nullptr;
+    {
+        // First call on a device: resolve the device address of the array with
+        // that device current (the host-side symbol is not a device address).
+        std::lock_guard<std::mutex> lock(g_static_mu);
+        if (g_static_ptr[dev] == nullptr) {
+            void* p = nullptr;
+            const cudaError_t e = cudaGetSymbolAddress(&p, g_lut_static_scratch);
+            if (e != cudaSuccess || p == nullptr)
+                return set_error(EPQ_ELAUNCH, "linear_noalloc: cudaGetSymbolAddress failed: %s",
+                                 cudaGetErrorString(e));
+            g_static_ptr[dev] = p;
+        }
+        ptr = g_static_ptr[dev];
+    }
+    // The completion counters must start at zero; clear the ones this call uses
+    // (partial sums are written before they are read).
+    int64_t n_counters = 0;
+    for (int i = 0; i < count; ++i) n_counters += s[i].rb;
+    if (cudaMemsetAsync(ptr, 0, n_counters * 4, st) != cudaSuccess)
+        return check_launch("linear_noalloc: clear counters");
+    return launch_linear_lut(s, count, x, x_dtype, outs, out_dtype, ptr, kStaticScratchBytes, st);
 }
 
 }  // namespace epq

@@ -45,7 +45,7 @@ class EpqStore(ctypes.Structure):
 EXPORTS = (
     "epq_abi_version", "epq_last_error", "epq_device_error", "epq_layout_bytes",
     "epq_relayout", "epq_linear_workspace_bytes", "epq_linear_multi", "epq_linear",
-    "epq_linear_bwd", "epq_materialize",
+    "epq_linear_bwd", "epq_materialize", "epq_linear_noalloc", "epq_linear_noalloc_max_scratch",
 )
 
 _lib = None
@@ -77,6 +77,8 @@ def load_library(path=None):
         lib.epq_linear.argtypes = [SP, P, I32, I64, I64, P, I64, I32, P, I64, P]
         lib.epq_linear_bwd.argtypes = [SP, P, I64, P, I64, I32, I64, P, I64, I32, P, P, P]
         lib.epq_materialize.argtypes = [SP, P, I64, I32, P]
+        lib.epq_linear_noalloc.argtypes = [SP, I32, P, I32, P, I32, P]
+        lib.epq_linear_noalloc_max_scratch.restype = I64
         for name in EXPORTS:
             getattr(lib, name)          # every declared entry point must be exported
         if lib.epq_abi_version() != 1:

@@ -163,6 +163,25 @@ int epq_linear(const epq_store* store, const void* x, int32_t x_dtype, int64_t m
                int64_t ldx, void* out, int64_t ldo, int32_t out_dtype, void* workspace,
                int64_t workspace_bytes, void* stream);
 
+/* Batch-1 linear that allocates nothing and takes no workspace: for callers
+ * that cannot call cudaMalloc when they run the op (a plugin inside a serving
+ * engine that owns all device memory, a loop where an allocation could block
+ * or fail).  No counterpart in the reference.
+ *   Same math and arguments as epq_linear_multi with m = 1 (x: k values,
+ *   outs[i]: n_i values), for EPQ_LAYOUT_TILED vector stores (vec 4, 8-bit,
+ *   group 128) only.  Its scratch is a file-scope device array of
+ *   epq_linear_noalloc_max_scratch() bytes (4 MiB) that every GPU loading the
+ *   library holds until exit; stores needing more are rejected with
+ *   EPQ_EWORKSPACE.  The first call on a device resolves the array's address
+ *   with that device current -- make that call before any stream capture.
+ *   All calls share the array (the counters are cleared on the stream at each
+ *   call), so calls that overlap on the GPU race: order them on one stream. */
+int epq_linear_noalloc(const epq_store* stores, int32_t count, const void* x, int32_t x_dtype,
+                       void* const* outs, int32_t out_dtype, void* stream);
+
+/* Bytes of the static scratch behind epq_linear_noalloc. */
+int64_t epq_linear_noalloc_max_scratch(void);
+
 /* Backward of out = x @ W^T with the indices frozen.
  *   dy [m, n] (ldy), x [m, k] (ldx): same dtype, f32/f16/bf16.
  *   dx [m, k] (lddx, dx_dtype) = dy @ W        (skipped when dx is NULL)
