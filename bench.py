@@ -10,9 +10,13 @@ with each launch reading the previous one's output.  The packed weights
 HBM; no L2 flush is needed.  Attention, norms and the bf16 lm_head are not
 part of the packed-linear path and are not in the step.
 
-Our arm replays the step as a CUDA graph of libepq.so launches (value), and
-separately through the public runner with host buffers (e2e: pinned H2D copy
-of the token input, replay, D2H copy of the output, every step).  At N > 1
+Our arm runs the step as ONE persistent launch of libepq.so's chain kernel
+(epq_chain_run: every packed linear of the token, weights streamed through a
+TMA ring per SM, grid barriers between dependent linears), replayed from a CUDA
+graph (value), and separately through the public runner with host buffers
+(e2e: pinned H2D copy of the token input, replay, D2H copy of the output, every
+step).  `--mode per-linear` instead replays 128 launches of the single-linear
+tensor-core GEMV (one per fused q/k/v, o, gate/up, down).  At N > 1
 each rank runs an independent replica on its own GPU (weak scaling; the 8B
 model fits one GPU, so there is no collective on the data path); the time is
 the max over ranks.
@@ -36,14 +40,17 @@ sys.path.insert(0, ROOT)
 
 METRIC = "decode tok/s bs1 @8B; dequant-GEMV HBM GB/s as % of B200 peak"
 UNIT = "tok/s"
-WORKLOAD = "llama3-8b packed linears, batch-1 decode token (224 linears, 128 launches)"
+WORKLOAD = "llama3-8b packed linears, batch-1 decode token (224 linears)"
 
-# DRAM traffic / algorithmic bytes of gemv_mma_kernel, from one ncu capture of
-# a Llama-3-8B gate+up launch (profiles/gemv_mma_kernel_llama3-8b_gateup_b1.md:
-# dram__bytes_read.sum + dram__bytes_write.sum = 31,236,352 B against 31,264,768
-# algorithmic bytes).  Traffic grows with the bytes streamed, so the step's
-# traffic is reported as this ratio times the step's algorithmic bytes.
-NCU_TRAFFIC_RATIO = 31236352 / 31264768
+# DRAM traffic / algorithmic bytes per mode, from one ncu capture each.  Traffic
+# grows with the bytes streamed, so a step's traffic is reported as the ratio
+# times the step's algorithmic bytes.
+#   per-linear: gemv_mma_kernel on a Llama-3-8B gate+up launch
+#     (profiles/gemv_mma_kernel_llama3-8b_gateup_b1.md): 31,236,352 B of
+#     dram__bytes_read.sum + dram__bytes_write.sum against 31,264,768 B.
+NCU_TRAFFIC_RATIO = {"per-linear": 31236352 / 31264768}
+TRAFFIC_NOTE = {"per-linear": "per step, scaled from one ncu capture of the gate+up launch "
+                              "(traffic/algorithmic = 0.999)"}
 
 
 def _peaks():
@@ -179,13 +186,20 @@ def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
     from epure import synthetic
-    from epure.decode import GraphedLinearStack
+    from epure.decode import ChainedLinearStack, GraphedLinearStack
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     shapes = synthetic.LLAMA3_8B
-    stack = synthetic.LinearStack(shapes, device=dev, seed=1000 * rank)
-    runner = GraphedLinearStack(stack, m=1, dtype=torch.bfloat16, device=dev).capture()
+    chain = args.mode == "chain"
+    stack = synthetic.LinearStack(shapes, device=dev, seed=1000 * rank,
+                                  gpu_layout="tiled" if chain else "mma16")
+    if chain:
+        runner = ChainedLinearStack(stack, dtype=torch.bfloat16, device=dev).capture()
+        kernel_name = "chain_kernel (one persistent launch per step)"
+    else:
+        runner = GraphedLinearStack(stack, m=1, dtype=torch.bfloat16, device=dev).capture()
+        kernel_name = "gemv_mma_kernel (all 128 launches of the step)"
     g = torch.Generator(device=dev).manual_seed(rank)
     runner.x.copy_(torch.randn(runner.x.shape, generator=g, device=dev).to(torch.bfloat16))
     step_bytes = stack.algorithmic_bytes(m=1, act_bytes=2)
@@ -257,7 +271,7 @@ def run_ours(args, rank, world, local_rank):
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic",
-            "config": {"workload": WORKLOAD, "global_batch": world, "seq_len": 1,
+            "config": {"workload": WORKLOAD, "mode": args.mode, "global_batch": world, "seq_len": 1,
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                        "l2": "inputs larger than L2 (1.9 GB of packed weights per step)",
                        "bytes_per_step": step_bytes},
@@ -265,11 +279,11 @@ def run_ours(args, rank, world, local_rank):
                          "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(achieved_gbs / hbm_peak, 4),
                          "peak_kind": peak_kind,
-                         "kernel": "gemv_mma_kernel (all launches of the step)",
+                         "kernel": kernel_name,
                          "launch_avg_us": round(ms * 1e3 / launches, 3),
-                         "traffic": int(step_bytes * NCU_TRAFFIC_RATIO),
-                         "traffic_note": "per step, scaled from one ncu capture of the "
-                                         "gate+up launch (traffic/algorithmic = 0.999)"},
+                         "traffic": (int(step_bytes * NCU_TRAFFIC_RATIO[args.mode])
+                                     if NCU_TRAFFIC_RATIO.get(args.mode) else None),
+                         "traffic_note": TRAFFIC_NOTE.get(args.mode)},
             "e2e": {"value": round(world * 1000.0 / e2e_ms, 2), "unit": UNIT,
                     "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
                     "d2h_bytes_per_step": out_host.numel() * out_host.element_size()},
@@ -291,6 +305,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--mode", choices=["chain", "per-linear"], default="chain")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -77,6 +77,7 @@ int make_store(const epq_store* in, StoreD* s, const char* who) {
 
 int lut_read_device_error(int* flag);
 int mma_read_device_error(int* flag);
+int chain_read_device_error(int* flag);
 
 static bool x_ok(const void* x, int64_t m, int64_t k, int64_t ldx) {
     return (m == 0 || k == 0) || (x != nullptr && ldx >= k);
@@ -94,12 +95,16 @@ const char* epq_last_error(void) { return g_err; }
 
 int epq_device_error(int* flag) {
     if (!flag) return set_error(EPQ_EINVAL, "epq_device_error: flag is NULL");
-    int lut = 0, mma = 0;
+    int lut = 0, mma = 0, chain = 0;
     int rc = lut_read_device_error(&lut);
     if (rc) return rc;
     rc = mma_read_device_error(&mma);
     if (rc) return rc;
-    *flag = (lut ? 1 : 0) | (mma ? 2 : 0);   // bit 0: LUT placement check, bit 1: a bounded wait gave up
+    rc = chain_read_device_error(&chain);
+    if (rc) return rc;
+    // bit 0: LUT placement check; bit 1: a bounded wait gave up (GEMV or chain);
+    // bit 2: the chain kernel's placement or grid check failed
+    *flag = (lut ? 1 : 0) | ((mma || chain == 1) ? 2 : 0) | (chain == 2 ? 4 : 0);
     return EPQ_OK;
 }
 

@@ -7,6 +7,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <vector>
+
 #include "epq.h"
 
 namespace epq {
@@ -107,6 +109,12 @@ int launch_materialize(const StoreD& s, void* w, int64_t ldw, int out_dtype, cud
 int64_t layout_bytes(int layout, int64_t n, int64_t k, int vec, int group);
 int launch_relayout(const uint8_t* src, int layout, int64_t n, int64_t k, int vec, int group,
                     uint8_t* dst, cudaStream_t st);
+
+// Persistent chain kernel (k_chain_lut.cu).
+struct ChainStepD;
+struct ChainHeaderD;
+int chain_grid(int* grid);
+int chain_read_device_error(int* flag);
 
 // Small-batch tensor-core GEMV over EPQ_LAYOUT_MMA16 stores (k_gemv_mma.cu).
 bool mma_eligible(const StoreD& s, int64_t m, int x_dtype);

@@ -1,0 +1,676 @@
+// Persistent chain kernel: a whole sequence of batch-1 packed linears (one
+// decode token through a decoder's packed linears) in ONE cooperative launch.
+//
+// Reference op per step: epure/kernels/_triton.py:56-107 (the table-mode fused
+// dequant-matmul), applied in sequence as PackedLinear.forward calls
+// (epure/runtime.py:98-126) where each step's input is an earlier step's output.
+//
+// Why one launch.  At batch 1 the packed weights of one linear are 1-30 MB; a
+// kernel that streams that much spends a fixed ~3 us filling and draining the
+// memory pipeline, which for 128 dependent launches per token costs more than
+// the whole HBM roofline.  Here a producer warp per SM streams the weights of
+// every step through a 6-stage TMA ring (cp.async.bulk + mbarriers, no
+// multicast) without ever waiting for activations -- weights are static -- so
+// HBM keeps streaming across step boundaries; only the consumers wait for the
+// previous step to finish (a grid barrier: a per-step arrival counter in the
+// workspace, bounded spin).
+//
+// Inner loop (per index byte: one PRMT, one LDS.32, one FADD).  For one scale
+// group (32 index positions) the consumers build an activation table
+// T[e][j] = dot(cb[e, 0:4], x[4j : 4j+4]) in shared memory (fp32, 256 B per
+// entry e: 2 slots x 32 positions), so a row's group sum is sum_j T[idx[r, j]][j]
+// and the scale multiplies it once.  Indices arrive in EPQ_LAYOUT_TILED order
+// (16 rows x 32 positions per 512-byte tile); a team of 8 lanes owns a tile,
+// each lane 4 positions (rotated per team: the 32 lanes of a warp always hit 32
+// different banks), and a 3-step butterfly leaves each lane with 2 row sums.
+//
+// Split over k without a reduction tail.  A step's tiles are ordered (store,
+// group, row block) and each CTA takes a contiguous range, so it covers about
+// one group of many rows (one table build) and writes scaled group sums to a
+// partial buffer [group][row].  Nobody reduces them in that step: the NEXT
+// step's consumers add the partials of exactly the input columns they need
+// while staging their activation slice (deterministic order), and after the
+// last step all CTAs reduce the final output rows.  Partial buffers ping-pong
+// between steps.
+//
+// Safety: every mbarrier wait and every grid-barrier spin is bounded; a wait
+// that gives up sets g_chain_error (read by epq_device_error) and the kernel
+// runs to completion.  The launch is cooperative, so all CTAs are co-resident.
+#include <climits>
+#include <cstring>
+#include <vector>
+
+#include "epq_common.cuh"
+
+namespace epq {
+
+struct ChainStoreD {
+    const uint8_t* idx;   // EPQ_LAYOUT_TILED
+    const void* scale;    // group-major, rows padded to 16: scale(r, g) at g * s_g + r
+    const void* cb;
+    int64_t s_g;
+    int64_t part_off;     // offset (floats) of this store's partials in a partial buffer
+    int cb_dtype, scale_f32, levels, n;
+    int rb, ng, tile0, pad;
+};
+
+struct ChainStepD {
+    ChainStoreD st[kLutMaxStores];
+    int count, feed, k, kpos;
+    int total_tiles, tiles_per_cta, pad0, pad1;
+};
+
+struct ChainHeaderD {
+    int n_steps, grid;
+    int64_t part_floats;              // floats per partial buffer
+    int64_t steps_off, ctr_off, part_off0, part_off1;   // byte offsets in the workspace
+};
+
+namespace {
+
+constexpr int kConsumerWarps = 16;
+constexpr int kConsumers = kConsumerWarps * 32;
+constexpr int kThreads = kConsumers + 32;
+constexpr int kRing = 3;
+constexpr int kChunkTiles = 64;                                    // one tile per 8-lane team
+constexpr uint32_t kStageIdx = kChunkTiles * 512;                  // 32 KB of index tiles
+constexpr uint32_t kStageBytes = kStageIdx + kChunkTiles * 64;     // + scales (<= fp32)
+constexpr int kXParts = kConsumers / 32;                           // activation staging split
+// Shared-window addresses (the dynamic block starts at a small offset `base`).
+constexpr uint32_t kXsOff = 8192;      // from base: 2 x codebook [1024] fp32 below, then
+                                       // 2 x activation slice partials [kXParts][128] fp32
+constexpr uint32_t kBarOff = kXsOff + 2 * kXParts * 512;   // from base: full[kRing], empty[kRing]
+constexpr uint32_t kMiscOff = kBarOff + 128;               // from base: broadcast words
+constexpr uint32_t kLowStages = 26624; // window address of stage 0
+constexpr uint32_t kTBase = 65536;     // window address of T (low 16 bits zero for the PRMT trick)
+constexpr uint32_t kHighStages = 131072;   // window address of stages 1..2
+constexpr uint32_t kWindowEnd = kHighStages + 2 * kStageBytes;
+static_assert(kLowStages + kStageBytes <= kTBase, "stage 0 must end below the table");
+constexpr int kDynSmem = (int)kWindowEnd;
+constexpr uint32_t kWaitLimit = 1u << 22;   // mbarrier polls
+constexpr uint32_t kSpinLimit = 1u << 22;   // grid-barrier polls
+
+__device__ int g_chain_error = 0;
+
+__device__ __forceinline__ uint32_t stage_addr(int s) {
+    return s == 0 ? kLowStages : kHighStages + (s - 1) * kStageBytes;
+}
+
+__device__ __forceinline__ float lds_f32(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ float lds_scale(uint32_t addr, bool f32) {
+    if (f32) return lds_f32(addr);
+    unsigned short h;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h) : "r"(addr));
+    return __half2float(__ushort_as_half(h));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait; once any wait in the kernel has given up, later waits return at once.
+__device__ __forceinline__ void mbar_wait(uint32_t bar, uint32_t parity) {
+    for (uint32_t i = 0; i < kWaitLimit; ++i) {
+        if (mbar_try_wait(bar, parity)) return;
+        if ((i & 1023u) == 1023u && *reinterpret_cast<volatile int*>(&g_chain_error)) return;
+    }
+    atomicExch(&g_chain_error, 1);
+}
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+        "l"(src), "r"(bytes), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ void consumers_sync() {
+    asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+// Grid barrier: until every CTA has counted step `c` for this run (bounded).
+__device__ __forceinline__ void grid_wait(const unsigned* c, unsigned target) {
+    for (uint32_t it = 0; it < kSpinLimit; ++it) {
+        if ((int)(ld_acquire(c) - target) >= 0) return;
+        if ((it & 255u) == 255u && *reinterpret_cast<volatile int*>(&g_chain_error)) return;
+    }
+    atomicExch(&g_chain_error, 1);
+}
+
+// Chunk iterator over a CTA's tile range of one step (identical in producer and consumers).
+struct ChunkIt {
+    int t, t_end;
+    __device__ bool next(const ChainStepD& S, int& si, int& g, int& rb0, int& nt) {
+        if (t >= t_end) return false;
+        si = 0;
+        while (si + 1 < S.count && t >= S.st[si + 1].tile0) ++si;
+        const ChainStoreD& C = S.st[si];
+        const int local = t - C.tile0;
+        g = local / C.rb;
+        rb0 = local - g * C.rb;
+        const int seg_end = min(t_end, C.tile0 + (g + 1) * C.rb);
+        nt = min(kChunkTiles, seg_end - t);
+        t += nt;
+        return true;
+    }
+};
+
+__global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __restrict__ ws, const void* x0,
+                                                            int x_dtype, void* out, int out_dtype) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+    if (base + kMiscOff + 64 > kLowStages || (int)gridDim.x != reinterpret_cast<const int*>(ws)[1]) {
+        // placement the addresses below rely on, or a grid other than the one
+        // the descriptors were built for
+        if (threadIdx.x == 0) atomicExch(&g_chain_error, 2);
+        return;
+    }
+    const ChainHeaderD& H = *reinterpret_cast<const ChainHeaderD*>(ws);
+    const ChainStepD* steps = reinterpret_cast<const ChainStepD*>(ws + H.steps_off);
+    unsigned* ctr = reinterpret_cast<unsigned*>(const_cast<uint8_t*>(ws) + H.ctr_off);  // [n_steps] + done + gen
+    float* part[2] = {reinterpret_cast<float*>(const_cast<uint8_t*>(ws) + H.part_off0),
+                      reinterpret_cast<float*>(const_cast<uint8_t*>(ws) + H.part_off1)};
+    const int n_steps = H.n_steps;
+    const int G = gridDim.x;
+    const uint32_t bar_full = base + kBarOff, bar_empty = bar_full + 8 * kRing;
+    unsigned* misc = reinterpret_cast<unsigned*>(smem + kMiscOff);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kRing; ++s) {
+            mbar_init(bar_full + 8 * s, 1);
+            mbar_init(bar_empty + 8 * s, kConsumerWarps);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        misc[0] = *reinterpret_cast<volatile unsigned*>(&ctr[n_steps + 1]);   // run generation
+    }
+    __syncthreads();
+    const unsigned target = (misc[0] + 1u) * (unsigned)G;
+
+    if (warp == kConsumerWarps) {
+        // ---------------- producer: stream every step's tiles into the ring ----------------
+        int i = 0;
+        for (int j = 0; j < n_steps; ++j) {
+            const ChainStepD& S = steps[j];
+            ChunkIt it{(int)blockIdx.x * S.tiles_per_cta,
+                       min(((int)blockIdx.x + 1) * S.tiles_per_cta, S.total_tiles)};
+            int si, g, rb0, nt;
+            while (it.next(S, si, g, rb0, nt)) {
+                const int stage = i % kRing;
+                if (i >= kRing) mbar_wait(bar_empty + 8 * stage, ((i / kRing) - 1) & 1);
+                const ChainStoreD& C = S.st[si];
+                const uint32_t esz = C.scale_f32 ? 4u : 2u;
+                const uint32_t dst = stage_addr(stage);
+                if (lane == 0) {
+                    mbar_expect_tx(bar_full + 8 * stage, nt * 512u + nt * 16u * esz);
+                    bulk_g2s(dst, C.idx + ((int64_t)g * C.rb + rb0) * 512, nt * 512u, bar_full + 8 * stage);
+                    bulk_g2s(dst + kStageIdx,
+                             static_cast<const char*>(C.scale) + ((int64_t)g * C.s_g + (int64_t)rb0 * 16) * esz,
+                             nt * 16u * esz, bar_full + 8 * stage);
+                }
+                __syncwarp();
+                ++i;
+            }
+        }
+        return;
+    }
+
+    // ---------------- consumers ----------------
+    const int team = lane >> 3, tl = lane & 7;
+    // Double-buffered staging (parity flips per change), so a new table's inputs
+    // can be written while no warp still needs the previous ones.
+    float* cbf_buf = reinterpret_cast<float*>(smem);                          // [2][256][4]
+    float* xs_buf = reinterpret_cast<float*>(smem + kXsOff);                  // [2][kXParts][128]
+    int cbp = 0, xsp = 0;
+    float* T = reinterpret_cast<float*>(smem + (kTBase - base));              // [256][2][32]
+    // Codebooks are fetched one step ahead into registers (values 2t, 2t+1 of
+    // each store of the step), so building a table never waits on DRAM.
+    uint2 cb_raw[kLutMaxStores];
+    float2 cb_cur[kLutMaxStores];
+    auto cb_prefetch = [&](int jj) {
+#pragma unroll
+        for (int q = 0; q < kLutMaxStores; ++q) cb_raw[q] = make_uint2(0u, 0u);
+        if (jj >= n_steps) return;
+        const ChainStepD& N = steps[jj];
+        const int e = 2 * threadIdx.x;
+#pragma unroll
+        for (int q = 0; q < kLutMaxStores; ++q) {
+            if (q < N.count && e < N.st[q].levels * 4) {
+                const int dt = N.st[q].cb_dtype;
+                const uint8_t* p = static_cast<const uint8_t*>(N.st[q].cb) + (int64_t)e * (dt == EPQ_F32 ? 4 : 2);
+                if (dt == EPQ_F32)
+                    asm volatile("ld.global.nc.v2.u32 {%0,%1}, [%2];" : "=r"(cb_raw[q].x), "=r"(cb_raw[q].y) : "l"(p));
+                else
+                    asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(cb_raw[q].x) : "l"(p));
+            }
+        }
+    };
+    auto cb_promote = [&](int jj) {
+        const ChainStepD& N = steps[jj];
+#pragma unroll
+        for (int q = 0; q < kLutMaxStores; ++q) {
+            const int dt = q < N.count ? N.st[q].cb_dtype : EPQ_F32;
+            if (dt == EPQ_F32) {
+                cb_cur[q] = make_float2(__uint_as_float(cb_raw[q].x), __uint_as_float(cb_raw[q].y));
+            } else if (dt == EPQ_F16) {
+                const __half2 h = *reinterpret_cast<const __half2*>(&cb_raw[q].x);
+                cb_cur[q] = __half22float2(h);
+            } else {
+                const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&cb_raw[q].x);
+                cb_cur[q] = __bfloat1622float2(h);
+            }
+        }
+    };
+    cb_prefetch(0);
+
+    int i = 0, slot = 0;
+    for (int j = 0; j < n_steps; ++j) {
+        const ChainStepD& S = steps[j];
+        cb_promote(j);
+        cb_prefetch(j + 1);
+        if (j > 0) {
+            if (threadIdx.x == 0) grid_wait(&ctr[j - 1], target);   // every CTA finished step j-1
+            consumers_sync();
+        }
+        // Input of this step: x0 (step 0) or the partials of step j-1's feed store.
+        const ChainStepD* P = j > 0 ? &steps[j - 1] : nullptr;
+        const float* pin = j > 0 ? part[(j - 1) & 1] + P->st[P->feed].part_off : nullptr;
+        const int64_t pin_stride = j > 0 ? (int64_t)P->st[P->feed].rb * 16 : 0;
+        const int pin_ng = j > 0 ? P->st[P->feed].ng : 0;
+        float* pout = part[j & 1];
+
+        ChunkIt it{(int)blockIdx.x * S.tiles_per_cta,
+                   min(((int)blockIdx.x + 1) * S.tiles_per_cta, S.total_tiles)};
+        int si, g, rb0, nt, cur_s = -1, cur_g = -1;
+        while (it.next(S, si, g, rb0, nt)) {
+            const ChainStoreD& C = S.st[si];
+            if (si != cur_s || g != cur_g) {
+                // New (store, group): stage the codebook / activation slice, build T.
+                if (si != cur_s) {
+                    cbp ^= 1;
+                    float* cbf = cbf_buf + cbp * 1024;
+                    // codebook values 2t, 2t+1 of store si, loaded during the previous step
+                    float2 v = make_float2(0.f, 0.f);
+#pragma unroll
+                    for (int q = 0; q < kLutMaxStores; ++q)
+                        if (q == si) v = cb_cur[q];
+                    reinterpret_cast<float2*>(cbf)[threadIdx.x] = v;
+                }
+                if (g != cur_g) {
+                    xsp ^= 1;
+                    float* xs = xs_buf + xsp * (kXParts * 128);
+                    // x[128 g + 4 c4 .. +4] = sum over the input partial slices; thread
+                    // (c4, part) adds slices part, part + kXParts, ... (fixed order).
+                    const int c4 = threadIdx.x & 31, part = threadIdx.x >> 5;
+                    const int64_t c = (int64_t)g * 128 + 4 * c4;
+                    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (c < S.k) {
+                        if (j == 0) {
+                            if (part == 0)
+                                v = make_float4(load_f(x0, x_dtype, c), load_f(x0, x_dtype, c + 1),
+                                                load_f(x0, x_dtype, c + 2), load_f(x0, x_dtype, c + 3));
+                        } else {
+                            const float4* col = reinterpret_cast<const float4*>(pin + c);
+                            const int64_t st4 = pin_stride >> 2;
+#pragma unroll 8
+                            for (int gp = part; gp < pin_ng; gp += kXParts) {
+                                const float4 u = __ldcg(col + gp * st4);
+                                v.x += u.x;
+                                v.y += u.y;
+                                v.z += u.z;
+                                v.w += u.w;
+                            }
+                        }
+                    }
+                    reinterpret_cast<float4*>(xs)[part * 32 + c4] = v;
+                }
+                cur_s = si;
+                cur_g = g;
+                consumers_sync();
+                {
+                    const float* cbf = cbf_buf + cbp * 1024;
+                    const float* xs = xs_buf + xsp * (kXParts * 128);
+                    float4 xv = reinterpret_cast<const float4*>(xs)[lane];
+#pragma unroll
+                    for (int h = 1; h < kXParts; ++h) {
+                        const float4 u = reinterpret_cast<const float4*>(xs)[h * 32 + lane];
+                        xv.x += u.x;
+                        xv.y += u.y;
+                        xv.z += u.z;
+                        xv.w += u.w;
+                    }
+                    const float x0v = xv.x, x1v = xv.y, x2v = xv.z, x3v = xv.w;
+                    const float4* cb4 = reinterpret_cast<const float4*>(cbf);
+#pragma unroll 4
+                    for (int q = 0; q < 256 / kConsumerWarps; ++q) {
+                        const int e = warp + kConsumerWarps * q;
+                        const float4 cv = cb4[e];
+                        float v = cv.x * x0v;
+                        v = fmaf(cv.y, x1v, v);
+                        v = fmaf(cv.z, x2v, v);
+                        v = fmaf(cv.w, x3v, v);
+                        T[e * 64 + (slot ^ 1) * 32 + lane] = v;
+                    }
+                }
+                slot ^= 1;
+                consumers_sync();
+            }
+            const int stage = i % kRing;
+            mbar_wait(bar_full + 8 * stage, (i / kRing) & 1);
+            const uint32_t sdst = stage_addr(stage);
+            const int tile = warp * 4 + team;
+            float acc[16];
+#pragma unroll
+            for (int r = 0; r < 16; ++r) acc[r] = 0.f;
+            if (tile < nt) {
+                const uint32_t tb = sdst + tile * 512;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int pos = tl + 8 * ((q + team) & 3);
+                    const uint4 w = lds128(tb + pos * 16);
+                    const uint32_t tbase = kTBase | (uint32_t)(slot * 128 + 4 * pos);
+                    const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                    for (int wi = 0; wi < 4; ++wi)
+#pragma unroll
+                        for (int b = 0; b < 4; ++b)
+                            acc[wi * 4 + b] += lds_f32(__byte_perm(ww[wi], tbase, 0x7604 | (b << 4)));
+                }
+            }
+            // Butterfly over the 8 lanes of the team: lane tl ends with rows 2tl, 2tl+1.
+            const bool b2 = tl & 4, b1 = tl & 2, b0 = tl & 1;
+            float a1[8], a2[4], a3[2];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const float send = b2 ? acc[q] : acc[q + 8];
+                const float keep = b2 ? acc[q + 8] : acc[q];
+                a1[q] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float send = b1 ? a1[q] : a1[q + 4];
+                const float keep = b1 ? a1[q + 4] : a1[q];
+                a2[q] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+            }
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+                const float send = b0 ? a2[q] : a2[q + 2];
+                const float keep = b0 ? a2[q + 2] : a2[q];
+                a3[q] = keep + __shfl_xor_sync(0xffffffffu, send, 1);
+            }
+            if (tile < nt) {
+                const bool f32 = C.scale_f32 != 0;
+                const uint32_t esz = f32 ? 4u : 2u;
+                const uint32_t sa = sdst + kStageIdx + tile * 16 * esz + 2 * tl * esz;
+                const float s0 = lds_scale(sa, f32), s1 = lds_scale(sa + esz, f32);
+                const int64_t row = (int64_t)(rb0 + tile) * 16 + 2 * tl;
+                *reinterpret_cast<float2*>(pout + C.part_off + (int64_t)g * C.rb * 16 + row) =
+                    make_float2(a3[0] * s0, a3[1] * s1);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_empty + 8 * stage);
+            ++i;
+        }
+        consumers_sync();                  // all of this CTA's partials for step j are written
+        if (threadIdx.x == 0) {
+            __threadfence();
+            atomicAdd(&ctr[j], 1u);
+        }
+    }
+
+    // Final output: the last step's feed store, rows split over the CTAs.
+    if (threadIdx.x == 0) grid_wait(&ctr[n_steps - 1], target);
+    consumers_sync();
+    {
+        const ChainStepD& L = steps[n_steps - 1];
+        const ChainStoreD& F = L.st[L.feed];
+        const float* pl = part[(n_steps - 1) & 1] + F.part_off;
+        const int64_t stride = (int64_t)F.rb * 16;
+        const int r0 = (int)((int64_t)F.n * blockIdx.x / G), r1 = (int)((int64_t)F.n * (blockIdx.x + 1) / G);
+        // 8 lanes per row, each adding every 8th slice; a 3-step shuffle combines them.
+        const int sub8 = lane & 7;
+        for (int rbase = r0; rbase < r1; rbase += kConsumers / 8) {
+            const int r = rbase + (threadIdx.x >> 3);
+            float v = 0.f;
+            if (r < r1) {
+#pragma unroll 4
+                for (int gg = sub8; gg < F.ng; gg += 8) v += __ldcg(pl + gg * stride + r);
+            }
+            v += __shfl_xor_sync(0xffffffffu, v, 1);
+            v += __shfl_xor_sync(0xffffffffu, v, 2);
+            v += __shfl_xor_sync(0xffffffffu, v, 4);
+            if (r < r1 && sub8 == 0) store_f(out, out_dtype, r, v);
+        }
+    }
+    consumers_sync();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        // The last CTA to finish advances the run generation for the next launch.
+        if (atomicAdd(&ctr[n_steps], 1u) == target - 1u) atomicAdd(&ctr[n_steps + 1], 1u);
+    }
+}
+
+int g_chain_sms[64] = {0};
+bool g_chain_attr[64] = {false};
+
+}  // namespace
+
+int chain_read_device_error(int* flag) {
+    if (cudaMemcpyFromSymbol(flag, g_chain_error, sizeof(int)) != cudaSuccess)
+        return check_launch("read chain error flag");
+    return EPQ_OK;
+}
+
+static int64_t al256(int64_t v) { return (v + 255) & ~int64_t(255); }
+
+// Host-side description of a chain (validated) and its workspace layout.
+struct StoreArr {
+    StoreD s[kLutMaxStores];
+};
+
+int chain_layout(const StoreArr* st, const int* counts, const int* feeds, int n_steps,
+                 int grid, std::vector<ChainStepD>* out_steps, ChainHeaderD* hdr, int64_t* ws_bytes) {
+    if (n_steps < 1) return set_error(EPQ_EINVAL, "chain: n_steps=%d", n_steps);
+    std::vector<ChainStepD> steps(n_steps);
+    int64_t part_floats = 0;
+    for (int j = 0; j < n_steps; ++j) {
+        ChainStepD& D = steps[j];
+        memset(&D, 0, sizeof(D));
+        D.count = counts[j];
+        D.feed = feeds[j];
+        if (D.count < 1 || D.count > kLutMaxStores || D.feed < 0 || D.feed >= D.count)
+            return set_error(EPQ_EINVAL, "chain: step %d has count=%d feed=%d", j, D.count, D.feed);
+        int64_t tiles = 0, floats = 0;
+        for (int i = 0; i < D.count; ++i) {
+            const StoreD& s = st[j].s[i];
+            if (!lut_eligible(s))
+                return set_error(EPQ_EUNSUPPORTED, "chain: step %d store %d is not an EPQ_LAYOUT_TILED "
+                                 "vector store (vec 4, 8-bit, group 128)", j, i);
+            if (s.k != st[j].s[0].k) return set_error(EPQ_ESHAPE, "chain: step %d stores differ in k", j);
+            const int64_t esz = s.scale_dtype == EPQ_F32 ? 4 : 2;
+            if ((s.scale_dtype != EPQ_F16 && s.scale_dtype != EPQ_F32) || s.s_n != 1 || s.s_g % 16 ||
+                s.s_g < s.rb * 16 || (reinterpret_cast<uintptr_t>(s.scale) % (16 * esz)) ||
+                (reinterpret_cast<uintptr_t>(s.idx) & 15))
+                return set_error(EPQ_ELAYOUT, "chain: step %d store %d needs group-major f16/f32 scales "
+                                 "with a row stride padded to 16 and 16-byte aligned buffers", j, i);
+            ChainStoreD& C = D.st[i];
+            C.idx = s.idx;
+            C.scale = s.scale;
+            C.cb = s.cb;
+            C.s_g = s.s_g;
+            C.cb_dtype = s.cb_dtype;
+            C.scale_f32 = s.scale_dtype == EPQ_F32;
+            C.levels = s.levels;
+            C.n = (int)s.n;
+            C.rb = (int)s.rb;
+            C.ng = (int)s.ng;
+            C.tile0 = (int)tiles;
+            C.part_off = floats;
+            tiles += s.ng * s.rb;
+            floats += s.ng * s.rb * 16;
+        }
+        if (tiles >= (int64_t(1) << 30)) return set_error(EPQ_EUNSUPPORTED, "chain: step %d too large", j);
+        D.k = (int)st[j].s[0].k;
+        D.kpos = (int)(st[j].s[0].k / 4);
+        D.total_tiles = (int)tiles;
+        D.tiles_per_cta = (int)cdiv(tiles, grid);
+        if (j > 0 && st[j - 1].s[feeds[j - 1]].n != st[j].s[0].k)
+            return set_error(EPQ_ESHAPE, "chain: step %d input width %lld != step %d feed output %lld", j,
+                             (long long)st[j].s[0].k, j - 1, (long long)st[j - 1].s[feeds[j - 1]].n);
+        part_floats = floats > part_floats ? floats : part_floats;
+    }
+    ChainHeaderD H{};
+    H.n_steps = n_steps;
+    H.grid = grid;
+    H.part_floats = part_floats;
+    H.steps_off = 256;
+    H.ctr_off = al256(H.steps_off + (int64_t)sizeof(ChainStepD) * n_steps);
+    H.part_off0 = al256(H.ctr_off + 4 * (n_steps + 2));
+    H.part_off1 = al256(H.part_off0 + 4 * part_floats);
+    *ws_bytes = al256(H.part_off1 + 4 * part_floats);
+    *hdr = H;
+    if (out_steps) *out_steps = std::move(steps);
+    return EPQ_OK;
+}
+
+int chain_grid(int* grid) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+        return set_error(EPQ_EUNSUPPORTED, "chain: no usable current device");
+    if (!g_chain_attr[dev]) {
+        if (cudaFuncSetAttribute(chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmem) !=
+            cudaSuccess)
+            return check_launch("cudaFuncSetAttribute(chain_kernel)");
+        int per_sm = 0, sms = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, chain_kernel, kThreads, kDynSmem) !=
+                cudaSuccess ||
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+            return check_launch("chain occupancy");
+        if (per_sm < 1) return set_error(EPQ_EUNSUPPORTED, "chain: kernel does not fit on an SM");
+        g_chain_sms[dev] = sms;
+        g_chain_attr[dev] = true;
+    }
+    *grid = g_chain_sms[dev];
+    return EPQ_OK;
+}
+
+int chain_write(const std::vector<ChainStepD>& steps, const ChainHeaderD& H, void* ws, cudaStream_t st) {
+    std::vector<uint8_t> host(H.part_off0, 0);
+    memcpy(host.data(), &H, sizeof(H));
+    memcpy(host.data() + H.steps_off, steps.data(), sizeof(ChainStepD) * steps.size());
+    // counters (and the run generation) start at zero
+    if (cudaMemcpyAsync(ws, host.data(), host.size(), cudaMemcpyHostToDevice, st) != cudaSuccess)
+        return check_launch("chain: write descriptors");
+    if (cudaStreamSynchronize(st) != cudaSuccess) return check_launch("chain: write descriptors");
+    return EPQ_OK;
+}
+
+int chain_launch(const void* ws, const void* x, int x_dtype, void* out, int out_dtype, int grid,
+                 cudaStream_t st) {
+    const uint8_t* wsp = static_cast<const uint8_t*>(ws);
+    void* args[] = {(void*)&wsp, (void*)&x, (void*)&x_dtype, (void*)&out, (void*)&out_dtype};
+    if (cudaLaunchCooperativeKernel((void*)chain_kernel, dim3(grid), dim3(kThreads), args, kDynSmem, st) !=
+        cudaSuccess)
+        return check_launch("chain_kernel");
+    return check_launch("chain_kernel");
+}
+
+}  // namespace epq
+
+using namespace epq;
+
+extern "C" {
+
+static int chain_collect(const epq_chain_step* steps, int32_t n_steps, StoreArr* st,
+                         int* counts, int* feeds) {
+    for (int j = 0; j < n_steps; ++j) {
+        counts[j] = steps[j].count;
+        feeds[j] = steps[j].feed;
+        if (counts[j] < 1 || counts[j] > kLutMaxStores)
+            return set_error(EPQ_EINVAL, "chain: step %d count=%d (1..%d)", j, counts[j], kLutMaxStores);
+        for (int i = 0; i < counts[j]; ++i) {
+            int rc = make_store(&steps[j].stores[i], &st[j].s[i], "chain");
+            if (rc) return rc;
+        }
+    }
+    return EPQ_OK;
+}
+
+int epq_chain_workspace_bytes(const epq_chain_step* steps, int32_t n_steps, int64_t* bytes) {
+    if (!steps || !bytes || n_steps < 1 || n_steps > 4096)
+        return set_error(EPQ_EINVAL, "chain_workspace_bytes: steps/bytes NULL or n_steps=%d", n_steps);
+    std::vector<StoreArr> st(n_steps);
+    std::vector<int> counts(n_steps), feeds(n_steps);
+    int rc = chain_collect(steps, n_steps, st.data(), counts.data(), feeds.data());
+    if (rc) return rc;
+    int grid = 0;
+    rc = chain_grid(&grid);
+    if (rc) return rc;
+    ChainHeaderD H;
+    return chain_layout(st.data(), counts.data(), feeds.data(), n_steps, grid, nullptr, &H, bytes);
+}
+
+int epq_chain_prepare(const epq_chain_step* steps, int32_t n_steps, void* workspace,
+                      int64_t workspace_bytes, void* stream) {
+    if (!steps || !workspace || n_steps < 1 || n_steps > 4096)
+        return set_error(EPQ_EINVAL, "chain_prepare: steps/workspace NULL or n_steps=%d", n_steps);
+    if (reinterpret_cast<uintptr_t>(workspace) & 255)
+        return set_error(EPQ_EALIGN, "chain_prepare: workspace must be 256-byte aligned");
+    std::vector<StoreArr> st(n_steps);
+    std::vector<int> counts(n_steps), feeds(n_steps);
+    int rc = chain_collect(steps, n_steps, st.data(), counts.data(), feeds.data());
+    if (rc) return rc;
+    int grid = 0;
+    rc = chain_grid(&grid);
+    if (rc) return rc;
+    std::vector<ChainStepD> desc;
+    ChainHeaderD H;
+    int64_t need = 0;
+    rc = chain_layout(st.data(), counts.data(), feeds.data(), n_steps, grid, &desc, &H, &need);
+    if (rc) return rc;
+    if (workspace_bytes < need)
+        return set_error(EPQ_EWORKSPACE, "chain_prepare: workspace of %lld bytes needed, %lld given",
+                         (long long)need, (long long)workspace_bytes);
+    return chain_write(desc, H, workspace, static_cast<cudaStream_t>(stream));
+}
+
+int epq_chain_run(const void* workspace, const void* x, int32_t x_dtype, void* out, int32_t out_dtype,
+                  void* stream) {
+    if (!workspace || !x || !out) return set_error(EPQ_EINVAL, "chain_run: NULL pointer");
+    if (!dtype_ok(x_dtype) || !dtype_ok(out_dtype))
+        return set_error(EPQ_EDTYPE, "chain_run: x/out dtype must be f32, f16 or bf16");
+    int grid = 0;
+    int rc = chain_grid(&grid);
+    if (rc) return rc;
+    return chain_launch(workspace, x, x_dtype, out, out_dtype, grid, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

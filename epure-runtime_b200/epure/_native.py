@@ -13,7 +13,8 @@ import threading
 import torch
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libepq.so")
+# The library next to this file, unless EPURE_LIBEPQ names another build.
+LIB_PATH = os.environ.get("EPURE_LIBEPQ") or os.path.join(_HERE, "libepq.so")
 
 EPQ_F32, EPQ_F16, EPQ_BF16 = 0, 1, 2
 LAYOUT_ROWS, LAYOUT_TILED, LAYOUT_MMA16 = 0, 1, 2
@@ -42,10 +43,15 @@ class EpqStore(ctypes.Structure):
     ]
 
 
+class EpqChainStep(ctypes.Structure):
+    _fields_ = [("stores", EpqStore * 4), ("count", ctypes.c_int32), ("feed", ctypes.c_int32)]
+
+
 EXPORTS = (
     "epq_abi_version", "epq_last_error", "epq_device_error", "epq_layout_bytes",
     "epq_relayout", "epq_linear_workspace_bytes", "epq_linear_multi", "epq_linear",
     "epq_linear_bwd", "epq_materialize", "epq_linear_noalloc", "epq_linear_noalloc_max_scratch",
+    "epq_chain_workspace_bytes", "epq_chain_prepare", "epq_chain_run",
 )
 
 _lib = None
@@ -79,6 +85,10 @@ def load_library(path=None):
         lib.epq_materialize.argtypes = [SP, P, I64, I32, P]
         lib.epq_linear_noalloc.argtypes = [SP, I32, P, I32, P, I32, P]
         lib.epq_linear_noalloc_max_scratch.restype = I64
+        CP = ctypes.POINTER(EpqChainStep)
+        lib.epq_chain_workspace_bytes.argtypes = [CP, I32, ctypes.POINTER(I64)]
+        lib.epq_chain_prepare.argtypes = [CP, I32, P, I64, P]
+        lib.epq_chain_run.argtypes = [P, P, I32, P, I32, P]
         for name in EXPORTS:
             getattr(lib, name)          # every declared entry point must be exported
         if lib.epq_abi_version() != 1:
@@ -257,6 +267,37 @@ def relayout(idx_rows, layout, n, k, vec, group):
     _check(lib.epq_relayout(src.data_ptr(), LAYOUT_CODES[layout], n, k, vec, group,
                             dst.data_ptr(), _stream_ptr(src.device)), "epq_relayout")
     return dst
+
+
+# ---------------------------------------------------------------------------
+# chains: a sequence of batch-1 linears in one persistent launch
+# ---------------------------------------------------------------------------
+def chain_prepare(steps):
+    """``steps``: list of (stores, feed).  Returns the prepared workspace (uint8 tensor)."""
+    lib = load_library()
+    arr = (EpqChainStep * len(steps))()
+    keep = []
+    for j, (stores, feed) in enumerate(steps):
+        arr[j].count = len(stores)
+        arr[j].feed = feed
+        for i, st in enumerate(stores):
+            arr[j].stores[i] = describe_store(st)
+            keep.append(st)
+    need = ctypes.c_int64(0)
+    _check(lib.epq_chain_workspace_bytes(arr, len(steps), ctypes.byref(need)),
+           "epq_chain_workspace_bytes")
+    dev = steps[0][0][0].packed.device
+    ws = torch.zeros(need.value, dtype=torch.uint8, device=dev)
+    _check(lib.epq_chain_prepare(arr, len(steps), ws.data_ptr(), ws.numel(), _stream_ptr(dev)),
+           "epq_chain_prepare")
+    return ws
+
+
+def chain_run(ws, x, out):
+    lib = load_library()
+    _check(lib.epq_chain_run(ws.data_ptr(), x.data_ptr(), dtype_code(x.dtype), out.data_ptr(),
+                             dtype_code(out.dtype), _stream_ptr(x.device)), "epq_chain_run")
+    return out
 
 
 def device_error():

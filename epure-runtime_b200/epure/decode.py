@@ -77,3 +77,56 @@ class GraphedLinearStack:
             out_host = torch.empty(self.out.shape, dtype=self.out.dtype, pin_memory=True)
         out_host.copy_(self.out, non_blocking=True)
         return out_host
+
+
+class ChainedLinearStack:
+    """The same token chain as GraphedLinearStack, as ONE persistent launch.
+
+    ``epq_chain_run`` walks all launches of the token inside one cooperative
+    kernel: weights stream continuously through each SM's TMA ring, layers
+    synchronise through grid barriers, and intermediate outputs stay as fp32
+    partial sums (they are never rounded to the activation dtype).  The stack's
+    stores must use the "tiled" GPU layout.  The launch is captured in a CUDA
+    graph; ``__call__`` copies the token in, replays and copies the result out.
+    """
+
+    def __init__(self, stack, dtype=torch.bfloat16, device=None):
+        self.stack = stack
+        self.device = torch.device(device or stack.device)
+        steps = stack.chain_steps()
+        self.ws = _native.chain_prepare(steps)
+        k0 = steps[0][0][0].in_features
+        last, feed = steps[-1]
+        self.x = torch.zeros((1, k0), dtype=dtype, device=self.device)
+        self.out = torch.zeros((1, last[feed].out_features), dtype=dtype, device=self.device)
+        self.graph = None
+        self.stream = torch.cuda.Stream(device=self.device)
+        self.launches_per_step = 1
+
+    def step_eager(self):
+        _native.chain_run(self.ws, self.x, self.out)
+        return self.out
+
+    def capture(self):
+        with torch.cuda.stream(self.stream):
+            self.step_eager()
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=self.stream):
+            self.step_eager()
+        self.graph = g
+        return self
+
+    def replay(self):
+        self.graph.replay()
+        return self.out
+
+    def __call__(self, x_host, out_host=None):
+        if self.graph is None:
+            self.capture()
+        self.x.copy_(x_host, non_blocking=True)
+        self.graph.replay()
+        if out_host is None:
+            out_host = torch.empty(self.out.shape, dtype=self.out.dtype, pin_memory=True)
+        out_host.copy_(self.out, non_blocking=True)
+        return out_host

@@ -84,10 +84,14 @@ class PackedWeight(nn.Module):
     # up to 16) or "tiled" (the batch-1 LUT kernel).
     GPU_LAYOUT = os.environ.get("EPURE_GPU_LAYOUT", "mma16")
 
-    def __init__(self, shape, packed, scale, cb, group, levels, vec=1):
+    def __init__(self, shape, packed, scale, cb, group, levels, vec=1, gpu_layout=None):
         super().__init__()
         if vec not in (1, 4):
             raise ValueError("vec must be 1 or 4")
+        if gpu_layout is not None:
+            if gpu_layout not in ("mma16", "tiled"):
+                raise ValueError("gpu_layout must be 'mma16' or 'tiled'")
+            self.GPU_LAYOUT = gpu_layout
         self.levels, self.group, self.vec = levels, group, vec
         self.shape = tuple(shape)
         self.in_features = self.shape[-1]

@@ -15,7 +15,7 @@ from .runtime import PackedWeight
 
 
 def make_store(n, k, *, vec=4, levels=256, group=128, device="cuda", seed=0,
-               cb_dtype=torch.float16, scale_dtype=torch.float16):
+               cb_dtype=torch.float16, scale_dtype=torch.float16, gpu_layout=None):
     """A random PackedWeight [n, k] with the benchmark's value distributions."""
     gen = torch.Generator(device=device).manual_seed(int(seed))
     ng = -(-k // group)
@@ -29,7 +29,8 @@ def make_store(n, k, *, vec=4, levels=256, group=128, device="cuda", seed=0,
             hi = (idx[:, 1::2] & 0x0F) if k % 2 == 0 else None
             idx = (lo | (hi << 4)) if hi is not None else lo
     scale = (torch.randn(n, ng, generator=gen, device=device) * 0.02).abs().to(scale_dtype)
-    return PackedWeight((n, k), idx.reshape(-1), scale, cb, group, levels, vec=vec)
+    return PackedWeight((n, k), idx.reshape(-1), scale, cb, group, levels, vec=vec,
+                        gpu_layout=gpu_layout)
 
 
 def store_bytes(st):
@@ -96,6 +97,17 @@ class LinearStack:
                 blk[name] = make_store(n, k, device=device, seed=s, **store_kw)
                 s += 1
             self.blocks.append(blk)
+
+    def chain_steps(self):
+        """(stores, feed) per launch: the store that feeds the next launch.
+
+        q feeds o, up feeds down, down feeds the next layer's q/k/v.
+        """
+        steps = []
+        for b in self.blocks:
+            steps += [([b["q_proj"], b["k_proj"], b["v_proj"]], 0), ([b["o_proj"]], 0),
+                      ([b["gate_proj"], b["up_proj"]], 1), ([b["down_proj"]], 0)]
+        return steps
 
     def groups(self):
         """The launches of one step: lists of stores that share an input."""

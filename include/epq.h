@@ -197,6 +197,37 @@ int epq_linear_bwd(const epq_store* store, const void* x, int64_t ldx, const voi
                    int64_t ldy, int32_t act_dtype, int64_t m, void* dx, int64_t lddx,
                    int32_t dx_dtype, float* dscale, float* dcb, void* stream);
 
+/* A chain of batch-1 linears run as ONE persistent kernel: step j multiplies
+ * its input vector by each of its stores; the output of store `feed` of step j
+ * is the input of step j + 1; the output of store `feed` of the last step is
+ * written to `out`.  Replaces a sequence of PackedLinear.forward calls
+ * (epure/runtime.py:98-126, each the Triton kernel of kernels/_triton.py:56-107)
+ * such as one decode token through a decoder's packed linears.
+ * Stores must be EPQ_LAYOUT_TILED vector stores (vec 4, 8-bit, group 128) with
+ * group-major f16/f32 scales whose row stride is padded to a multiple of 16
+ * (scale_stride_n = 1, scale_stride_g % 16 == 0, >= 16 * ceil(n / 16)) and
+ * 16-byte aligned buffers; the stores of a step share k; the feed output width
+ * equals the next step's k.  Intermediate outputs are not written. */
+typedef struct epq_chain_step {
+    epq_store stores[4];
+    int32_t count;    /* 1..4 stores sharing the step's input                      */
+    int32_t feed;     /* index of the store whose output feeds the next step / out */
+} epq_chain_step;
+
+/* Workspace bytes for a chain (descriptors, counters, two partial-sum buffers). */
+int epq_chain_workspace_bytes(const epq_chain_step* steps, int32_t n_steps, int64_t* bytes);
+
+/* Writes the chain's descriptors into the workspace (256-byte aligned) and zeroes
+ * its counters.  Synchronous; call once per chain, on the device it will run on. */
+int epq_chain_prepare(const epq_chain_step* steps, int32_t n_steps, void* workspace,
+                      int64_t workspace_bytes, void* stream);
+
+/* Runs a prepared chain on x (k0 values) into out.  One cooperative launch;
+ * capturable in a CUDA graph.  Runs on one workspace must be ordered (same
+ * stream); each run leaves the workspace ready for the next. */
+int epq_chain_run(const void* workspace, const void* x, int32_t x_dtype, void* out,
+                  int32_t out_dtype, void* stream);
+
 /* Dense W [n, k] (row stride ldw) in out_dtype with PackedWeight.materialize's
  * rounding: cb and scale are first rounded to out_dtype, their product is
  * rounded to out_dtype (runtime.py:85-88). */
