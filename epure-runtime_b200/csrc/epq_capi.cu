@@ -95,16 +95,18 @@ const char* epq_last_error(void) { return g_err; }
 
 int epq_device_error(int* flag) {
     if (!flag) return set_error(EPQ_EINVAL, "epq_device_error: flag is NULL");
-    int lut = 0, mma = 0, chain = 0;
+    int lut = 0, mma = 0, chain = 0, tc = 0;
     int rc = lut_read_device_error(&lut);
     if (rc) return rc;
     rc = mma_read_device_error(&mma);
     if (rc) return rc;
+    rc = tc_read_device_error(&tc);
+    if (rc) return rc;
     rc = chain_read_device_error(&chain);
     if (rc) return rc;
-    // bit 0: LUT placement check; bit 1: a bounded wait gave up (GEMV or chain);
+    // bit 0: LUT placement check; bit 1: a bounded wait gave up (GEMV, GEMM or chain);
     // bit 2: the chain kernel's placement or grid check failed
-    *flag = (lut ? 1 : 0) | ((mma || chain == 1) ? 2 : 0) | (chain == 2 ? 4 : 0);
+    *flag = (lut ? 1 : 0) | ((mma || tc || chain == 1) ? 2 : 0) | (chain == 2 ? 4 : 0);
     return EPQ_OK;
 }
 
@@ -174,6 +176,10 @@ int epq_linear_multi(const epq_store* stores, int32_t count, const void* x, int3
     bool all_mma = true;
     for (int i = 0; i < count; ++i) all_mma = all_mma && mma_eligible(s[i], m, x_dtype);
     if (all_mma) return launch_linear_mma(s, count, x, x_dtype, m, ldx, outs, ldo, out_dtype, st);
+    bool all_tc = (reinterpret_cast<uintptr_t>(x) & 15) == 0 && ldx % 8 == 0;
+    for (int i = 0; i < count; ++i)
+        all_tc = all_tc && tc_eligible(s[i], m, x_dtype) && s[i].layout == s[0].layout;
+    if (all_tc) return launch_linear_tc(s, count, x, x_dtype, m, ldx, outs, ldo, out_dtype, st);
     if (all_lut) {
         if (reinterpret_cast<uintptr_t>(x) % dtype_size(x_dtype))
             return set_error(EPQ_EALIGN, "linear: x misaligned");

@@ -121,6 +121,12 @@ bool mma_eligible(const StoreD& s, int64_t m, int x_dtype);
 int launch_linear_mma(const StoreD* s, int count, const void* x, int x_dtype, int64_t m, int64_t ldx,
                       void* const* outs, const int64_t* ldo, int out_dtype, cudaStream_t st);
 
+// Tensor-core dequant-GEMM for M > 16 over EPQ_LAYOUT_MMA16 / EPQ_LAYOUT_TILED stores (k_gemm_tc.cu).
+bool tc_eligible(const StoreD& s, int64_t m, int x_dtype);
+int launch_linear_tc(const StoreD* s, int count, const void* x, int x_dtype, int64_t m, int64_t ldx,
+                     void* const* outs, const int64_t* ldo, int out_dtype, cudaStream_t st);
+int tc_read_device_error(int* flag);
+
 // Batch-1 LUT kernel over up to 4 stores sharing x.
 constexpr int kLutMaxStores = 4;
 bool lut_eligible(const StoreD& s);

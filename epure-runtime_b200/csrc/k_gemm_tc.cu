@@ -1,0 +1,503 @@
+// Batched / prefill (M > 16) dequant-GEMM on the 5th-generation tensor cores:
+// out[m, r] = sum_c x[m, c] W[r, c],  W[r, 4j+p] = cb[idx[r, j], p] * scale[r, g(j)].
+//
+// Reference op: epure/kernels/_triton.py:56-107 (_dequant_matmul: per K-tile the
+// weight tile is gathered from the codebook, scaled, and fed to tl.dot) and the
+// bf16 fallback of PackedLinear.forward, F.linear(x, materialize(bf16))
+// (epure/runtime.py:78-89, 123-124).
+//
+// Design (B200, sm_100a):
+// * One CTA computes a 128 (weight rows) x BN (activation rows) tile of out^T
+//   with tcgen05.mma (cta_group::1, kind::f16): A = the dequantised weight tile
+//   (M = 128), B = the activation tile (N = BN), D = fp32 in TMEM (BN columns).
+// * Pipeline stages of 64 k (one 128-byte swizzle atom of 16-bit values):
+//   - warp 0 (one thread) loads the activation tile with a 2-D TMA copy
+//     (128-byte swizzle, rows past M zero-filled, no multicast);
+//   - warps 2-5 decode the weight tile: a 16-byte index load gives 16 codebook
+//     indices; each index gathers one 8-byte codebook entry (already converted
+//     to the activation type) from a 16-way replicated codebook in shared
+//     memory (lane l reads copy l % 16: no bank conflicts), multiplies it by
+//     the row's group scale in the activation type -- exactly the reference's
+//     cb.to(dtype)[idx] * scale.to(dtype) -- and stores it into the swizzled
+//     K-major A tile.  Lanes are assigned so that every half-warp store covers
+//     16 distinct 8-byte bank pairs;
+//   - warp 1 (one thread) issues 4 MMAs (k = 16 each) per stage and commits
+//     them to the stage's "empty" barrier, which frees both tiles.
+// * After the k loop warps 2-5 read the accumulator with tcgen05.ld (warp w
+//   owns TMEM lanes 32 (w % 4) .. +31 = 32 weight rows) and write the output in
+//   the requested dtype: per activation row, 32 consecutive outputs per warp.
+// * Index layouts: EPQ_LAYOUT_MMA16 (per (16-row block, group) 512-byte tiles,
+//   lane t = 4 (r % 8) + q holds rows r, r + 8 at positions q + 4 s) and
+//   EPQ_LAYOUT_TILED (per (group, 16-row block) 32 positions x 16 rows).  The
+//   index/scale loads go through registers, prefetched one group ahead.
+// * Every mbarrier wait is bounded; a wait that gives up sets a device error
+//   flag and a CTA-wide abort word, the kernel runs to its end, and TMEM is
+//   released only after the last commit has landed.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <climits>
+#include <mutex>
+
+#include "epq_common.cuh"
+#include "epq_sm100.cuh"
+
+namespace epq {
+namespace {
+
+using namespace sm100;
+
+constexpr int kRows = 128;                 // weight rows per tile (UMMA M)
+constexpr int kKStage = 64;                // k per pipeline stage
+constexpr int kDecWarps = 4;               // decode + epilogue warps
+constexpr int kThreads = 64 + kDecWarps * 32;
+constexpr int kReplicaBytes = 256 * 16 * 8;
+constexpr int kWStage = kRows * kKStage * 2;
+constexpr int kSmemLimit = 232448;         // 227 KB per CTA
+constexpr uint32_t kWaitLimit = 1u << 22;
+
+__device__ int g_tc_wait_timeout = 0;
+
+template <int BN>
+struct Cfg {
+    static constexpr int kXStage = BN * kKStage * 2;
+    static constexpr int kStageBytes = kXStage + kWStage;
+    static constexpr int kStagesRaw = (kSmemLimit - 1024 - 256 - kReplicaBytes) / kStageBytes;
+    static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
+    static constexpr int kXOff = kReplicaBytes;
+    static constexpr int kWOff = kXOff + kStages * kXStage;
+    static constexpr int kBarOff = kWOff + kStages * kWStage;
+    static constexpr int kSmem = 1024 + kBarOff + 256;
+    static_assert(kStages >= 2, "stages");
+    static_assert(kSmem <= kSmemLimit, "shared memory");
+};
+
+struct TcStore {
+    const uint8_t* idx;
+    const void* scale;    // group-major: scale(r, g) at g * s_g + r
+    int64_t s_g;
+    const void* cb;
+    void* out;
+    int64_t ldo;
+    int cb_dtype, scale_dtype, levels;
+    int n, ng, rb;        // rows, groups, 16-row blocks
+    int tile0;            // first global row tile of this store
+};
+
+struct TcParams {
+    TcStore st[kLutMaxStores];
+    int count, m, k, out_dtype;
+};
+
+template <bool kBf16>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+    if constexpr (kBf16) {
+        __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&v);
+    } else {
+        __half2 v = __floats2half2_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&v);
+    }
+}
+template <bool kBf16>
+__device__ __forceinline__ uint32_t mul2(uint32_t a, uint32_t b) {
+    if constexpr (kBf16) {
+        __nv_bfloat162 r = __hmul2(*reinterpret_cast<__nv_bfloat162*>(&a),
+                                   *reinterpret_cast<__nv_bfloat162*>(&b));
+        return *reinterpret_cast<uint32_t*>(&r);
+    } else {
+        __half2 r = __hmul2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
+        return *reinterpret_cast<uint32_t*>(&r);
+    }
+}
+// Scale (r, g) in the activation type, duplicated into both halves.
+template <bool kBf16>
+__device__ __forceinline__ uint32_t scale_pair(const TcStore& S, int64_t r, int64_t g) {
+    const float s = load_f(S.scale, S.scale_dtype, g * S.s_g + r);
+    return pack2<kBf16>(s, s);
+}
+
+// One codebook index (byte `byte` of `word`) -> 4 scaled weights at shared address dst.
+template <bool kBf16>
+__device__ __forceinline__ void put(uint32_t rep_lane, uint32_t word, int byte, uint32_t sc,
+                                    uint32_t dst) {
+    const uint32_t e = (word >> (8 * byte)) & 0xFFu;
+    uint2 v = lds64(rep_lane + e * 128u);
+    v.x = mul2<kBf16>(v.x, sc);
+    v.y = mul2<kBf16>(v.y, sc);
+    sts64(dst, v);
+}
+
+template <bool kBf16, int kLayout, int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ TcParams P) {
+    using C = Cfg<BN>;
+    constexpr int S_ = C::kStages;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t sbase = (raw + 1023u) & ~1023u;
+    uint8_t* sgen = smem_raw + (sbase - raw);
+    const uint32_t xst0 = sbase + C::kXOff;
+    const uint32_t wst0 = sbase + C::kWOff;
+    const uint32_t bar0 = sbase + C::kBarOff;
+    auto full_x = [&](int s) { return bar0 + 8u * s; };
+    auto full_w = [&](int s) { return bar0 + 64u + 8u * s; };
+    auto empty = [&](int s) { return bar0 + 128u + 8u * s; };
+    const uint32_t accum = bar0 + 192u;
+    const uint32_t tslot = bar0 + 200u;
+    volatile int* abortp = reinterpret_cast<volatile int*>(sgen + C::kBarOff + 204);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tile = blockIdx.x;
+    int si = 0;
+    while (si + 1 < P.count && tile >= P.st[si + 1].tile0) ++si;
+    const TcStore& S = P.st[si];
+    const int rt = tile - S.tile0;       // 128-row tile within the store
+    const int m0 = blockIdx.y * BN;
+    const int nkb = P.k / kKStage;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S_; ++s) {
+            mbar_init(full_x(s), 1);
+            mbar_init(full_w(s), kDecWarps * 32);
+            mbar_init(empty(s), 1);
+        }
+        mbar_init(accum, 1);
+        *abortp = 0;
+        mbar_init_fence();
+    }
+    if (warp == 1) tmem_alloc(tslot, BN);
+    // Codebook -> 16 interleaved copies in the activation type.
+    for (int e = threadIdx.x; e < 256; e += kThreads) {
+        uint2 v = make_uint2(0u, 0u);
+        if (e < S.levels) {
+            const int64_t b = (int64_t)e * 4;
+            v.x = pack2<kBf16>(load_f(S.cb, S.cb_dtype, b), load_f(S.cb, S.cb_dtype, b + 1));
+            v.y = pack2<kBf16>(load_f(S.cb, S.cb_dtype, b + 2), load_f(S.cb, S.cb_dtype, b + 3));
+        }
+        uint2* dst = reinterpret_cast<uint2*>(sgen) + e * 16;
+#pragma unroll
+        for (int c = 0; c < 16; ++c) dst[c] = v;
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sgen + C::kBarOff + 200);
+
+    if (warp == 0) {
+        // ---------------- activation tiles (TMA) ----------------
+        if (lane == 0) {
+            tma_prefetch_desc(&xmap);
+            int issued = 0;
+            for (int kb = 0; kb < nkb; ++kb) {
+                const int s = kb % S_;
+                const uint32_t par = ((kb / S_) & 1) ^ 1;
+                if (!mbar_wait_bounded(empty(s), par, abortp, &g_tc_wait_timeout, kWaitLimit)) break;
+                mbar_expect_tx(full_x(s), C::kXStage);
+                tma_load_2d(xst0 + s * C::kXStage, &xmap, full_x(s), kb * kKStage, m0);
+                ++issued;
+            }
+            // Every copy issued must land before the CTA can exit.
+            const int first = issued > S_ ? issued - S_ : 0;
+            for (int kb = first; kb < issued; ++kb) {
+                const int s = kb % S_;
+                for (uint32_t i = 0; i < kWaitLimit; ++i)
+                    if (mbar_try_wait(full_x(s), (kb / S_) & 1)) break;
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issue (one thread) ----------------
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_f16<kBf16, kRows, BN>();
+            for (int kb = 0; kb < nkb; ++kb) {
+                const int s = kb % S_;
+                const uint32_t par = (kb / S_) & 1;
+                if (!mbar_wait_bounded(full_x(s), par, abortp, &g_tc_wait_timeout, kWaitLimit)) break;
+                if (!mbar_wait_bounded(full_w(s), par, abortp, &g_tc_wait_timeout, kWaitLimit)) break;
+                tc_fence_after();
+                const uint64_t ad = desc_kmajor_sw128(wst0 + s * kWStage);
+                const uint64_t bd = desc_kmajor_sw128(xst0 + s * C::kXStage);
+#pragma unroll
+                for (int kk = 0; kk < kKStage / 16; ++kk)
+                    mma_f16_ss(tmem, ad + 2 * kk, bd + 2 * kk, idesc, (kb | kk) != 0);
+                mma_commit(empty(s));
+            }
+            mma_commit(accum);
+            // The accumulator (and every MMA) is complete before TMEM can be released.
+            for (uint32_t i = 0; i < kWaitLimit; ++i)
+                if (mbar_try_wait(accum, 0)) break;
+        }
+        __syncwarp();
+    } else {
+        // ---------------- decode (weight tiles) + epilogue ----------------
+        const int dw = warp - 2;
+        const uint32_t rep_lane = sbase + (lane & 15) * 8;
+        int kb = 0;
+        if constexpr (kLayout == EPQ_LAYOUT_MMA16) {
+            // Lane -> (r0, q): half-warp hw takes q in {2hw, 2hw+1}, so the 16 stores of a
+            // half-warp hit 16 distinct bank pairs of the swizzled rows.
+            const int hw = lane >> 4, i16 = lane & 15, r0 = i16 >> 1, h = i16 & 1;
+            const int t = 4 * r0 + 2 * hw + h;
+            uint32_t xo[4];
+#pragma unroll
+            for (int s4 = 0; s4 < 4; ++s4)
+                xo[s4] = (uint32_t)(r0 * 128 + h * 8 + ((((2 * s4 + hw) ^ r0)) << 4));
+            int rb[2];
+            bool ok[2];
+            const uint8_t* ip[2];
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                rb[j] = rt * 8 + 2 * dw + j;
+                ok[j] = rb[j] < S.rb;
+                ip[j] = S.idx + ((int64_t)rb[j] * S.ng) * 512 + t * 16;
+            }
+            uint4 cw[2], nw[2];
+            uint32_t cs[2][2], ns[2][2];
+            auto fetch = [&](int g, uint4 (&w)[2], uint32_t (&sc)[2][2]) {
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    if (ok[j]) {
+                        w[j] = ldg_nc_v4(ip[j] + (int64_t)g * 512);
+                        sc[j][0] = scale_pair<kBf16>(S, (int64_t)rb[j] * 16 + r0, g);
+                        sc[j][1] = scale_pair<kBf16>(S, (int64_t)rb[j] * 16 + r0 + 8, g);
+                    }
+                }
+            };
+            fetch(0, nw, ns);
+            for (int g = 0; g < S.ng; ++g) {
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    cw[j] = nw[j];
+                    cs[j][0] = ns[j][0];
+                    cs[j][1] = ns[j][1];
+                }
+                if (g + 1 < S.ng) fetch(g + 1, nw, ns);
+#pragma unroll
+                for (int half = 0; half < 2; ++half, ++kb) {
+                    const int s = kb % S_;
+                    if (!mbar_wait_bounded(empty(s), ((kb / S_) & 1) ^ 1, abortp, &g_tc_wait_timeout,
+                                           kWaitLimit))
+                        break;
+                    const uint32_t wst = wst0 + s * kWStage;
+#pragma unroll
+                    for (int j = 0; j < 2; ++j) {
+                        if (!ok[j]) continue;
+                        const uint32_t w_lo = half ? cw[j].y : cw[j].x;   // rows r0
+                        const uint32_t w_hi = half ? cw[j].w : cw[j].z;   // rows r0 + 8
+                        const uint32_t d0 = wst + (2 * dw + j) * 2048;
+#pragma unroll
+                        for (int s4 = 0; s4 < 4; ++s4) {
+                            put<kBf16>(rep_lane, w_lo, s4, cs[j][0], d0 + xo[s4]);
+                            put<kBf16>(rep_lane, w_hi, s4, cs[j][1], d0 + 1024 + xo[s4]);
+                        }
+                    }
+                    fence_async_smem();
+                    mbar_arrive(full_w(s));
+                }
+                if (*abortp) break;
+            }
+        } else {
+            // EPQ_LAYOUT_TILED: half-warp j takes row block 2 dw + j; lane i16 takes
+            // position 16 half + i16 (chunk i16 / 2, half-chunk i16 % 2) of all 16 rows.
+            const int j = lane >> 4, i16 = lane & 15, c = i16 >> 1, h = i16 & 1;
+            uint32_t yo[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) yo[q] = (uint32_t)(((c ^ q) << 4) + h * 8);
+            const int rbj = rt * 8 + 2 * dw + j;
+            const bool okj = rbj < S.rb;
+            const uint8_t* ipj = S.idx + ((int64_t)rbj * 32 + i16) * 16;
+            const int64_t gstride = (int64_t)S.rb * 512;
+            uint4 cw[2], nw[2];
+            uint32_t cs[16], ns[16];
+            auto fetch = [&](int g, uint4 (&w)[2], uint32_t (&sc)[16]) {
+                if (okj) {
+                    w[0] = ldg_nc_v4(ipj + g * gstride);
+                    w[1] = ldg_nc_v4(ipj + g * gstride + 256);
+#pragma unroll
+                    for (int rr = 0; rr < 16; ++rr)
+                        sc[rr] = scale_pair<kBf16>(S, (int64_t)rbj * 16 + rr, g);
+                }
+            };
+            fetch(0, nw, ns);
+            for (int g = 0; g < S.ng; ++g) {
+                cw[0] = nw[0];
+                cw[1] = nw[1];
+#pragma unroll
+                for (int rr = 0; rr < 16; ++rr) cs[rr] = ns[rr];
+                if (g + 1 < S.ng) fetch(g + 1, nw, ns);
+#pragma unroll
+                for (int half = 0; half < 2; ++half, ++kb) {
+                    const int s = kb % S_;
+                    if (!mbar_wait_bounded(empty(s), ((kb / S_) & 1) ^ 1, abortp, &g_tc_wait_timeout,
+                                           kWaitLimit))
+                        break;
+                    if (okj) {
+                        const uint4 v = cw[half];
+                        const uint32_t d0 = wst0 + s * kWStage + (2 * dw + j) * 2048;
+                        const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                        for (int rr = 0; rr < 16; ++rr)
+                            put<kBf16>(rep_lane, wd[rr >> 2], rr & 3, cs[rr],
+                                       d0 + rr * 128 + yo[rr & 7]);
+                    }
+                    fence_async_smem();
+                    mbar_arrive(full_w(s));
+                }
+                if (*abortp) break;
+            }
+        }
+
+        // ---------------- epilogue: TMEM -> out ----------------
+        const bool got = mbar_wait_bounded(accum, 0, abortp, &g_tc_wait_timeout, kWaitLimit);
+        tc_fence_after();
+        const int sub = warp & 3;
+        const int64_t r = (int64_t)rt * kRows + sub * 32 + lane;     // weight row = output column
+        const bool rv = got && r < S.n;
+#pragma unroll 1
+        for (int cc = 0; cc < BN / 32; ++cc) {
+            if (m0 + cc * 32 >= P.m) break;
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(tmem + ((uint32_t)(sub * 32) << 16) + cc * 32, v);
+            if (rv) {
+#pragma unroll
+                for (int q = 0; q < 32; ++q) {
+                    const int mm = m0 + cc * 32 + q;
+                    if (mm < P.m) store_f(S.out, P.out_dtype, (int64_t)mm * S.ldo + r, __uint_as_float(v[q]));
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, BN);
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+bool g_attr[3][2][2][64];
+
+template <bool kBf16, int kLayout, int BN>
+int launch_tc(const CUtensorMap& xmap, const TcParams& P, int tiles, int bi, cudaStream_t st,
+              int dev) {
+    using C = Cfg<BN>;
+    auto kern = gemm_tc_kernel<kBf16, kLayout, BN>;
+    bool& done = g_attr[bi][kBf16 ? 1 : 0][kLayout == EPQ_LAYOUT_MMA16 ? 1 : 0][dev];
+    if (!done) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) !=
+            cudaSuccess)
+            return check_launch("cudaFuncSetAttribute(gemm_tc_kernel)");
+        done = true;
+    }
+    const dim3 grid(tiles, (unsigned)cdiv(P.m, BN));
+    kern<<<grid, kThreads, C::kSmem, st>>>(xmap, P);
+    return check_launch("gemm_tc_kernel");
+}
+
+template <bool kBf16, int kLayout>
+int launch_bn(int bn, const CUtensorMap& xmap, const TcParams& P, int tiles, cudaStream_t st,
+              int dev) {
+    if (bn == 256) return launch_tc<kBf16, kLayout, 256>(xmap, P, tiles, 2, st, dev);
+    if (bn == 128) return launch_tc<kBf16, kLayout, 128>(xmap, P, tiles, 1, st, dev);
+    return launch_tc<kBf16, kLayout, 64>(xmap, P, tiles, 0, st, dev);
+}
+
+}  // namespace
+
+int tc_read_device_error(int* flag) {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_tc_wait_timeout, sizeof(int)) != cudaSuccess)
+        return check_launch("epq_device_error");
+    *flag = v;
+    return EPQ_OK;
+}
+
+bool tc_eligible(const StoreD& s, int64_t m, int x_dtype) {
+    const int64_t esz = s.scale_dtype == EPQ_F32 ? 4 : 2;
+    return (s.layout == EPQ_LAYOUT_MMA16 || s.layout == EPQ_LAYOUT_TILED) && s.bits == 8 &&
+           s.vec == 4 && s.group == 128 && s.levels <= 256 && s.p == 32 && m > 16 &&
+           (x_dtype == EPQ_BF16 || x_dtype == EPQ_F16) &&
+           (s.scale_dtype == EPQ_F16 || s.scale_dtype == EPQ_F32) && s.s_n == 1 &&
+           (s.s_g % 16) == 0 && s.s_g >= s.rb * 16 &&
+           (reinterpret_cast<uintptr_t>(s.scale) % esz) == 0 &&
+           (reinterpret_cast<uintptr_t>(s.idx) & 15) == 0 && s.k % 128 == 0 && s.n > 0 &&
+           s.n < (1 << 30) && s.k > 0 && s.k < (1 << 30);
+}
+
+int launch_linear_tc(const StoreD* s, int count, const void* x, int x_dtype, int64_t m, int64_t ldx,
+                     void* const* outs, const int64_t* ldo, int out_dtype, cudaStream_t st) {
+    if ((reinterpret_cast<uintptr_t>(x) & 15) || (ldx % 8))
+        return set_error(EPQ_EALIGN, "linear: x must be 16-byte aligned with ldx a multiple of 8");
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return set_error(EPQ_EUNSUPPORTED, "device ordinal %d", dev);
+    for (int i = 1; i < count; ++i)
+        if (s[i].layout != s[0].layout)
+            return set_error(EPQ_ELAYOUT, "linear: fused stores need one layout");
+    PFN_cuTensorMapEncodeTiled_v12000 enc = encode_fn();
+    if (!enc) return set_error(EPQ_EUNSUPPORTED, "linear: cuTensorMapEncodeTiled unavailable");
+    const int bn = m >= 256 ? 256 : (m > 64 ? 128 : 64);
+    if (cdiv(m, bn) > 65535) return set_error(EPQ_EUNSUPPORTED, "linear: m too large");
+
+    TcParams P{};
+    P.count = count;
+    P.m = (int)m;
+    P.k = (int)s[0].k;
+    P.out_dtype = out_dtype;
+    int64_t tiles = 0;
+    for (int i = 0; i < count; ++i) {
+        TcStore& S = P.st[i];
+        S.idx = s[i].idx;
+        S.scale = s[i].scale;
+        S.s_g = s[i].s_g;
+        S.cb = s[i].cb;
+        S.out = outs[i];
+        S.ldo = ldo ? ldo[i] : s[i].n;
+        S.cb_dtype = s[i].cb_dtype;
+        S.scale_dtype = s[i].scale_dtype;
+        S.levels = s[i].levels;
+        S.n = (int)s[i].n;
+        S.ng = (int)s[i].ng;
+        S.rb = (int)s[i].rb;
+        S.tile0 = (int)tiles;
+        tiles += cdiv(s[i].n, kRows);
+    }
+    if (tiles >= (int64_t(1) << 31) - 1) return set_error(EPQ_EUNSUPPORTED, "linear: too many rows");
+
+    CUtensorMap xmap;
+    const cuuint64_t gdim[2] = {(cuuint64_t)P.k, (cuuint64_t)m};
+    const cuuint64_t gstride[1] = {(cuuint64_t)ldx * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)kKStage, (cuuint32_t)bn};
+    const cuuint32_t estride[2] = {1, 1};
+    const CUresult cr = enc(&xmap, x_dtype == EPQ_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                       : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                            2, const_cast<void*>(x), gdim, gstride, box, estride,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (cr != CUDA_SUCCESS) return set_error(EPQ_EINVAL, "linear: activation tensor map (error %d)", (int)cr);
+
+    const bool bf = x_dtype == EPQ_BF16;
+    const bool mma16 = s[0].layout == EPQ_LAYOUT_MMA16;
+    if (bf) {
+        return mma16 ? launch_bn<true, EPQ_LAYOUT_MMA16>(bn, xmap, P, (int)tiles, st, dev)
+                     : launch_bn<true, EPQ_LAYOUT_TILED>(bn, xmap, P, (int)tiles, st, dev);
+    }
+    return mma16 ? launch_bn<false, EPQ_LAYOUT_MMA16>(bn, xmap, P, (int)tiles, st, dev)
+                 : launch_bn<false, EPQ_LAYOUT_TILED>(bn, xmap, P, (int)tiles, st, dev);
+}
+
+}  // namespace epq
