@@ -13,23 +13,28 @@
 // * Pipeline stages of 64 k (one 128-byte swizzle atom of 16-bit values):
 //   - warp 0 (one thread) loads the activation tile with a 2-D TMA copy
 //     (128-byte swizzle, rows past M zero-filled, no multicast);
-//   - warps 2-5 decode the weight tile: a 16-byte index load gives 16 codebook
-//     indices; each index gathers one 8-byte codebook entry (already converted
+//   - warps 2-9 decode the weight tile, one 16-row block each: a 16-byte index
+//     load gives 16 codebook indices; each index gathers one 8-byte codebook
+//     entry (already converted
 //     to the activation type) from a 16-way replicated codebook in shared
 //     memory (lane l reads copy l % 16: no bank conflicts), multiplies it by
 //     the row's group scale in the activation type -- exactly the reference's
 //     cb.to(dtype)[idx] * scale.to(dtype) -- and stores it into the swizzled
 //     K-major A tile.  Lanes are assigned so that every half-warp store covers
-//     16 distinct 8-byte bank pairs;
+//     16 distinct 8-byte bank pairs.  Each warp's shared-memory writes are
+//     fenced to the async proxy before the warp arrives on the stage's "full"
+//     barrier;
 //   - warp 1 (one thread) issues 4 MMAs (k = 16 each) per stage and commits
 //     them to the stage's "empty" barrier, which frees both tiles.
-// * After the k loop warps 2-5 read the accumulator with tcgen05.ld (warp w
-//   owns TMEM lanes 32 (w % 4) .. +31 = 32 weight rows) and write the output in
-//   the requested dtype: per activation row, 32 consecutive outputs per warp.
+// * After the k loop warps 2-9 read the accumulator with tcgen05.ld (warp w
+//   owns TMEM lanes 32 (w % 4) .. +31 = 32 weight rows, and half of the
+//   activation columns) and write the output in the requested dtype: per
+//   activation row, 32 consecutive outputs per warp.
 // * Index layouts: EPQ_LAYOUT_MMA16 (per (16-row block, group) 512-byte tiles,
 //   lane t = 4 (r % 8) + q holds rows r, r + 8 at positions q + 4 s) and
 //   EPQ_LAYOUT_TILED (per (group, 16-row block) 32 positions x 16 rows).  The
-//   index/scale loads go through registers, prefetched one group ahead.
+//   index/scale loads go through registers, prefetched two (tiled) or three
+//   (mma16) groups ahead so that their L2 latency stays off the decode path.
 // * Every mbarrier wait is bounded; a wait that gives up sets a device error
 //   flag and a CTA-wide abort word, the kernel runs to its end, and TMEM is
 //   released only after the last commit has landed.
@@ -49,7 +54,7 @@ using namespace sm100;
 
 constexpr int kRows = 128;                 // weight rows per tile (UMMA M)
 constexpr int kKStage = 64;                // k per pipeline stage
-constexpr int kDecWarps = 4;               // decode + epilogue warps
+constexpr int kDecWarps = 8;               // decode + epilogue warps (one 16-row block each)
 constexpr int kThreads = 64 + kDecWarps * 32;
 constexpr int kReplicaBytes = 256 * 16 * 8;
 constexpr int kWStage = kRows * kKStage * 2;
@@ -110,13 +115,6 @@ __device__ __forceinline__ uint32_t mul2(uint32_t a, uint32_t b) {
         return *reinterpret_cast<uint32_t*>(&r);
     }
 }
-// Scale (r, g) in the activation type, duplicated into both halves.
-template <bool kBf16>
-__device__ __forceinline__ uint32_t scale_pair(const TcStore& S, int64_t r, int64_t g) {
-    const float s = load_f(S.scale, S.scale_dtype, g * S.s_g + r);
-    return pack2<kBf16>(s, s);
-}
-
 // One codebook index (byte `byte` of `word`) -> 4 scaled weights at shared address dst.
 template <bool kBf16>
 __device__ __forceinline__ void put(uint32_t rep_lane, uint32_t word, int byte, uint32_t sc,
@@ -126,6 +124,31 @@ __device__ __forceinline__ void put(uint32_t rep_lane, uint32_t word, int byte, 
     v.x = mul2<kBf16>(v.x, sc);
     v.y = mul2<kBf16>(v.y, sc);
     sts64(dst, v);
+}
+
+// Eight consecutive scales (r0 .. r0 + 7, group g) as activation-type pairs; the
+// scale rows are 16-byte aligned (group-major, rows padded to 16).
+template <bool kBf16>
+__device__ __forceinline__ void scale8(const TcStore& S, int64_t r0, int64_t g, uint32_t (&o)[8]) {
+    const char* p = static_cast<const char*>(S.scale);
+    if (S.scale_dtype == EPQ_F32) {
+        const float* f = reinterpret_cast<const float*>(p) + g * S.s_g + r0;
+        const uint4 a = ldg_nc_v4(f), b = ldg_nc_v4(f + 4);
+        const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = pack2<kBf16>(__uint_as_float(w[i]), __uint_as_float(w[i]));
+    } else {
+        const __half* hp = reinterpret_cast<const __half*>(p) + g * S.s_g + r0;
+        const uint4 a = ldg_nc_v4(hp);
+        const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const __half2 h2 = *reinterpret_cast<const __half2*>(&w[i]);
+            const float lo = __low2float(h2), hi = __high2float(h2);
+            o[2 * i] = pack2<kBf16>(lo, lo);
+            o[2 * i + 1] = pack2<kBf16>(hi, hi);
+        }
+    }
 }
 
 template <bool kBf16, int kLayout, int BN>
@@ -159,7 +182,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < S_; ++s) {
             mbar_init(full_x(s), 1);
-            mbar_init(full_w(s), kDecWarps * 32);
+            mbar_init(full_w(s), kDecWarps);
             mbar_init(empty(s), 1);
         }
         mbar_init(accum, 1);
@@ -167,7 +190,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init_fence();
     }
     if (warp == 1) tmem_alloc(tslot, BN);
-    // Codebook -> 16 interleaved copies in the activation type.
+    // Codebook -> 16 interleaved copies in the activation type: entries are converted
+    // once into the first W stage (free until the k loop starts), then fanned out with
+    // consecutive lanes writing consecutive copies.
+    uint2* conv = reinterpret_cast<uint2*>(sgen + C::kWOff);
     for (int e = threadIdx.x; e < 256; e += kThreads) {
         uint2 v = make_uint2(0u, 0u);
         if (e < S.levels) {
@@ -175,10 +201,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             v.x = pack2<kBf16>(load_f(S.cb, S.cb_dtype, b), load_f(S.cb, S.cb_dtype, b + 1));
             v.y = pack2<kBf16>(load_f(S.cb, S.cb_dtype, b + 2), load_f(S.cb, S.cb_dtype, b + 3));
         }
-        uint2* dst = reinterpret_cast<uint2*>(sgen) + e * 16;
-#pragma unroll
-        for (int c = 0; c < 16; ++c) dst[c] = v;
+        conv[e] = v;
     }
+    __syncthreads();
+    for (int slot = threadIdx.x; slot < 256 * 16; slot += kThreads)
+        reinterpret_cast<uint2*>(sgen)[slot] = conv[slot >> 4];
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -229,9 +256,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
     } else {
-        // ---------------- decode (weight tiles) + epilogue ----------------
+        // ---------------- decode: warp dw fills row block dw (16 rows) of each W stage ----------------
         const int dw = warp - 2;
         const uint32_t rep_lane = sbase + (lane & 15) * 8;
+        const int rb = rt * 8 + dw;
+        const bool ok = rb < S.rb;
+        const int ng = S.ng;
         int kb = 0;
         if constexpr (kLayout == EPQ_LAYOUT_MMA16) {
             // Lane -> (r0, q): half-warp hw takes q in {2hw, 2hw+1}, so the 16 stores of a
@@ -241,120 +271,114 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t xo[4];
 #pragma unroll
             for (int s4 = 0; s4 < 4; ++s4)
-                xo[s4] = (uint32_t)(r0 * 128 + h * 8 + ((((2 * s4 + hw) ^ r0)) << 4));
-            int rb[2];
-            bool ok[2];
-            const uint8_t* ip[2];
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                rb[j] = rt * 8 + 2 * dw + j;
-                ok[j] = rb[j] < S.rb;
-                ip[j] = S.idx + ((int64_t)rb[j] * S.ng) * 512 + t * 16;
-            }
-            uint4 cw[2], nw[2];
-            uint32_t cs[2][2], ns[2][2];
-            auto fetch = [&](int g, uint4 (&w)[2], uint32_t (&sc)[2][2]) {
-#pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    if (ok[j]) {
-                        w[j] = ldg_nc_v4(ip[j] + (int64_t)g * 512);
-                        sc[j][0] = scale_pair<kBf16>(S, (int64_t)rb[j] * 16 + r0, g);
-                        sc[j][1] = scale_pair<kBf16>(S, (int64_t)rb[j] * 16 + r0 + 8, g);
-                    }
+                xo[s4] = (uint32_t)(dw * 2048 + r0 * 128 + h * 8 + ((((2 * s4 + hw) ^ r0)) << 4));
+            const uint8_t* ip = S.idx + ((int64_t)rb * ng) * 512 + t * 16;
+            const int64_t row_a = (int64_t)rb * 16 + r0;
+            // Three groups in flight: index words and the rows' two scales.
+            uint4 w0{}, w1{}, w2{};
+            uint32_t a0 = 0, b0 = 0, a1 = 0, b1 = 0, a2 = 0, b2 = 0;
+            auto fetch = [&](int g, uint4& w, uint32_t& sa, uint32_t& sb) {
+                if (ok && g < ng) {
+                    w = ldg_nc_v4(ip + (int64_t)g * 512);
+                    const float fa = load_f(S.scale, S.scale_dtype, (int64_t)g * S.s_g + row_a);
+                    const float fb = load_f(S.scale, S.scale_dtype, (int64_t)g * S.s_g + row_a + 8);
+                    sa = pack2<kBf16>(fa, fa);
+                    sb = pack2<kBf16>(fb, fb);
                 }
             };
-            fetch(0, nw, ns);
-            for (int g = 0; g < S.ng; ++g) {
-#pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    cw[j] = nw[j];
-                    cs[j][0] = ns[j][0];
-                    cs[j][1] = ns[j][1];
-                }
-                if (g + 1 < S.ng) fetch(g + 1, nw, ns);
+            fetch(0, w0, a0, b0);
+            fetch(1, w1, a1, b1);
+            fetch(2, w2, a2, b2);
+            for (int g = 0; g < ng; ++g) {
+                const uint4 cw = w0;
+                const uint32_t ca = a0, cb2 = b0;
+                w0 = w1; a0 = a1; b0 = b1;
+                w1 = w2; a1 = a2; b1 = b2;
+                fetch(g + 3, w2, a2, b2);
 #pragma unroll
                 for (int half = 0; half < 2; ++half, ++kb) {
                     const int s = kb % S_;
                     if (!mbar_wait_bounded(empty(s), ((kb / S_) & 1) ^ 1, abortp, &g_tc_wait_timeout,
                                            kWaitLimit))
                         break;
-                    const uint32_t wst = wst0 + s * kWStage;
-#pragma unroll
-                    for (int j = 0; j < 2; ++j) {
-                        if (!ok[j]) continue;
-                        const uint32_t w_lo = half ? cw[j].y : cw[j].x;   // rows r0
-                        const uint32_t w_hi = half ? cw[j].w : cw[j].z;   // rows r0 + 8
-                        const uint32_t d0 = wst + (2 * dw + j) * 2048;
+                    if (ok) {
+                        const uint32_t w_lo = half ? cw.y : cw.x;   // rows r0
+                        const uint32_t w_hi = half ? cw.w : cw.z;   // rows r0 + 8
+                        const uint32_t d0 = wst0 + s * kWStage;
 #pragma unroll
                         for (int s4 = 0; s4 < 4; ++s4) {
-                            put<kBf16>(rep_lane, w_lo, s4, cs[j][0], d0 + xo[s4]);
-                            put<kBf16>(rep_lane, w_hi, s4, cs[j][1], d0 + 1024 + xo[s4]);
+                            put<kBf16>(rep_lane, w_lo, s4, ca, d0 + xo[s4]);
+                            put<kBf16>(rep_lane, w_hi, s4, cb2, d0 + 1024 + xo[s4]);
                         }
                     }
                     fence_async_smem();
-                    mbar_arrive(full_w(s));
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(full_w(s));
                 }
                 if (*abortp) break;
             }
         } else {
-            // EPQ_LAYOUT_TILED: half-warp j takes row block 2 dw + j; lane i16 takes
-            // position 16 half + i16 (chunk i16 / 2, half-chunk i16 % 2) of all 16 rows.
-            const int j = lane >> 4, i16 = lane & 15, c = i16 >> 1, h = i16 & 1;
+            // EPQ_LAYOUT_TILED: lane takes position 16 half + i16 of rows 8 hr .. 8 hr + 7.
+            const int hr = lane >> 4, i16 = lane & 15, c = i16 >> 1, h = i16 & 1;
             uint32_t yo[8];
 #pragma unroll
-            for (int q = 0; q < 8; ++q) yo[q] = (uint32_t)(((c ^ q) << 4) + h * 8);
-            const int rbj = rt * 8 + 2 * dw + j;
-            const bool okj = rbj < S.rb;
-            const uint8_t* ipj = S.idx + ((int64_t)rbj * 32 + i16) * 16;
+            for (int q = 0; q < 8; ++q)
+                yo[q] = (uint32_t)(dw * 2048 + (8 * hr + q) * 128 + ((c ^ q) << 4) + h * 8);
+            const uint8_t* ip = S.idx + ((int64_t)rb * 32 + i16) * 16;
             const int64_t gstride = (int64_t)S.rb * 512;
-            uint4 cw[2], nw[2];
-            uint32_t cs[16], ns[16];
-            auto fetch = [&](int g, uint4 (&w)[2], uint32_t (&sc)[16]) {
-                if (okj) {
-                    w[0] = ldg_nc_v4(ipj + g * gstride);
-                    w[1] = ldg_nc_v4(ipj + g * gstride + 256);
-#pragma unroll
-                    for (int rr = 0; rr < 16; ++rr)
-                        sc[rr] = scale_pair<kBf16>(S, (int64_t)rbj * 16 + rr, g);
+            const int sh = 8 * (hr & 1);   // byte offset of rows 8 hr.. inside a 16-row column
+            uint4 p0{}, p1{}, q0{}, q1{};
+            uint32_t s0[8] = {}, s1[8] = {};
+            auto fetch = [&](int g, uint4& lo, uint4& hi, uint32_t (&sc)[8]) {
+                if (ok && g < ng) {
+                    lo = ldg_nc_v4(ip + g * gstride);
+                    hi = ldg_nc_v4(ip + g * gstride + 256);
+                    scale8<kBf16>(S, (int64_t)rb * 16 + 8 * hr, g, sc);
                 }
             };
-            fetch(0, nw, ns);
-            for (int g = 0; g < S.ng; ++g) {
-                cw[0] = nw[0];
-                cw[1] = nw[1];
+            fetch(0, p0, p1, s0);
+            fetch(1, q0, q1, s1);
+            for (int g = 0; g < ng; ++g) {
+                const uint4 c0 = p0, c1 = p1;
+                uint32_t cs[8];
 #pragma unroll
-                for (int rr = 0; rr < 16; ++rr) cs[rr] = ns[rr];
-                if (g + 1 < S.ng) fetch(g + 1, nw, ns);
+                for (int i = 0; i < 8; ++i) cs[i] = s0[i];
+                p0 = q0; p1 = q1;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) s0[i] = s1[i];
+                fetch(g + 2, q0, q1, s1);
 #pragma unroll
                 for (int half = 0; half < 2; ++half, ++kb) {
                     const int s = kb % S_;
                     if (!mbar_wait_bounded(empty(s), ((kb / S_) & 1) ^ 1, abortp, &g_tc_wait_timeout,
                                            kWaitLimit))
                         break;
-                    if (okj) {
-                        const uint4 v = cw[half];
-                        const uint32_t d0 = wst0 + s * kWStage + (2 * dw + j) * 2048;
-                        const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
+                    if (ok) {
+                        const uint4 v = half ? c1 : c0;
+                        const uint32_t lo = sh ? v.z : v.x, hi = sh ? v.w : v.y;
+                        const uint32_t d0 = wst0 + s * kWStage;
 #pragma unroll
-                        for (int rr = 0; rr < 16; ++rr)
-                            put<kBf16>(rep_lane, wd[rr >> 2], rr & 3, cs[rr],
-                                       d0 + rr * 128 + yo[rr & 7]);
+                        for (int q = 0; q < 8; ++q)
+                            put<kBf16>(rep_lane, q < 4 ? lo : hi, q & 3, cs[q], d0 + yo[q]);
                     }
                     fence_async_smem();
-                    mbar_arrive(full_w(s));
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(full_w(s));
                 }
                 if (*abortp) break;
             }
         }
 
         // ---------------- epilogue: TMEM -> out ----------------
+        // Warp w reads TMEM lanes 32 (w % 4) .. +31 (32 weight rows); warps 2-5 take the
+        // first half of the activation columns, warps 6-9 the second.
         const bool got = mbar_wait_bounded(accum, 0, abortp, &g_tc_wait_timeout, kWaitLimit);
         tc_fence_after();
-        const int sub = warp & 3;
+        const int sub = warp & 3, colh = dw >> 2;
         const int64_t r = (int64_t)rt * kRows + sub * 32 + lane;     // weight row = output column
         const bool rv = got && r < S.n;
 #pragma unroll 1
-        for (int cc = 0; cc < BN / 32; ++cc) {
+        for (int cc = colh * (BN / 64); cc < (colh + 1) * (BN / 64); ++cc) {
             if (m0 + cc * 32 >= P.m) break;
             uint32_t v[32];
             tmem_ld_32x32b_x32(tmem + ((uint32_t)(sub * 32) << 16) + cc * 32, v);
@@ -374,7 +398,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_dealloc(tmem, BN);
     }
 }
-
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     static std::once_flag once;
@@ -433,7 +456,7 @@ bool tc_eligible(const StoreD& s, int64_t m, int x_dtype) {
            (x_dtype == EPQ_BF16 || x_dtype == EPQ_F16) &&
            (s.scale_dtype == EPQ_F16 || s.scale_dtype == EPQ_F32) && s.s_n == 1 &&
            (s.s_g % 16) == 0 && s.s_g >= s.rb * 16 &&
-           (reinterpret_cast<uintptr_t>(s.scale) % esz) == 0 &&
+           (reinterpret_cast<uintptr_t>(s.scale) % (16 * esz)) == 0 &&
            (reinterpret_cast<uintptr_t>(s.idx) & 15) == 0 && s.k % 128 == 0 && s.n > 0 &&
            s.n < (1 << 30) && s.k > 0 && s.k < (1 << 30);
 }
