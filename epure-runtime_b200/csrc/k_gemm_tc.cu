@@ -9,32 +9,35 @@
 // Design (B200, sm_100a):
 // * One CTA computes a 128 (weight rows) x BN (activation rows) tile of out^T
 //   with tcgen05.mma (cta_group::1, kind::f16): A = the dequantised weight tile
-//   (M = 128), B = the activation tile (N = BN), D = fp32 in TMEM (BN columns).
+//   (M = 128) held in TENSOR MEMORY, B = the activation tile (N = BN) in shared
+//   memory, D = fp32 in TMEM columns 0 .. BN-1.
 // * Pipeline stages of 64 k (one 128-byte swizzle atom of 16-bit values):
 //   - warp 0 (one thread) loads the activation tile with a 2-D TMA copy
-//     (128-byte swizzle, rows past M zero-filled, no multicast);
-//   - warps 2-9 decode the weight tile, one 16-row block each: a 16-byte index
-//     load gives 16 codebook indices; each index gathers one 8-byte codebook
-//     entry (already converted
-//     to the activation type) from a 16-way replicated codebook in shared
-//     memory (lane l reads copy l % 16: no bank conflicts), multiplies it by
-//     the row's group scale in the activation type -- exactly the reference's
-//     cb.to(dtype)[idx] * scale.to(dtype) -- and stores it into the swizzled
-//     K-major A tile.  Lanes are assigned so that every half-warp store covers
-//     16 distinct 8-byte bank pairs.  Each warp's shared-memory writes are
-//     fenced to the async proxy before the warp arrives on the stage's "full"
-//     barrier;
-//   - warp 1 (one thread) issues 4 MMAs (k = 16 each) per stage and commits
-//     them to the stage's "empty" barrier, which frees both tiles.
-// * After the k loop warps 2-9 read the accumulator with tcgen05.ld (warp w
-//   owns TMEM lanes 32 (w % 4) .. +31 = 32 weight rows, and half of the
-//   activation columns) and write the output in the requested dtype: per
-//   activation row, 32 consecutive outputs per warp.
+//     (128-byte swizzle, rows past M zero-filled, no multicast) into a ring of
+//     up to 8 shared-memory stages;
+//   - warps 2-9 decode the weight tile straight into TMEM: thread = one weight
+//     row = one TMEM lane (warp w owns lanes 32 (w % 4) .. +31; two warps share
+//     a lane quarter, each filling half of the stage's 32 columns).  Each index
+//     byte gathers one 8-byte codebook entry (already converted to the
+//     activation type) from a 16-way replicated codebook in shared memory
+//     (lane l reads copy l % 16: no bank conflicts), is multiplied by the row's
+//     group scale in the activation type -- exactly the reference's
+//     cb.to(dtype)[idx] * scale.to(dtype) -- and lands in TMEM with
+//     tcgen05.st.  Weight stages occupy TMEM columns 256 + 32 s;
+//   - warp 1 (one thread) issues 4 MMAs (k = 16 each) per stage, A from TMEM,
+//     and commits them to the stage's "empty" barrier, which frees both the
+//     activation stage and the weight stage.
+//   The dequantised weights never touch shared memory: the shared-memory port
+//   carries only the activation tiles (read by the tensor core) and the
+//   codebook gathers.
+// * After the k loop warps 2-9 read the accumulator with tcgen05.ld (warp w:
+//   32 weight rows, half of the activation columns) and write the output in
+//   the requested dtype: per activation row, 32 consecutive outputs per warp.
 // * Index layouts: EPQ_LAYOUT_MMA16 (per (16-row block, group) 512-byte tiles,
-//   lane t = 4 (r % 8) + q holds rows r, r + 8 at positions q + 4 s) and
-//   EPQ_LAYOUT_TILED (per (group, 16-row block) 32 positions x 16 rows).  The
-//   index/scale loads go through registers, prefetched two (tiled) or three
-//   (mma16) groups ahead so that their L2 latency stays off the decode path.
+//   lane t = 4 (r % 8) + q holds rows r, r + 8 at positions q + 4 s: a row's
+//   group is four 8-byte pieces) and EPQ_LAYOUT_TILED (per (group, 16-row
+//   block) 32 positions x 16 rows: one byte per position).  Index bytes and
+//   scales are loaded per row into registers, two or three groups ahead of use.
 // * Every mbarrier wait is bounded; a wait that gives up sets a device error
 //   flag and a CTA-wide abort word, the kernel runs to its end, and TMEM is
 //   released only after the last commit has landed.
@@ -57,7 +60,11 @@ constexpr int kKStage = 64;                // k per pipeline stage
 constexpr int kDecWarps = 8;               // decode + epilogue warps (one 16-row block each)
 constexpr int kThreads = 64 + kDecWarps * 32;
 constexpr int kReplicaBytes = 256 * 16 * 8;
-constexpr int kWStage = kRows * kKStage * 2;
+constexpr int kMaxStages = 8;
+constexpr int kAStageCols = kKStage / 2;     // TMEM columns of one weight stage (2 x 16 bit each)
+constexpr uint32_t kACol0 = 256;             // weight stages live in TMEM columns 256 ..
+constexpr uint32_t kTmemCols = 512;          // accumulator in 0 .. BN-1
+static_assert(kACol0 + kMaxStages * kAStageCols <= kTmemCols, "TMEM columns");
 constexpr int kSmemLimit = 232448;         // 227 KB per CTA
 constexpr uint32_t kWaitLimit = 1u << 22;
 
@@ -66,15 +73,14 @@ __device__ int g_tc_wait_timeout = 0;
 template <int BN>
 struct Cfg {
     static constexpr int kXStage = BN * kKStage * 2;
-    static constexpr int kStageBytes = kXStage + kWStage;
-    static constexpr int kStagesRaw = (kSmemLimit - 1024 - 256 - kReplicaBytes) / kStageBytes;
-    static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
+    static constexpr int kStagesRaw = (kSmemLimit - 1024 - 256 - kReplicaBytes) / kXStage;
+    static constexpr int kStages = kStagesRaw > kMaxStages ? kMaxStages : kStagesRaw;
     static constexpr int kXOff = kReplicaBytes;
-    static constexpr int kWOff = kXOff + kStages * kXStage;
-    static constexpr int kBarOff = kWOff + kStages * kWStage;
+    static constexpr int kBarOff = kXOff + kStages * kXStage;
     static constexpr int kSmem = 1024 + kBarOff + 256;
     static_assert(kStages >= 2, "stages");
     static_assert(kSmem <= kSmemLimit, "shared memory");
+    static_assert(BN <= (int)kACol0, "accumulator columns");
 };
 
 struct TcStore {
@@ -115,42 +121,6 @@ __device__ __forceinline__ uint32_t mul2(uint32_t a, uint32_t b) {
         return *reinterpret_cast<uint32_t*>(&r);
     }
 }
-// One codebook index (byte `byte` of `word`) -> 4 scaled weights at shared address dst.
-template <bool kBf16>
-__device__ __forceinline__ void put(uint32_t rep_lane, uint32_t word, int byte, uint32_t sc,
-                                    uint32_t dst) {
-    const uint32_t e = (word >> (8 * byte)) & 0xFFu;
-    uint2 v = lds64(rep_lane + e * 128u);
-    v.x = mul2<kBf16>(v.x, sc);
-    v.y = mul2<kBf16>(v.y, sc);
-    sts64(dst, v);
-}
-
-// Eight consecutive scales (r0 .. r0 + 7, group g) as activation-type pairs; the
-// scale rows are 16-byte aligned (group-major, rows padded to 16).
-template <bool kBf16>
-__device__ __forceinline__ void scale8(const TcStore& S, int64_t r0, int64_t g, uint32_t (&o)[8]) {
-    const char* p = static_cast<const char*>(S.scale);
-    if (S.scale_dtype == EPQ_F32) {
-        const float* f = reinterpret_cast<const float*>(p) + g * S.s_g + r0;
-        const uint4 a = ldg_nc_v4(f), b = ldg_nc_v4(f + 4);
-        const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-        for (int i = 0; i < 8; ++i) o[i] = pack2<kBf16>(__uint_as_float(w[i]), __uint_as_float(w[i]));
-    } else {
-        const __half* hp = reinterpret_cast<const __half*>(p) + g * S.s_g + r0;
-        const uint4 a = ldg_nc_v4(hp);
-        const uint32_t w[4] = {a.x, a.y, a.z, a.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const __half2 h2 = *reinterpret_cast<const __half2*>(&w[i]);
-            const float lo = __low2float(h2), hi = __high2float(h2);
-            o[2 * i] = pack2<kBf16>(lo, lo);
-            o[2 * i + 1] = pack2<kBf16>(hi, hi);
-        }
-    }
-}
-
 template <bool kBf16, int kLayout, int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ TcParams P) {
@@ -161,7 +131,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t sbase = (raw + 1023u) & ~1023u;
     uint8_t* sgen = smem_raw + (sbase - raw);
     const uint32_t xst0 = sbase + C::kXOff;
-    const uint32_t wst0 = sbase + C::kWOff;
     const uint32_t bar0 = sbase + C::kBarOff;
     auto full_x = [&](int s) { return bar0 + 8u * s; };
     auto full_w = [&](int s) { return bar0 + 64u + 8u * s; };
@@ -189,11 +158,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         *abortp = 0;
         mbar_init_fence();
     }
-    if (warp == 1) tmem_alloc(tslot, BN);
+    if (warp == 1) tmem_alloc(tslot, kTmemCols);
     // Codebook -> 16 interleaved copies in the activation type: entries are converted
-    // once into the first W stage (free until the k loop starts), then fanned out with
-    // consecutive lanes writing consecutive copies.
-    uint2* conv = reinterpret_cast<uint2*>(sgen + C::kWOff);
+    // once into the first activation stage (free until the k loop starts), then fanned
+    // out with consecutive lanes writing consecutive copies.
+    uint2* conv = reinterpret_cast<uint2*>(sgen + C::kXOff);
     for (int e = threadIdx.x; e < 256; e += kThreads) {
         uint2 v = make_uint2(0u, 0u);
         if (e < S.levels) {
@@ -206,6 +175,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     for (int slot = threadIdx.x; slot < 256 * 16; slot += kThreads)
         reinterpret_cast<uint2*>(sgen)[slot] = conv[slot >> 4];
+    // The activation stages are written by TMA (async proxy) after this point.
+    fence_async_smem();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -233,7 +204,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     } else if (warp == 1) {
-        // ---------------- MMA issue (one thread) ----------------
+        // ---------------- MMA issue (one thread): A from TMEM, B from shared memory ----------------
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_f16<kBf16, kRows, BN>();
             for (int kb = 0; kb < nkb; ++kb) {
@@ -242,11 +213,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!mbar_wait_bounded(full_x(s), par, abortp, &g_tc_wait_timeout, kWaitLimit)) break;
                 if (!mbar_wait_bounded(full_w(s), par, abortp, &g_tc_wait_timeout, kWaitLimit)) break;
                 tc_fence_after();
-                const uint64_t ad = desc_kmajor_sw128(wst0 + s * kWStage);
+                const uint32_t ta = tmem + kACol0 + s * kAStageCols;
                 const uint64_t bd = desc_kmajor_sw128(xst0 + s * C::kXStage);
 #pragma unroll
                 for (int kk = 0; kk < kKStage / 16; ++kk)
-                    mma_f16_ss(tmem, ad + 2 * kk, bd + 2 * kk, idesc, (kb | kk) != 0);
+                    mma_f16_ts(tmem, ta + 8 * kk, bd + 2 * kk, idesc, (kb | kk) != 0);
                 mma_commit(empty(s));
             }
             mma_commit(accum);
@@ -256,116 +227,122 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
     } else {
-        // ---------------- decode: warp dw fills row block dw (16 rows) of each W stage ----------------
-        const int dw = warp - 2;
+        // ---------------- decode: thread = one weight row (TMEM lane) ----------------
+        // Warp w owns TMEM lanes 32 (w % 4) .. +31; warps 2-5 fill the first half of each
+        // stage's 16 index positions, warps 6-9 the second half (layout dependent split).
+        const int sub = warp & 3, c2 = (warp - 2) >> 2;
         const uint32_t rep_lane = sbase + (lane & 15) * 8;
-        const int rb = rt * 8 + dw;
+        const int rb = rt * 8 + 2 * sub + (lane >> 4);      // 16-row block of this row
+        const int r16 = lane & 15;
         const bool ok = rb < S.rb;
+        const int64_t row = (int64_t)rb * 16 + r16;
         const int ng = S.ng;
+        const uint32_t trow = tmem + ((uint32_t)(32 * sub) << 16) + kACol0;
         int kb = 0;
         if constexpr (kLayout == EPQ_LAYOUT_MMA16) {
-            // Lane -> (r0, q): half-warp hw takes q in {2hw, 2hw+1}, so the 16 stores of a
-            // half-warp hit 16 distinct bank pairs of the swizzled rows.
-            const int hw = lane >> 4, i16 = lane & 15, r0 = i16 >> 1, h = i16 & 1;
-            const int t = 4 * r0 + 2 * hw + h;
-            uint32_t xo[4];
-#pragma unroll
-            for (int s4 = 0; s4 < 4; ++s4)
-                xo[s4] = (uint32_t)(dw * 2048 + r0 * 128 + h * 8 + ((((2 * s4 + hw) ^ r0)) << 4));
-            const uint8_t* ip = S.idx + ((int64_t)rb * ng) * 512 + t * 16;
-            const int64_t row_a = (int64_t)rb * 16 + r0;
-            // Three groups in flight: index words and the rows' two scales.
-            uint4 w0{}, w1{}, w2{};
-            uint32_t a0 = 0, b0 = 0, a1 = 0, b1 = 0, a2 = 0, b2 = 0;
-            auto fetch = [&](int g, uint4& w, uint32_t& sa, uint32_t& sb) {
+            // Row r's 32 positions of a group sit in four 8-byte pieces (lanes t = 4 (r%8) + q,
+            // q = 0..3, half (r/8)%2); this warp takes q = 2 c2 and 2 c2 + 1: positions
+            // q + 4 s, i.e. local positions {2 c2, 2 c2 + 1} + 4 s_l of each stage.
+            const uint8_t* ip = S.idx + ((int64_t)rb * ng) * 512 + (4 * (r16 & 7) + 2 * c2) * 16 +
+                                8 * ((r16 >> 3) & 1);
+            uint2 a0{}, b0{}, a1{}, b1{}, a2{}, b2{};
+            uint32_t s0 = 0, s1 = 0, s2 = 0;
+            auto fetch = [&](int g, uint2& a, uint2& b, uint32_t& sc) {
                 if (ok && g < ng) {
-                    w = ldg_nc_v4(ip + (int64_t)g * 512);
-                    const float fa = load_f(S.scale, S.scale_dtype, (int64_t)g * S.s_g + row_a);
-                    const float fb = load_f(S.scale, S.scale_dtype, (int64_t)g * S.s_g + row_a + 8);
-                    sa = pack2<kBf16>(fa, fa);
-                    sb = pack2<kBf16>(fb, fb);
+                    a = ldg_nc_v2(ip + (int64_t)g * 512);
+                    b = ldg_nc_v2(ip + (int64_t)g * 512 + 16);
+                    const float f = load_f(S.scale, S.scale_dtype, (int64_t)g * S.s_g + row);
+                    sc = pack2<kBf16>(f, f);
                 }
             };
-            fetch(0, w0, a0, b0);
-            fetch(1, w1, a1, b1);
-            fetch(2, w2, a2, b2);
+            fetch(0, a0, b0, s0);
+            fetch(1, a1, b1, s1);
+            fetch(2, a2, b2, s2);
             for (int g = 0; g < ng; ++g) {
-                const uint4 cw = w0;
-                const uint32_t ca = a0, cb2 = b0;
-                w0 = w1; a0 = a1; b0 = b1;
-                w1 = w2; a1 = a2; b1 = b2;
-                fetch(g + 3, w2, a2, b2);
+                const uint2 ca = a0, cbb = b0;
+                const uint32_t cs = s0;
+                a0 = a1; b0 = b1; s0 = s1;
+                a1 = a2; b1 = b2; s1 = s2;
+                fetch(g + 3, a2, b2, s2);
 #pragma unroll
                 for (int half = 0; half < 2; ++half, ++kb) {
                     const int s = kb % S_;
-                    if (!mbar_wait_bounded(empty(s), ((kb / S_) & 1) ^ 1, abortp, &g_tc_wait_timeout,
-                                           kWaitLimit))
-                        break;
-                    if (ok) {
-                        const uint32_t w_lo = half ? cw.y : cw.x;   // rows r0
-                        const uint32_t w_hi = half ? cw.w : cw.z;   // rows r0 + 8
-                        const uint32_t d0 = wst0 + s * kWStage;
+                    // tcgen05.st below is warp-collective: the whole warp continues or stops
+                    const bool w_ok = mbar_wait_bounded(empty(s), ((kb / S_) & 1) ^ 1, abortp,
+                                                        &g_tc_wait_timeout, kWaitLimit);
+                    if (!__all_sync(0xffffffffu, w_ok)) break;
+                    tc_fence_after();
+                    const uint32_t wa = half ? ca.y : ca.x, wb = half ? cbb.y : cbb.x;
+                    const uint32_t t0 = trow + s * kAStageCols + 4 * c2;
 #pragma unroll
-                        for (int s4 = 0; s4 < 4; ++s4) {
-                            put<kBf16>(rep_lane, w_lo, s4, ca, d0 + xo[s4]);
-                            put<kBf16>(rep_lane, w_hi, s4, cb2, d0 + 1024 + xo[s4]);
-                        }
+                    for (int sl = 0; sl < 4; ++sl) {
+                        const uint2 va = lds64(rep_lane + ((wa >> (8 * sl)) & 0xFFu) * 128u);
+                        const uint2 vb = lds64(rep_lane + ((wb >> (8 * sl)) & 0xFFu) * 128u);
+                        tmem_st_32x32b_x4(t0 + 8 * sl, mul2<kBf16>(va.x, cs), mul2<kBf16>(va.y, cs),
+                                          mul2<kBf16>(vb.x, cs), mul2<kBf16>(vb.y, cs));
                     }
-                    fence_async_smem();
+                    tmem_st_wait();
+                    tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(full_w(s));
                 }
-                if (*abortp) break;
+                if (__any_sync(0xffffffffu, *abortp != 0)) break;
             }
         } else {
-            // EPQ_LAYOUT_TILED: lane takes position 16 half + i16 of rows 8 hr .. 8 hr + 7.
-            const int hr = lane >> 4, i16 = lane & 15, c = i16 >> 1, h = i16 & 1;
-            uint32_t yo[8];
-#pragma unroll
-            for (int q = 0; q < 8; ++q)
-                yo[q] = (uint32_t)(dw * 2048 + (8 * hr + q) * 128 + ((c ^ q) << 4) + h * 8);
-            const uint8_t* ip = S.idx + ((int64_t)rb * 32 + i16) * 16;
+            // EPQ_LAYOUT_TILED: byte ((g RB + rb) 32 + p) 16 + r16; this warp takes local
+            // positions 8 c2 .. 8 c2 + 7 of each stage (16 contiguous TMEM columns).
+            const uint8_t* ip = S.idx + ((int64_t)rb * 32 + 8 * c2) * 16 + r16;
             const int64_t gstride = (int64_t)S.rb * 512;
-            const int sh = 8 * (hr & 1);   // byte offset of rows 8 hr.. inside a 16-row column
-            uint4 p0{}, p1{}, q0{}, q1{};
-            uint32_t s0[8] = {}, s1[8] = {};
-            auto fetch = [&](int g, uint4& lo, uint4& hi, uint32_t (&sc)[8]) {
+            uint32_t w0[4] = {}, w1[4] = {};
+            uint32_t s0 = 0, s1 = 0;
+            auto fetch = [&](int g, uint32_t (&w)[4], uint32_t& sc) {
                 if (ok && g < ng) {
-                    lo = ldg_nc_v4(ip + g * gstride);
-                    hi = ldg_nc_v4(ip + g * gstride + 256);
-                    scale8<kBf16>(S, (int64_t)rb * 16 + 8 * hr, g, sc);
+                    const uint8_t* p = ip + g * gstride;
+#pragma unroll
+                    for (int hq = 0; hq < 4; ++hq) {   // (half, quad): positions 16 (hq/2) + 4 (hq%2) ..
+                        const int p0 = 16 * (hq >> 1) + 4 * (hq & 1);
+                        const uint32_t e0 = ldg_nc_u8(p + (p0 + 0) * 16), e1 = ldg_nc_u8(p + (p0 + 1) * 16);
+                        const uint32_t e2 = ldg_nc_u8(p + (p0 + 2) * 16), e3 = ldg_nc_u8(p + (p0 + 3) * 16);
+                        w[hq] = e0 | (e1 << 8) | (e2 << 16) | (e3 << 24);
+                    }
+                    const float f = load_f(S.scale, S.scale_dtype, (int64_t)g * S.s_g + row);
+                    sc = pack2<kBf16>(f, f);
                 }
             };
-            fetch(0, p0, p1, s0);
-            fetch(1, q0, q1, s1);
+            fetch(0, w0, s0);
+            fetch(1, w1, s1);
             for (int g = 0; g < ng; ++g) {
-                const uint4 c0 = p0, c1 = p1;
-                uint32_t cs[8];
+                uint32_t cw[4];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) cs[i] = s0[i];
-                p0 = q0; p1 = q1;
+                for (int i = 0; i < 4; ++i) cw[i] = w0[i];
+                const uint32_t cs = s0;
 #pragma unroll
-                for (int i = 0; i < 8; ++i) s0[i] = s1[i];
-                fetch(g + 2, q0, q1, s1);
+                for (int i = 0; i < 4; ++i) w0[i] = w1[i];
+                s0 = s1;
+                fetch(g + 2, w1, s1);
 #pragma unroll
                 for (int half = 0; half < 2; ++half, ++kb) {
                     const int s = kb % S_;
-                    if (!mbar_wait_bounded(empty(s), ((kb / S_) & 1) ^ 1, abortp, &g_tc_wait_timeout,
-                                           kWaitLimit))
-                        break;
-                    if (ok) {
-                        const uint4 v = half ? c1 : c0;
-                        const uint32_t lo = sh ? v.z : v.x, hi = sh ? v.w : v.y;
-                        const uint32_t d0 = wst0 + s * kWStage;
+                    // tcgen05.st below is warp-collective: the whole warp continues or stops
+                    const bool w_ok = mbar_wait_bounded(empty(s), ((kb / S_) & 1) ^ 1, abortp,
+                                                        &g_tc_wait_timeout, kWaitLimit);
+                    if (!__all_sync(0xffffffffu, w_ok)) break;
+                    tc_fence_after();
+                    uint32_t v[16];
 #pragma unroll
-                        for (int q = 0; q < 8; ++q)
-                            put<kBf16>(rep_lane, q < 4 ? lo : hi, q & 3, cs[q], d0 + yo[q]);
+                    for (int j = 0; j < 8; ++j) {
+                        const uint32_t w = cw[2 * half + (j >> 2)];
+                        const uint2 e = lds64(rep_lane + ((w >> (8 * (j & 3))) & 0xFFu) * 128u);
+                        v[2 * j] = mul2<kBf16>(e.x, cs);
+                        v[2 * j + 1] = mul2<kBf16>(e.y, cs);
                     }
-                    fence_async_smem();
+                    tmem_st_32x32b_x16(trow + s * kAStageCols + 16 * c2, v);
+                    tmem_st_wait();
+                    tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(full_w(s));
                 }
-                if (*abortp) break;
+                if (__any_sync(0xffffffffu, *abortp != 0)) break;
             }
         }
 
@@ -374,11 +351,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         // first half of the activation columns, warps 6-9 the second.
         const bool got = mbar_wait_bounded(accum, 0, abortp, &g_tc_wait_timeout, kWaitLimit);
         tc_fence_after();
-        const int sub = warp & 3, colh = dw >> 2;
         const int64_t r = (int64_t)rt * kRows + sub * 32 + lane;     // weight row = output column
         const bool rv = got && r < S.n;
 #pragma unroll 1
-        for (int cc = colh * (BN / 64); cc < (colh + 1) * (BN / 64); ++cc) {
+        for (int cc = c2 * (BN / 64); cc < (c2 + 1) * (BN / 64); ++cc) {
             if (m0 + cc * 32 >= P.m) break;
             uint32_t v[32];
             tmem_ld_32x32b_x32(tmem + ((uint32_t)(sub * 32) << 16) + cc * 32, v);
@@ -395,9 +371,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, BN);
+        tmem_dealloc(tmem, kTmemCols);
     }
 }
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     static std::once_flag once;
