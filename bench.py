@@ -21,6 +21,15 @@ each rank runs an independent replica on its own GPU (weak scaling; the 8B
 model fits one GPU, so there is no collective on the data path); the time is
 the max over ranks.
 
+Other workloads (not the headline; each prints its own metric):
+  --mode prefill [--tokens 2048]: a prompt of `tokens` rows through every packed
+      linear (the tensor-core dequant-GEMM, one launch per fused group), metric
+      prefill tok/s, roofline against the sustained bf16 tensor peak;
+  --model qwen3-1.7b|llama3-8b|llama3-70b picks the decoder shapes;
+  --layers L keeps the first L layers (small cases for profiling);
+  --fallback also times the reference's bf16 fallback path on the GPU
+      (F.linear(x, materialize(bf16)) store by store, torch ops) on the same step.
+
 The reference arm (--impl reference) runs the reference's fused CPU kernel
 (kernel/src/lib.rs, restated in C under oracle/) on the host cores: each step
 is one layer's 7 linears with f32 activations, and tokens/s is scaled by the
@@ -66,6 +75,16 @@ def _peaks():
         return float(p["hbm_gbs"]), "measured"
     except Exception:
         return 6650.0, "fallback"
+
+
+def _tensor_peak():
+    """Sustained bf16 tensor throughput (a kernel timed inside a long step)."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops_sustained"]), "measured (sustained)"
+    except Exception:
+        return 1400.0, "fallback (sustained)"
 
 
 class ClockSampler:
@@ -188,6 +207,46 @@ def run_reference(args, rank, world):
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
+def time_fallback(stack, x, steps):
+    """The reference's GPU path without its Triton kernel, on the same step.
+
+    PackedLinear.forward falls back to F.linear(x, materialize(x.dtype))
+    (epure/runtime.py:78-89, 123-124): the codebook cast to the activation type,
+    gathered by index, multiplied by the row's group scale (repeat_interleave
+    over the group), then one cuBLAS GEMM.  Run with torch ops, store by store,
+    in the step's order; CUDA events around `steps` steps.
+    """
+    import torch
+    import torch.nn.functional as F
+
+    def weight(st):
+        dt = x.dtype
+        idx = st.index_rows().long()                                   # [n, k/4]
+        w = st.cb.to(dt)[idx].reshape(st.out_features, -1)[:, :st.in_features]
+        sc = st.scale.to(dt).repeat_interleave(st.group, dim=1)[:, :st.in_features]
+        return w * sc
+
+    def step():
+        h = x
+        for grp, feed in zip(stack.groups(), [0, 0, 1, 0] * len(stack.blocks)):
+            outs = [F.linear(h, weight(st)) for st in grp]
+            h = outs[feed]
+        return h
+
+    step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    return {"what": "reference bf16 fallback: F.linear(x, materialize(bf16)) per store (torch ops)",
+            "ms_per_step": round(ms, 4), "value": round(x.shape[0] * 1000.0 / ms, 2), "unit": UNIT,
+            "steps": steps}
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
@@ -196,19 +255,25 @@ def run_ours(args, rank, world, local_rank):
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    shapes = synthetic.LLAMA3_8B
+    shapes = synthetic.SHAPES[args.model]
     chain = args.mode == "chain"
-    stack = synthetic.LinearStack(shapes, device=dev, seed=1000 * rank,
+    prefill = args.mode == "prefill"
+    m = args.tokens if prefill else 1
+    stack = synthetic.LinearStack(shapes, layers=args.layers, device=dev, seed=1000 * rank,
                                   gpu_layout="tiled" if chain else "mma16")
     if chain:
         runner = ChainedLinearStack(stack, dtype=torch.bfloat16, device=dev).capture()
         kernel_name = "chain_kernel (one persistent launch per step)"
+    elif prefill:
+        runner = GraphedLinearStack(stack, m=m, dtype=torch.bfloat16, device=dev).capture()
+        kernel_name = "gemm_tc_kernel (all launches of the step)"
     else:
         runner = GraphedLinearStack(stack, m=1, dtype=torch.bfloat16, device=dev).capture()
-        kernel_name = "gemv_mma_kernel (all 128 launches of the step)"
+        kernel_name = "gemv_mma_kernel (all launches of the step)"
     g = torch.Generator(device=dev).manual_seed(rank)
     runner.x.copy_(torch.randn(runner.x.shape, generator=g, device=dev).to(torch.bfloat16))
-    step_bytes = stack.algorithmic_bytes(m=1, act_bytes=2)
+    step_bytes = stack.algorithmic_bytes(m=m, act_bytes=2)
+    step_flops = stack.flops(m=m)
     launches = runner.launches_per_step
 
     def barrier():
@@ -263,10 +328,34 @@ def run_ours(args, rank, world, local_rank):
 
     hbm_peak, peak_kind = _peaks()
     achieved_gbs = step_bytes / (ms * 1e-3) / 1e9
+    workload = WORKLOAD if args.model == "llama3-8b" else WORKLOAD.replace("llama3-8b", args.model)
+    if prefill:
+        workload = workload.replace("batch-1 decode token", f"{m}-token prefill")
+    if stack.layers != shapes.layers:
+        workload += f" (first {stack.layers} of {shapes.layers} layers)"
+    if prefill:
+        tf_peak, tf_kind = _tensor_peak()
+        achieved_tf = step_flops / (ms * 1e-3) / 1e12
+        roofline = {"bound": "tensor", "achieved": round(achieved_tf, 1), "peak": tf_peak,
+                    "unit": "TFLOP/s", "frac": round(achieved_tf / tf_peak, 4),
+                    "peak_kind": tf_kind, "kernel": kernel_name,
+                    "launch_avg_us": round(ms * 1e3 / launches, 3), "traffic": None}
+    else:
+        roofline = {"bound": "hbm", "achieved": round(achieved_gbs, 1),
+                    "peak": hbm_peak, "unit": "GB/s",
+                    "frac": round(achieved_gbs / hbm_peak, 4),
+                    "peak_kind": peak_kind,
+                    "kernel": kernel_name,
+                    "launch_avg_us": round(ms * 1e3 / launches, 3),
+                    "traffic": (int(step_bytes * NCU_TRAFFIC_RATIO[args.mode])
+                                if NCU_TRAFFIC_RATIO.get(args.mode) and stack.layers == 32
+                                and args.model == "llama3-8b" else None),
+                    "traffic_note": TRAFFIC_NOTE.get(args.mode)}
     if rank == 0:
         line = {
-            "metric": METRIC,
-            "value": round(world * 1000.0 / ms, 2),
+            "metric": (f"prefill tok/s @{args.model} ({m}-token prompt, packed linears)"
+                       if prefill else METRIC),
+            "value": round(world * m * 1000.0 / ms, 2),
             "unit": UNIT,
             "n_gpus": world,
             "steps": args.steps,
@@ -277,26 +366,22 @@ def run_ours(args, rank, world, local_rank):
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic",
-            "config": {"workload": WORKLOAD, "mode": args.mode, "global_batch": world, "seq_len": 1,
+            "config": {"workload": workload, "mode": args.mode, "global_batch": world * m,
+                       "seq_len": m,
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                       "l2": "inputs larger than L2 (1.9 GB of packed weights per step)",
-                       "bytes_per_step": step_bytes},
-            "roofline": {"bound": "hbm", "achieved": round(achieved_gbs, 1),
-                         "peak": hbm_peak, "unit": "GB/s",
-                         "frac": round(achieved_gbs / hbm_peak, 4),
-                         "peak_kind": peak_kind,
-                         "kernel": kernel_name,
-                         "launch_avg_us": round(ms * 1e3 / launches, 3),
-                         "traffic": (int(step_bytes * NCU_TRAFFIC_RATIO[args.mode])
-                                     if NCU_TRAFFIC_RATIO.get(args.mode) else None),
-                         "traffic_note": TRAFFIC_NOTE.get(args.mode)},
-            "e2e": {"value": round(world * 1000.0 / e2e_ms, 2), "unit": UNIT,
+                       "l2": (f"inputs larger than L2 ({step_bytes / 1e9:.2f} GB moved per step)"
+                              if step_bytes > 126e6 else "working set may fit in L2"),
+                       "bytes_per_step": step_bytes, "flops_per_step": step_flops},
+            "roofline": roofline,
+            "e2e": {"value": round(world * m * 1000.0 / e2e_ms, 2), "unit": UNIT,
                     "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
                     "d2h_bytes_per_step": out_host.numel() * out_host.element_size()},
             "gpu_launches": launches * args.steps,
             "clocks": clocks.summary(),
         }
-        if world == 1 and not args.no_cpu_baseline:
+        if args.fallback:
+            line["fallback"] = time_fallback(stack, runner.x, steps=max(1, min(args.steps, 3)))
+        if world == 1 and not args.no_cpu_baseline and args.mode != "prefill":
             tok_s, info = cpu_reference_sample(seconds=args.cpu_seconds)
             line["cpu_baseline"] = {"value": round(tok_s, 4), "unit": UNIT, **info}
         print(json.dumps(line), flush=True)
@@ -311,7 +396,12 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--mode", choices=["chain", "per-linear"], default="chain")
+    ap.add_argument("--mode", choices=["chain", "per-linear", "prefill"], default="chain")
+    ap.add_argument("--model", choices=["qwen3-1.7b", "llama3-8b", "llama3-70b"], default="llama3-8b")
+    ap.add_argument("--layers", type=int, default=None)
+    ap.add_argument("--tokens", type=int, default=2048)
+    ap.add_argument("--fallback", action="store_true",
+                    help="also time the reference's bf16 fallback path on the same step (GPU)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
