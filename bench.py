@@ -27,6 +27,9 @@ Other workloads (not the headline; each prints its own metric):
       prefill tok/s, roofline against the sustained bf16 tensor peak;
   --model qwen3-1.7b|llama3-8b|llama3-70b picks the decoder shapes;
   --layers L keeps the first L layers (small cases for profiling);
+  --tp (with N > 1): one model tensor-parallel over the N GPUs (column-parallel
+      q/k/v and gate/up, row-parallel o and down, an NCCL all-reduce after o and
+      after down), one token stream, strong scaling;
   --fallback also times the reference's bf16 fallback path on the GPU
       (F.linear(x, materialize(bf16)) store by store, torch ops) on the same step.
 
@@ -143,16 +146,17 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # CPU reference arm / CPU baseline
 # ---------------------------------------------------------------------------
-def cpu_reference_sample(seconds=10.0, threads=0, steps=None, warmup=1):
-    """Time the lib.rs restatement on one 8B layer; returns (tok/s, info)."""
+def cpu_reference_sample(seconds=10.0, threads=0, steps=None, warmup=1, model="llama3-8b"):
+    """Time the lib.rs restatement on one layer of `model`; returns (tok/s, info)."""
     import numpy as np
     from oracle import oracle as O
     from epure import synthetic
 
+    shapes = synthetic.SHAPES[model]
     O.build_c_oracle()
     rng = np.random.default_rng(0)
     layer = []
-    for name, n, k in synthetic.LLAMA3_8B.linears():
+    for name, n, k in shapes.linears():
         idx = rng.integers(0, 256, (n, k // 4), dtype=np.uint8)
         cb = rng.standard_normal((256, 4)).astype(np.float16).astype(np.float32)
         sc = np.abs(rng.normal(0, 0.02, (n, k // 128))).astype(np.float16).astype(np.float32)
@@ -177,18 +181,19 @@ def cpu_reference_sample(seconds=10.0, threads=0, steps=None, warmup=1):
         elif time.perf_counter() - t_total >= seconds:
             break
     per_layer = statistics.median(times)
-    tok_s = 1.0 / (per_layer * synthetic.LLAMA3_8B.layers)
+    tok_s = 1.0 / (per_layer * shapes.layers)
     used = threads if threads > 0 else O.c_threads()
     info = {"cores": used, "kind": "port",
-            "sample": f"1 of 32 layers (7 linears, f32 activations), {len(times)} timed "
-                      f"repetitions, median {per_layer*1e3:.1f} ms/layer; tok/s = 1/(32 x layer)"}
+            "sample": f"1 of {shapes.layers} {model} layers (7 linears, f32 activations), "
+                      f"{len(times)} timed repetitions, median {per_layer*1e3:.1f} ms/layer; "
+                      f"tok/s = 1/({shapes.layers} x layer)"}
     return tok_s, info
 
 
 def run_reference(args, rank, world):
     if rank != 0:
         return 0
-    tok_s, info = cpu_reference_sample(steps=args.steps, warmup=args.warmup)
+    tok_s, info = cpu_reference_sample(steps=args.steps, warmup=args.warmup, model=args.model)
     line = {
         "impl": "reference", "metric": METRIC, "value": round(tok_s, 4), "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -256,12 +261,23 @@ def run_ours(args, rank, world, local_rank):
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     shapes = synthetic.SHAPES[args.model]
-    chain = args.mode == "chain"
+    use_tp = args.tp and world > 1
+    chain = args.mode == "chain" and not use_tp
     prefill = args.mode == "prefill"
     m = args.tokens if prefill else 1
-    stack = synthetic.LinearStack(shapes, layers=args.layers, device=dev, seed=1000 * rank,
-                                  gpu_layout="tiled" if chain else "mma16")
-    if chain:
+    if use_tp:
+        # every rank draws its own shards of one model (same seed on every rank)
+        stack = synthetic.LinearStack(shapes, layers=args.layers, device=dev, seed=1000,
+                                      gpu_layout="mma16", tp=(rank, world))
+    else:
+        stack = synthetic.LinearStack(shapes, layers=args.layers, device=dev, seed=1000 * rank,
+                                      gpu_layout="tiled" if chain else "mma16")
+    if use_tp:
+        from epure.tp import TPLinearStack
+        runner = TPLinearStack(stack.blocks, m=m, dtype=torch.bfloat16, device=dev).capture()
+        kernel_name = (("gemm_tc_kernel" if prefill else "gemv_mma_kernel") +
+                       f" on 1/{world} shards + NCCL all-reduce after o and down")
+    elif chain:
         runner = ChainedLinearStack(stack, dtype=torch.bfloat16, device=dev).capture()
         kernel_name = "chain_kernel (one persistent launch per step)"
     elif prefill:
@@ -328,7 +344,8 @@ def run_ours(args, rank, world, local_rank):
 
     hbm_peak, peak_kind = _peaks()
     achieved_gbs = step_bytes / (ms * 1e-3) / 1e9
-    workload = WORKLOAD if args.model == "llama3-8b" else WORKLOAD.replace("llama3-8b", args.model)
+    workload = WORKLOAD.replace("llama3-8b", args.model).replace(
+        "224 linears", f"{7 * stack.layers} linears")
     if prefill:
         workload = workload.replace("batch-1 decode token", f"{m}-token prefill")
     if stack.layers != shapes.layers:
@@ -351,29 +368,43 @@ def run_ours(args, rank, world, local_rank):
                                 if NCU_TRAFFIC_RATIO.get(args.mode) and stack.layers == 32
                                 and args.model == "llama3-8b" else None),
                     "traffic_note": TRAFFIC_NOTE.get(args.mode)}
+    streams = 1 if use_tp else world          # independent token streams across the job
+    if use_tp:
+        # aggregate over the ranks: each streams its shard bytes in the same step time
+        roofline["achieved"] = round(roofline["achieved"] * world, 1)
+        roofline["peak"] = round(roofline["peak"] * world, 1)
+        roofline["aggregate_over_gpus"] = world
+        roofline["traffic"] = None
+        roofline.pop("traffic_note", None)
     if rank == 0:
+        metric = (f"prefill tok/s @{args.model} ({m}-token prompt, packed linears)"
+                  if prefill else METRIC)
+        if use_tp and not prefill:
+            metric = f"decode tok/s bs1 @{args.model}, tensor-parallel over {world} GPUs (packed linears)"
         line = {
-            "metric": (f"prefill tok/s @{args.model} ({m}-token prompt, packed linears)"
-                       if prefill else METRIC),
-            "value": round(world * m * 1000.0 / ms, 2),
+            "metric": metric,
+            "value": round(streams * m * 1000.0 / ms, 2),
             "unit": UNIT,
             "n_gpus": world,
             "steps": args.steps,
             "warmup": args.warmup,
             "ms_per_step": round(ms, 5),
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "strong" if use_tp else "weak",
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic",
-            "config": {"workload": workload, "mode": args.mode, "global_batch": world * m,
+            "config": {"workload": workload,
+                       "mode": ("tp-" + ("prefill" if prefill else "per-linear")) if use_tp else args.mode,
+                       "global_batch": streams * m,
                        "seq_len": m,
-                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "parallelism": (f"tp{world}" if use_tp else
+                                       f"replicas x{world}" if world > 1 else "single GPU"),
                        "l2": (f"inputs larger than L2 ({step_bytes / 1e9:.2f} GB moved per step)"
                               if step_bytes > 126e6 else "working set may fit in L2"),
                        "bytes_per_step": step_bytes, "flops_per_step": step_flops},
             "roofline": roofline,
-            "e2e": {"value": round(world * m * 1000.0 / e2e_ms, 2), "unit": UNIT,
+            "e2e": {"value": round(streams * m * 1000.0 / e2e_ms, 2), "unit": UNIT,
                     "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
                     "d2h_bytes_per_step": out_host.numel() * out_host.element_size()},
             "gpu_launches": launches * args.steps,
@@ -382,9 +413,12 @@ def run_ours(args, rank, world, local_rank):
         if args.fallback:
             line["fallback"] = time_fallback(stack, runner.x, steps=max(1, min(args.steps, 3)))
         if world == 1 and not args.no_cpu_baseline and args.mode != "prefill":
-            tok_s, info = cpu_reference_sample(seconds=args.cpu_seconds)
+            tok_s, info = cpu_reference_sample(seconds=args.cpu_seconds, model=args.model)
             line["cpu_baseline"] = {"value": round(tok_s, 4), "unit": UNIT, **info}
         print(json.dumps(line), flush=True)
+    if use_tp:
+        runner.release()        # the graph holds NCCL work: drop it before the group goes
+        torch.cuda.synchronize(dev)
     return 0
 
 
@@ -400,6 +434,8 @@ def main():
     ap.add_argument("--model", choices=["qwen3-1.7b", "llama3-8b", "llama3-70b"], default="llama3-8b")
     ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--tokens", type=int, default=2048)
+    ap.add_argument("--tp", action="store_true",
+                    help="at N > 1: one model tensor-parallel over the N GPUs instead of N replicas")
     ap.add_argument("--fallback", action="store_true",
                     help="also time the reference's bf16 fallback path on the same step (GPU)")
     args = ap.parse_args()

@@ -1,5 +1,5 @@
 // sm_100a building blocks shared by the tensor-core GEMM kernels: mbarriers
-// with bounded waits, 2-D TMA tile loads (never with cluster multicast), the
+// with bounded waits, 2-D TMA tile loads (each into the issuing CTA only), the
 // tcgen05 shared-memory / instruction descriptors, MMA issue and commit, TMEM
 // allocation and loads.  Encodings follow the PTX ISA for tcgen05 (matrix
 // descriptor: start address >> 4 in bits 0-13, leading byte offset >> 4 in
@@ -59,7 +59,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
 
 // ---------------------------------------------------------------- TMA
 // 2-D tiled tensor load into shared memory, completing on an mbarrier
-// (no cluster multicast).  c0 is the innermost coordinate.
+// (destination: the issuing CTA's shared memory).  c0 is the innermost coordinate.
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, uint32_t bar, int c0,
                                             int c1) {
     asm volatile(

@@ -9,8 +9,8 @@
 // kernel that streams that much spends a fixed ~3 us filling and draining the
 // memory pipeline, which for 128 dependent launches per token costs more than
 // the whole HBM roofline.  Here a producer warp per SM streams the weights of
-// every step through a 6-stage TMA ring (cp.async.bulk + mbarriers, no
-// multicast) without ever waiting for activations -- weights are static -- so
+// every step through a 6-stage TMA ring (cp.async.bulk + mbarriers, each copy to
+// this CTA only) without ever waiting for activations -- weights are static -- so
 // HBM keeps streaming across step boundaries; only the consumers wait for the
 // previous step to finish (a grid barrier: a per-step arrival counter in the
 // workspace, bounded spin).

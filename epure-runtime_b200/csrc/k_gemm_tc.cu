@@ -13,7 +13,7 @@
 //   memory, D = fp32 in TMEM columns 0 .. BN-1.
 // * Pipeline stages of 64 k (one 128-byte swizzle atom of 16-bit values):
 //   - warp 0 (one thread) loads the activation tile with a 2-D TMA copy
-//     (128-byte swizzle, rows past M zero-filled, no multicast) into a ring of
+//     (128-byte swizzle, rows past M zero-filled, this CTA only) into a ring of
 //     up to 8 shared-memory stages;
 //   - warps 2-9 decode the weight tile straight into TMEM: thread = one weight
 //     row = one TMEM lane (warp w owns lanes 32 (w % 4) .. +31; two warps share

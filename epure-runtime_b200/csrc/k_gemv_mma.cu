@@ -24,8 +24,8 @@
 //   lane 4*r + q holds the indices of rows r and r + 8 at positions q + 4s,
 //   s = 0..7.  Tiles run group-fastest, so the 32 groups of one 16-row block
 //   ("chunk") are one contiguous 16 KB run.
-// * A producer warp streams chunks with TMA bulk copies (cp.async.bulk, no
-//   multicast) into a 4-stage shared-memory ring guarded by mbarriers: one
+// * A producer warp streams chunks with TMA bulk copies (cp.async.bulk, into this
+//   CTA's shared memory only) into a 4-stage shared-memory ring guarded by mbarriers: one
 //   16 KB copy for the indices and one 32/64-byte copy per group for the
 //   scales (stored group-major, rows padded to 16).  16 consumer warps each
 //   take two tiles of a chunk; per tile a lane does 16 gathers (PRMT + IMAD +

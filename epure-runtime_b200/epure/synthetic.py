@@ -85,7 +85,10 @@ class LinearStack:
     left out, so a step moves exactly the packed bytes plus activations.
     """
 
-    def __init__(self, shapes, layers=None, device="cuda", seed=0, **store_kw):
+    def __init__(self, shapes, layers=None, device="cuda", seed=0, tp=None, **store_kw):
+        """``tp=(rank, world)`` draws only this rank's tensor-parallel shards:
+        column-parallel linears (q/k/v, gate/up) with out_features / world rows,
+        row-parallel ones (o, down) with in_features / world columns."""
         self.shapes = shapes
         self.layers = layers if layers is not None else shapes.layers
         self.device = torch.device(device)
@@ -94,6 +97,16 @@ class LinearStack:
         for _ in range(self.layers):
             blk = {}
             for name, n, k in shapes.linears():
+                if tp is not None and tp[1] > 1:
+                    world = tp[1]
+                    if name in ("o_proj", "down_proj"):
+                        if k % (world * 128):
+                            raise ValueError(f"{name}: in_features {k} not splittable into {world} groups")
+                        k //= world
+                    else:
+                        if n % world:
+                            raise ValueError(f"{name}: out_features {n} not divisible by {world}")
+                        n //= world
                 blk[name] = make_store(n, k, device=device, seed=s, **store_kw)
                 s += 1
             self.blocks.append(blk)
