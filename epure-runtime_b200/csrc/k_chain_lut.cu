@@ -75,11 +75,12 @@ constexpr int kRing = 3;
 constexpr int kChunkTiles = 64;                                    // one tile per 8-lane team
 constexpr uint32_t kStageIdx = kChunkTiles * 512;                  // 32 KB of index tiles
 constexpr uint32_t kStageBytes = kStageIdx + kChunkTiles * 64;     // + scales (<= fp32)
-constexpr int kXParts = kConsumers / 32;                           // activation staging split
+constexpr int kXGroups = kConsumerWarps / 4;     // activation staging: warp groups of 4 parts
+static_assert(kConsumerWarps == 16, "staging: 4 column-quad groups x 4 part groups of warps");
 // Shared-window addresses (the dynamic block starts at a small offset `base`).
 constexpr uint32_t kXsOff = 8192;      // from base: 2 x codebook [1024] fp32 below, then
-                                       // 2 x activation slice partials [kXParts][128] fp32
-constexpr uint32_t kBarOff = kXsOff + 2 * kXParts * 512;   // from base: full[kRing], empty[kRing]
+                                       // 2 x activation slice sums [kXGroups][128] fp32
+constexpr uint32_t kBarOff = kXsOff + 2 * kXGroups * 512;  // from base: full[kRing], empty[kRing]
 constexpr uint32_t kMiscOff = kBarOff + 128;               // from base: broadcast words
 constexpr uint32_t kLowStages = 26624; // window address of stage 0
 constexpr uint32_t kTBase = 65536;     // window address of T (low 16 bits zero for the PRMT trick)
@@ -100,6 +101,16 @@ __device__ __forceinline__ float lds_f32(uint32_t addr) {
     float v;
     asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
     return v;
+}
+__device__ __forceinline__ float4 lds_f32x4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ void sts_f32(uint32_t addr, float v) {
+    asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
 __device__ __forceinline__ uint4 lds128(uint32_t addr) {
     uint4 v;
@@ -248,9 +259,9 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
     // Double-buffered staging (parity flips per change), so a new table's inputs
     // can be written while no warp still needs the previous ones.
     float* cbf_buf = reinterpret_cast<float*>(smem);                          // [2][256][4]
-    float* xs_buf = reinterpret_cast<float*>(smem + kXsOff);                  // [2][kXParts][128]
+    float* xs_buf = reinterpret_cast<float*>(smem + kXsOff);                  // [2][kXGroups][128]
     int cbp = 0, xsp = 0;
-    float* T = reinterpret_cast<float*>(smem + (kTBase - base));              // [256][2][32]
+    // T ([256][2][32] fp32) lives at window address kTBase and is addressed directly.
     // Codebooks are fetched one step ahead into registers (values 2t, 2t+1 of
     // each store of the step), so building a table never waits on DRAM.
     uint2 cb_raw[kLutMaxStores];
@@ -326,10 +337,14 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
                 }
                 if (g != cur_g) {
                     xsp ^= 1;
-                    float* xs = xs_buf + xsp * (kXParts * 128);
-                    // x[128 g + 4 c4 .. +4] = sum over the input partial slices; thread
-                    // (c4, part) adds slices part, part + kXParts, ... (fixed order).
-                    const int c4 = threadIdx.x & 31, part = threadIdx.x >> 5;
+                    float* xs = xs_buf + xsp * (kXGroups * 128);
+                    // x[128 g + 4 c4 .. +4] = sum over the input partial slices.  Warp w
+                    // covers column quads 8 (w % 4) .. +7 (128 contiguous bytes per slice)
+                    // for parts 4 (w / 4) + lane / 8; part p adds slices p, p + 16, ...
+                    // Two xor-shuffles sum the warp's 4 parts; the table build adds the
+                    // kXGroups warp-group sums (fixed order throughout).
+                    const int c4 = 8 * (warp & 3) + (lane & 7);
+                    const int part = 4 * (warp >> 2) + (lane >> 3);
                     const int64_t c = (int64_t)g * 128 + 4 * c4;
                     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
                     if (c < S.k) {
@@ -341,7 +356,7 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
                             const float4* col = reinterpret_cast<const float4*>(pin + c);
                             const int64_t st4 = pin_stride >> 2;
 #pragma unroll 8
-                            for (int gp = part; gp < pin_ng; gp += kXParts) {
+                            for (int gp = part; gp < pin_ng; gp += 16) {
                                 const float4 u = __ldcg(col + gp * st4);
                                 v.x += u.x;
                                 v.y += u.y;
@@ -350,17 +365,23 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
                             }
                         }
                     }
-                    reinterpret_cast<float4*>(xs)[part * 32 + c4] = v;
+#pragma unroll
+                    for (int off = 8; off <= 16; off <<= 1) {
+                        v.x += __shfl_xor_sync(0xffffffffu, v.x, off);
+                        v.y += __shfl_xor_sync(0xffffffffu, v.y, off);
+                        v.z += __shfl_xor_sync(0xffffffffu, v.z, off);
+                        v.w += __shfl_xor_sync(0xffffffffu, v.w, off);
+                    }
+                    if (lane < 8) reinterpret_cast<float4*>(xs)[(warp >> 2) * 32 + c4] = v;
                 }
                 cur_s = si;
                 cur_g = g;
                 consumers_sync();
                 {
-                    const float* cbf = cbf_buf + cbp * 1024;
-                    const float* xs = xs_buf + xsp * (kXParts * 128);
+                    const float* xs = xs_buf + xsp * (kXGroups * 128);
                     float4 xv = reinterpret_cast<const float4*>(xs)[lane];
 #pragma unroll
-                    for (int h = 1; h < kXParts; ++h) {
+                    for (int h = 1; h < kXGroups; ++h) {
                         const float4 u = reinterpret_cast<const float4*>(xs)[h * 32 + lane];
                         xv.x += u.x;
                         xv.y += u.y;
@@ -368,16 +389,25 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
                         xv.w += u.w;
                     }
                     const float x0v = xv.x, x1v = xv.y, x2v = xv.z, x3v = xv.w;
-                    const float4* cb4 = reinterpret_cast<const float4*>(cbf);
-#pragma unroll 4
-                    for (int q = 0; q < 256 / kConsumerWarps; ++q) {
-                        const int e = warp + kConsumerWarps * q;
-                        const float4 cv = cb4[e];
-                        float v = cv.x * x0v;
-                        v = fmaf(cv.y, x1v, v);
-                        v = fmaf(cv.z, x2v, v);
-                        v = fmaf(cv.w, x3v, v);
-                        T[e * 64 + (slot ^ 1) * 32 + lane] = v;
+                    // The warp's 16 codebook entries are loaded before any table store:
+                    // the loads cannot be reordered past stores to the same shared
+                    // window, so interleaving them would serialise 16 load->store chains.
+                    const uint32_t cb_addr = base + cbp * 4096u + 16u * warp;
+                    const uint32_t t_addr = kTBase + 4u * ((slot ^ 1) * 32 + lane) + 256u * warp;
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        float4 cv[8];
+#pragma unroll
+                        for (int q = 0; q < 8; ++q)
+                            cv[q] = lds_f32x4(cb_addr + 16u * kConsumerWarps * (8 * h + q));
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) {
+                            float v = cv[q].x * x0v;
+                            v = fmaf(cv[q].y, x1v, v);
+                            v = fmaf(cv[q].z, x2v, v);
+                            v = fmaf(cv[q].w, x3v, v);
+                            sts_f32(t_addr + 256u * kConsumerWarps * (8 * h + q), v);
+                        }
                     }
                 }
                 slot ^= 1;
