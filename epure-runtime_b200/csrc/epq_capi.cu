@@ -95,18 +95,20 @@ const char* epq_last_error(void) { return g_err; }
 
 int epq_device_error(int* flag) {
     if (!flag) return set_error(EPQ_EINVAL, "epq_device_error: flag is NULL");
-    int lut = 0, mma = 0, chain = 0, tc = 0;
+    int lut = 0, mma = 0, chain = 0, tc = 0, bwd = 0;
     int rc = lut_read_device_error(&lut);
     if (rc) return rc;
     rc = mma_read_device_error(&mma);
     if (rc) return rc;
     rc = tc_read_device_error(&tc);
     if (rc) return rc;
+    rc = bwd_tc_read_device_error(&bwd);
+    if (rc) return rc;
     rc = chain_read_device_error(&chain);
     if (rc) return rc;
-    // bit 0: LUT placement check; bit 1: a bounded wait gave up (GEMV, GEMM or chain);
+    // bit 0: LUT placement check; bit 1: a bounded wait gave up (GEMV, GEMM, backward or chain);
     // bit 2: the chain kernel's placement or grid check failed
-    *flag = (lut ? 1 : 0) | ((mma || tc || chain == 1) ? 2 : 0) | (chain == 2 ? 4 : 0);
+    *flag = (lut ? 1 : 0) | ((mma || tc || bwd || chain == 1) ? 2 : 0) | (chain == 2 ? 4 : 0);
     return EPQ_OK;
 }
 
@@ -242,8 +244,18 @@ int epq_linear_bwd(const epq_store* store, const void* x, int64_t ldx, const voi
     if (m > 0 && s.n > 0 && (!dy || ldy < s.n)) return set_error(EPQ_EINVAL, "linear_bwd: dy/ldy");
     if ((dscale || dcb) && !x_ok(x, m, s.k, ldx)) return set_error(EPQ_EINVAL, "linear_bwd: x/ldx");
     if (dx && lddx < s.k) return set_error(EPQ_ESHAPE, "linear_bwd: lddx < k");
-    return launch_bwd_generic(s, x, ldx, dy, ldy, act_dtype, m, dx, lddx, dx_dtype, dscale, dcb,
-                              static_cast<cudaStream_t>(stream));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if ((dscale || dcb) && s.n > 0 && bwd_tc_eligible(s, m, act_dtype, x, ldx, dy, ldy)) {
+        // dscale / dcb on the tensor cores (dW never stored); dX below
+        if (dcb && cudaMemsetAsync(dcb, 0, sizeof(float) * s.levels * s.vec, st) != cudaSuccess)
+            return check_launch("memset dcb");
+        rc = launch_bwd_dw_tc(s, x, ldx, dy, ldy, act_dtype, m, dscale, dcb, st);
+        if (rc) return rc;
+        return dx ? launch_bwd_generic(s, x, ldx, dy, ldy, act_dtype, m, dx, lddx, dx_dtype, nullptr,
+                                       nullptr, st)
+                  : EPQ_OK;
+    }
+    return launch_bwd_generic(s, x, ldx, dy, ldy, act_dtype, m, dx, lddx, dx_dtype, dscale, dcb, st);
 }
 
 int epq_materialize(const epq_store* store, void* w, int64_t ldw, int32_t out_dtype, void* stream) {

@@ -127,6 +127,13 @@ int launch_linear_tc(const StoreD* s, int count, const void* x, int x_dtype, int
                      void* const* outs, const int64_t* ldo, int out_dtype, cudaStream_t st);
 int tc_read_device_error(int* flag);
 
+// Tensor-core compressed-state backward: dscale / dcb from dY^T X tiles (k_bwd_tc.cu).
+bool bwd_tc_eligible(const StoreD& s, int64_t m, int act_dtype, const void* x, int64_t ldx,
+                     const void* dy, int64_t ldy);
+int launch_bwd_dw_tc(const StoreD& s, const void* x, int64_t ldx, const void* dy, int64_t ldy,
+                     int act_dtype, int64_t m, float* dscale, float* dcb, cudaStream_t st);
+int bwd_tc_read_device_error(int* flag);
+
 // Batch-1 LUT kernel over up to 4 stores sharing x.
 constexpr int kLutMaxStores = 4;
 bool lut_eligible(const StoreD& s);

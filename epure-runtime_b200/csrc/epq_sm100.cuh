@@ -8,6 +8,8 @@
 // in 7-9 / 10-12, A/B major in 15 / 16, N >> 3 in 17-22, M >> 4 in 24-28).
 #pragma once
 
+#include <cuda.h>
+
 #include <cstdint>
 
 namespace epq {
@@ -98,13 +100,28 @@ __device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t saddr) {
     return d;
 }
 
+// MN-major operand tile in the 128-byte swizzle (what a 2-D TMA box {64, rows}
+// with 128-byte swizzle writes when the 64 contiguous elements run along M or
+// N): atoms of 8 K-rows x 64 MN-elements (1024 bytes), K-row groups `sbo`
+// bytes apart, 64-element MN blocks `lbo` bytes apart.  Advancing k by 16
+// rows adds 2 * sbo bytes.
+__device__ __forceinline__ uint64_t desc_mnmajor_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)2 << 61;
+    return d;
+}
+
 // kind::f16 instruction descriptor: fp32 accumulator, A and B both bf16 (or
-// both f16), both K-major, tile M x N.
-template <bool kBf16, int M, int N>
+// both f16), tile M x N; A / B K-major unless kAmn / kBmn (MN-major).
+template <bool kBf16, int M, int N, bool kAmn = false, bool kBmn = false>
 __host__ __device__ constexpr uint32_t idesc_f16() {
     static_assert(M == 64 || M == 128, "M");
     static_assert(N % 16 == 0 && N >= 16 && N <= 256, "N");
     return (1u << 4) | ((kBf16 ? 1u : 0u) << 7) | ((kBf16 ? 1u : 0u) << 10) |
+           ((kAmn ? 1u : 0u) << 15) | ((kBmn ? 1u : 0u) << 16) |
            ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
@@ -208,4 +225,11 @@ __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
 }
 
 }  // namespace sm100
+
+// Host: 2-D tensor map over a row-major [outer, inner] matrix of 16-bit elements
+// (row stride `ld` elements), box {box_inner, box_outer}, 128-byte swizzle, zero
+// fill outside the matrix (k_gemm_tc.cu).
+int make_tmap_2d(CUtensorMap* map, const void* base, int dtype, int64_t inner, int64_t outer,
+                 int64_t ld, int box_inner, int box_outer, const char* who);
+
 }  // namespace epq

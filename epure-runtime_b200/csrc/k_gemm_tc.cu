@@ -389,6 +389,29 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
+}  // namespace
+
+// 2-D tensor map over a row-major [outer, inner] matrix of 16-bit elements with row
+// stride `ld` (elements), box {box_inner, box_outer}, 128-byte swizzle, zero fill.
+int make_tmap_2d(CUtensorMap* map, const void* base, int dtype, int64_t inner, int64_t outer,
+                 int64_t ld, int box_inner, int box_outer, const char* who) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc = encode_fn();
+    if (!enc) return set_error(EPQ_EUNSUPPORTED, "%s: cuTensorMapEncodeTiled unavailable", who);
+    const cuuint64_t gdim[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+    const cuuint64_t gstride[1] = {(cuuint64_t)ld * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer};
+    const cuuint32_t estride[2] = {1, 1};
+    const CUresult cr = enc(map, dtype == EPQ_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                  : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                            2, const_cast<void*>(base), gdim, gstride, box, estride,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (cr != CUDA_SUCCESS) return set_error(EPQ_EINVAL, "%s: tensor map (error %d)", who, (int)cr);
+    return EPQ_OK;
+}
+
+namespace {
+
 bool g_attr[3][2][2][64];
 
 template <bool kBf16, int kLayout, int BN>
@@ -448,8 +471,6 @@ int launch_linear_tc(const StoreD* s, int count, const void* x, int x_dtype, int
     for (int i = 1; i < count; ++i)
         if (s[i].layout != s[0].layout)
             return set_error(EPQ_ELAYOUT, "linear: fused stores need one layout");
-    PFN_cuTensorMapEncodeTiled_v12000 enc = encode_fn();
-    if (!enc) return set_error(EPQ_EUNSUPPORTED, "linear: cuTensorMapEncodeTiled unavailable");
     const int bn = m >= 256 ? 256 : (m > 64 ? 128 : 64);
     if (cdiv(m, bn) > 65535) return set_error(EPQ_EUNSUPPORTED, "linear: m too large");
 
@@ -479,16 +500,8 @@ int launch_linear_tc(const StoreD* s, int count, const void* x, int x_dtype, int
     if (tiles >= (int64_t(1) << 31) - 1) return set_error(EPQ_EUNSUPPORTED, "linear: too many rows");
 
     CUtensorMap xmap;
-    const cuuint64_t gdim[2] = {(cuuint64_t)P.k, (cuuint64_t)m};
-    const cuuint64_t gstride[1] = {(cuuint64_t)ldx * 2};
-    const cuuint32_t box[2] = {(cuuint32_t)kKStage, (cuuint32_t)bn};
-    const cuuint32_t estride[2] = {1, 1};
-    const CUresult cr = enc(&xmap, x_dtype == EPQ_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                                       : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                            2, const_cast<void*>(x), gdim, gstride, box, estride,
-                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (cr != CUDA_SUCCESS) return set_error(EPQ_EINVAL, "linear: activation tensor map (error %d)", (int)cr);
+    const int trc = make_tmap_2d(&xmap, x, x_dtype, P.k, m, ldx, kKStage, bn, "linear");
+    if (trc) return trc;
 
     const bool bf = x_dtype == EPQ_BF16;
     const bool mma16 = s[0].layout == EPQ_LAYOUT_MMA16;
