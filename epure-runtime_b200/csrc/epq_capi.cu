@@ -104,6 +104,10 @@ int epq_device_error(int* flag) {
     if (rc) return rc;
     rc = bwd_tc_read_device_error(&bwd);
     if (rc) return rc;
+    int dxe = 0;
+    rc = dx_tc_read_device_error(&dxe);
+    if (rc) return rc;
+    bwd = bwd || dxe;
     rc = chain_read_device_error(&chain);
     if (rc) return rc;
     // bit 0: LUT placement check; bit 1: a bounded wait gave up (GEMV, GEMM, backward or chain);
@@ -245,16 +249,22 @@ int epq_linear_bwd(const epq_store* store, const void* x, int64_t ldx, const voi
     if ((dscale || dcb) && !x_ok(x, m, s.k, ldx)) return set_error(EPQ_EINVAL, "linear_bwd: x/ldx");
     if (dx && lddx < s.k) return set_error(EPQ_ESHAPE, "linear_bwd: lddx < k");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // dX: tensor cores (W decoded along its rows into TMEM) where eligible
+    if (dx && m > 0 && s.k > 0 && dx_tc_eligible(s, m, act_dtype, dy, ldy)) {
+        rc = launch_bwd_dx_tc(s, dy, ldy, act_dtype, m, dx, lddx, dx_dtype, st);
+        if (rc) return rc;
+        dx = nullptr;
+    }
     if ((dscale || dcb) && s.n > 0 && bwd_tc_eligible(s, m, act_dtype, x, ldx, dy, ldy)) {
-        // dscale / dcb on the tensor cores (dW never stored); dX below
+        // dscale / dcb on the tensor cores (dW never stored)
         if (dcb && cudaMemsetAsync(dcb, 0, sizeof(float) * s.levels * s.vec, st) != cudaSuccess)
             return check_launch("memset dcb");
         rc = launch_bwd_dw_tc(s, x, ldx, dy, ldy, act_dtype, m, dscale, dcb, st);
         if (rc) return rc;
-        return dx ? launch_bwd_generic(s, x, ldx, dy, ldy, act_dtype, m, dx, lddx, dx_dtype, nullptr,
-                                       nullptr, st)
-                  : EPQ_OK;
+        dscale = nullptr;
+        dcb = nullptr;
     }
+    if (!dx && !dscale && !dcb) return EPQ_OK;
     return launch_bwd_generic(s, x, ldx, dy, ldy, act_dtype, m, dx, lddx, dx_dtype, dscale, dcb, st);
 }
 

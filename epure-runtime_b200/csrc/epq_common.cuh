@@ -133,6 +133,11 @@ bool bwd_tc_eligible(const StoreD& s, int64_t m, int act_dtype, const void* x, i
 int launch_bwd_dw_tc(const StoreD& s, const void* x, int64_t ldx, const void* dy, int64_t ldy,
                      int act_dtype, int64_t m, float* dscale, float* dcb, cudaStream_t st);
 int bwd_tc_read_device_error(int* flag);
+// Tensor-core dX = dY W with W decoded along its rows (k_bwd_dx_tc.cu).
+bool dx_tc_eligible(const StoreD& s, int64_t m, int act_dtype, const void* dy, int64_t ldy);
+int launch_bwd_dx_tc(const StoreD& s, const void* dy, int64_t ldy, int act_dtype, int64_t m, void* dx,
+                     int64_t lddx, int dx_dtype, cudaStream_t st);
+int dx_tc_read_device_error(int* flag);
 
 // Batch-1 LUT kernel over up to 4 stores sharing x.
 constexpr int kLutMaxStores = 4;

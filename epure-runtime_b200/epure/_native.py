@@ -218,8 +218,10 @@ def linear(x, store, out_dtype=None):
     return linear_multi(x, [store], out_dtype)[0]
 
 
-def linear_bwd(x, dy, store, need_dx=True, need_dscale=True, need_dcb=True):
-    """(dx, dscale [n, ng] f32, dcb [levels*vec] f32) of ``sum(dy * (x @ W^T))``."""
+def linear_bwd(x, dy, store, need_dx=True, need_dscale=True, need_dcb=True, dx_dtype=None):
+    """(dx, dscale [n, ng] f32, dcb [levels*vec] f32) of ``sum(dy * (x @ W^T))``.
+
+    ``dx`` has ``dx_dtype`` (default: x's dtype)."""
     lib = load_library()
     k, n = store.in_features, store.out_features
     x2 = x.reshape(-1, k).contiguous()
@@ -227,7 +229,8 @@ def linear_bwd(x, dy, store, need_dx=True, need_dscale=True, need_dcb=True):
     m = x2.shape[0]
     dev = x.device
     d = describe_store(store)
-    dx = torch.empty((m, k), dtype=x.dtype, device=dev) if need_dx else None
+    dx_dtype = dx_dtype or x.dtype
+    dx = torch.empty((m, k), dtype=dx_dtype, device=dev) if need_dx else None
     ng = -(-k // store.group)
     dscale = torch.empty((n, ng), dtype=torch.float32, device=dev) if need_dscale else None
     dcb = torch.empty(store.levels * store.vec, dtype=torch.float32, device=dev) \
@@ -235,7 +238,7 @@ def linear_bwd(x, dy, store, need_dx=True, need_dscale=True, need_dcb=True):
     rc = lib.epq_linear_bwd(
         ctypes.byref(d), x2.data_ptr(), x2.stride(0), dy2.data_ptr(), dy2.stride(0),
         dtype_code(x2.dtype), m, dx.data_ptr() if dx is not None else None, k,
-        dtype_code(x.dtype), dscale.data_ptr() if dscale is not None else None,
+        dtype_code(dx_dtype), dscale.data_ptr() if dscale is not None else None,
         dcb.data_ptr() if dcb is not None else None, _stream_ptr(dev))
     _check(rc, "epq_linear_bwd")
     return (dx.reshape(*x.shape[:-1], k) if dx is not None else None), dscale, dcb

@@ -1,11 +1,13 @@
-"""The tensor-core compressed-state backward (dscale, dcb from dY^T X tiles) on the GPU.
+"""The tensor-core backward on the GPU: dX = dY W and dscale, dcb from dY^T X tiles.
 
 With 16-bit activations and m >= 64, epq_linear_bwd computes dscale and dcb on
 the tensor cores: dW = dY^T X in fp32 (exact products of the 16-bit inputs,
 fp32 accumulation) reduced in the epilogue, dW never written.  Compared with
 the float64 gradients of the same 16-bit inputs (the autograd of
 materialize + F.linear, oracle.grads_reference): <= 2e-4 relative per tensor;
-and with the general (SIMT) kernel on fp32 copies of the same inputs.
+and with the general (SIMT) kernel on fp32 copies of the same inputs.  dX
+(W decoded along its rows into tensor memory, exactly the reference's bf16
+weight) in fp32 equals the float64 product dY W_bf16 to fp32 accumulation noise.
 """
 import numpy as np
 import pytest
@@ -109,3 +111,36 @@ def test_autograd_fine_tune_step(oracle_mod):
     assert _rel(s.scale.grad, want_ds) <= 2e-4
     assert _rel(s.cb.grad.reshape(-1), want_dcb) <= 2e-4
     verify_frozen(model, snap)
+
+
+def _w16_f64(O, st, dtype="bfloat16"):
+    idx = st.index_rows().cpu().numpy()
+    return O.materialize(idx, st.scale.detach().float().cpu().numpy(), st.cb.detach().float().cpu().numpy(),
+                         st.out_features, st.in_features, 4, 128, 256, dtype).astype(np.float64)
+
+
+@pytest.mark.parametrize("n,k,m", [(128, 128, 64), (192, 256, 100), (1024, 4096, 256),
+                                   (6144, 2048, 512), (64, 1024, 17), (2048, 512, 300)])
+def test_dx_tensor_cores(n, k, m, oracle_mod, gpu_layout):
+    from epure import _native, synthetic
+    O = oracle_mod
+    st = synthetic.make_store(n, k, device=DEV, seed=2 * n + k)
+    x, dy = _inputs(m, n, k, seed=m + 1)
+    dx32, _, _ = _native.linear_bwd(x, dy, st, need_dscale=False, need_dcb=False,
+                                    dx_dtype=torch.float32)
+    want = dy.double().cpu().numpy() @ _w16_f64(O, st)
+    assert _rel(dx32, want) <= (1e-5 if n <= 4096 else 3e-5)
+    dx16, _, _ = _native.linear_bwd(x, dy, st, need_dscale=False, need_dcb=False)
+    want_dx, _, _ = _want(O, st, x, dy)
+    assert _rel(dx16.float(), want_dx) <= 1e-2
+
+
+def test_dx_fp16_and_fp32_scales(oracle_mod):
+    from epure import _native, synthetic
+    O = oracle_mod
+    st = synthetic.make_store(256, 512, device=DEV, seed=21, scale_dtype=torch.float32)
+    x, dy = _inputs(96, 256, 512, seed=22, dtype=torch.float16)
+    dx32, _, _ = _native.linear_bwd(x, dy, st, need_dscale=False, need_dcb=False,
+                                    dx_dtype=torch.float32)
+    want = dy.double().cpu().numpy() @ _w16_f64(O, st, "float16")
+    assert _rel(dx32, want) <= 1e-5
