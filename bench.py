@@ -22,6 +22,9 @@ model fits one GPU, so there is no collective on the data path); the time is
 the max over ranks.
 
 Other workloads (not the headline; each prints its own metric):
+  --mode finetune [--tokens 16384]: one compressed-state fine-tuning step (the
+      config-3 batch of 8 x 2048 tokens, Qwen3-1.7B shapes by default) through
+      every packed linear: forward, dX, dscale/dcb (epure.train.PackedTrainStep);
   --mode prefill [--tokens 2048]: a prompt of `tokens` rows through every packed
       linear (the tensor-core dequant-GEMM, one launch per fused group), metric
       prefill tok/s, roofline against the sustained bf16 tensor peak;
@@ -252,6 +255,144 @@ def time_fallback(stack, x, steps):
             "steps": steps}
 
 
+def run_finetune(args, rank, world, local_rank):
+    """One compressed-state fine-tuning step over every packed linear (config 3)."""
+    import torch
+    import torch.distributed as dist
+    from epure import synthetic
+    from epure.train import PackedTrainStep
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    model = args.model
+    shapes = synthetic.SHAPES[model]
+    m = args.tokens
+    # make_trainable(mode="both") keeps scales and codebooks as fp32 parameters
+    stack = synthetic.LinearStack(shapes, layers=args.layers, device=dev, seed=1000 * rank,
+                                  gpu_layout="mma16", scale_dtype=torch.float32,
+                                  cb_dtype=torch.float32)
+    trainer = PackedTrainStep(stack, m, device=dev, seed=rank)
+    g = torch.Generator(device=dev).manual_seed(rank)
+    x = torch.randn(m, shapes.hidden, generator=g, device=dev).to(torch.bfloat16)
+    flops = trainer.flops()
+    for _ in range(args.warmup):
+        trainer.step(x)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    stream = torch.cuda.current_stream(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            trainer.step(x)
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+    ms = ev0.elapsed_time(ev1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    # end to end: the token batch from pinned host memory, the step, one gradient read back
+    xh = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
+    xh.copy_(x.cpu())
+    gh = torch.empty(1, dtype=torch.float32, pin_memory=True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        xd = xh.to(dev, non_blocking=True)
+        trainer.step(xd)
+        gh.copy_(trainer.grads[0]["q_proj"][1][:1], non_blocking=True)
+        stream.synchronize()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    tf_peak, tf_kind = _tensor_peak()
+    achieved = flops / (ms * 1e-3) / 1e12
+    if rank == 0:
+        line = {
+            "metric": f"fine-tune tok/s @{model} (packed linears fwd + dX + dscale/dcb, {m} tokens/step)",
+            "value": round(world * m * 1000.0 / ms, 2), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": f"{model} packed linears, compressed-state fine-tune step "
+                                   f"({7 * stack.layers} linears, fp32 scales and codebooks)",
+                       "mode": "finetune", "global_batch": world * m, "seq_len": m,
+                       "parallelism": f"data-parallel replicas x{world}" if world > 1 else "single GPU",
+                       "flops_per_step": flops},
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": tf_peak,
+                         "unit": "TFLOP/s", "frac": round(achieved / tf_peak, 4), "peak_kind": tf_kind,
+                         "kernel": "gemm_tc_kernel + bwd_dx_tc_kernel + bwd_dw_tc_kernel",
+                         "traffic": None},
+            "e2e": {"value": round(world * m * 1000.0 / e2e_ms, 2), "unit": UNIT,
+                    "h2d_bytes_per_step": x.numel() * x.element_size(), "d2h_bytes_per_step": 4},
+            "gpu_launches": (4 + 7) * stack.layers * args.steps,
+            "clocks": clocks.summary(),
+        }
+        if args.fallback:
+            line["fallback"] = time_fallback_finetune(stack, x, steps=max(1, min(args.steps, 2)))
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def time_fallback_finetune(stack, x, steps):
+    """The reference's fine-tuning autograd on the same step (GPU, torch ops).
+
+    make_trainable (finetune.py:49-102) + PackedLinear.forward's fallback
+    F.linear(x, materialize(bf16)) (runtime.py:78-89, 123-124): torch autograd
+    differentiates the gather/scale expansion and the GEMM; fp32 parameters.
+    """
+    import torch
+    import torch.nn.functional as F
+    params = []
+    for b in stack.blocks:
+        pb = {}
+        for name, st in b.items():
+            pb[name] = (st.index_rows().long(), st.cb.float().clone().requires_grad_(True),
+                        st.scale.float().clone().requires_grad_(True), st)
+        params.append(pb)
+
+    def weight(p):
+        idx, cb, sc, st = p
+        w = cb.to(torch.bfloat16)[idx].reshape(st.out_features, -1)[:, :st.in_features]
+        return w * sc.to(torch.bfloat16).repeat_interleave(st.group, dim=1)[:, :st.in_features]
+
+    def step():
+        h = x.detach().requires_grad_(True)
+        outs = []
+        for pb in params:
+            q = F.linear(h, weight(pb["q_proj"]))
+            k = F.linear(h, weight(pb["k_proj"]))
+            v = F.linear(h, weight(pb["v_proj"]))
+            o = F.linear(q, weight(pb["o_proj"]))
+            gt = F.linear(o, weight(pb["gate_proj"]))
+            u = F.linear(o, weight(pb["up_proj"]))
+            h = F.linear(u, weight(pb["down_proj"]))
+            outs += [k, v, gt]
+        loss = h.float().square().mean() + sum(t.float().mean() for t in outs)
+        loss.backward()
+
+    step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    return {"what": "reference fine-tune autograd: F.linear(x, materialize(bf16)) per store, "
+                    "fp32 scale/codebook parameters (torch ops)",
+            "ms_per_step": round(ms, 3), "value": round(x.shape[0] * 1000.0 / ms, 2), "unit": UNIT,
+            "steps": steps}
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
@@ -430,10 +571,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--mode", choices=["chain", "per-linear", "prefill"], default="chain")
-    ap.add_argument("--model", choices=["qwen3-1.7b", "llama3-8b", "llama3-70b"], default="llama3-8b")
+    ap.add_argument("--mode", choices=["chain", "per-linear", "prefill", "finetune"], default="chain")
+    ap.add_argument("--model", choices=["qwen3-1.7b", "llama3-8b", "llama3-70b"], default=None)
     ap.add_argument("--layers", type=int, default=None)
-    ap.add_argument("--tokens", type=int, default=2048)
+    ap.add_argument("--tokens", type=int, default=None)
     ap.add_argument("--tp", action="store_true",
                     help="at N > 1: one model tensor-parallel over the N GPUs instead of N replicas")
     ap.add_argument("--fallback", action="store_true",
@@ -441,6 +582,11 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    args.model_set = args.model is not None
+    if args.model is None:
+        args.model = "qwen3-1.7b" if args.mode == "finetune" else "llama3-8b"
+    if args.tokens is None:
+        args.tokens = 8 * 2048 if args.mode == "finetune" else 2048
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -457,6 +603,8 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
     try:
+        if args.mode == "finetune":
+            return run_finetune(args, rank, world, local_rank)
         return run_ours(args, rank, world, local_rank)
     finally:
         if world > 1:
