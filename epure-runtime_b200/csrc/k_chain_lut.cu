@@ -25,9 +25,10 @@
 // different banks), and a 3-step butterfly leaves each lane with 2 row sums.
 //
 // Split over k without a reduction tail.  A step's tiles are ordered (store,
-// group, row block) and each CTA takes a contiguous range, so it covers about
-// one group of many rows (one table build) and writes scaled group sums to a
-// partial buffer [group][row].  Nobody reduces them in that step: the NEXT
+// group, row block) and each CTA takes a contiguous range, chosen on the host
+// to balance tiles against table builds (a CTA whose range crosses a group
+// boundary builds one table more), so it covers about one group of many rows
+// and writes scaled group sums to a partial buffer [group][row].  Nobody reduces them in that step: the NEXT
 // step's consumers add the partials of exactly the input columns they need
 // while staging their activation slice (deterministic order), and after the
 // last step all CTAs reduce the final output rows.  Partial buffers ping-pong
@@ -57,7 +58,8 @@ struct ChainStoreD {
 struct ChainStepD {
     ChainStoreD st[kLutMaxStores];
     int count, feed, k, kpos;
-    int total_tiles, tiles_per_cta, pad0, pad1;
+    int total_tiles, pad0;
+    int64_t range_off;    // workspace offset of int32 [grid + 1]: CTA c takes tiles [r[c], r[c+1])
 };
 
 struct ChainHeaderD {
@@ -231,8 +233,8 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
         int i = 0;
         for (int j = 0; j < n_steps; ++j) {
             const ChainStepD& S = steps[j];
-            ChunkIt it{(int)blockIdx.x * S.tiles_per_cta,
-                       min(((int)blockIdx.x + 1) * S.tiles_per_cta, S.total_tiles)};
+            const int* rg = reinterpret_cast<const int*>(ws + S.range_off);
+            ChunkIt it{rg[blockIdx.x], rg[blockIdx.x + 1]};
             int si, g, rb0, nt;
             while (it.next(S, si, g, rb0, nt)) {
                 const int stage = i % kRing;
@@ -318,8 +320,8 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
         const int pin_ng = j > 0 ? P->st[P->feed].ng : 0;
         float* pout = part[j & 1];
 
-        ChunkIt it{(int)blockIdx.x * S.tiles_per_cta,
-                   min(((int)blockIdx.x + 1) * S.tiles_per_cta, S.total_tiles)};
+        const int* rg = reinterpret_cast<const int*>(ws + S.range_off);
+        ChunkIt it{rg[blockIdx.x], rg[blockIdx.x + 1]};
         int si, g, rb0, nt, cur_s = -1, cur_g = -1;
         while (it.next(S, si, g, rb0, nt)) {
             const ChainStoreD& C = S.st[si];
@@ -521,13 +523,71 @@ int chain_read_device_error(int* flag) {
 
 static int64_t al256(int64_t v) { return (v + 255) & ~int64_t(255); }
 
+// Tile ranges of one step over `grid` CTAs.  A CTA's time is about its tiles
+// plus one table build (activation slice staging + LUT build) per (store, group)
+// segment it enters; a build costs about kTableTiles tiles of chunk work, so a
+// range that straddles a segment boundary is much dearer than its tile count.
+// The ranges stay contiguous in (store, group, row block) order and minimise the
+// largest per-CTA cost (binary search on the cost; greedy packing); CTAs left
+// over get empty ranges.
+constexpr int kTableTiles = 96;
+
+static int pack_ranges(const std::vector<int>& seg, int64_t cap, std::vector<int>* starts) {
+    int ctas = 0;
+    int64_t cost = 0, t = 0;
+    bool open = false;
+    if (starts) starts->clear();
+    for (const int z : seg) {
+        int64_t rem = z;
+        bool entered = false;          // has the open CTA paid for this segment's table?
+        while (rem > 0) {
+            if (!open) {
+                open = true;
+                entered = false;
+                ++ctas;
+                cost = 0;
+                if (starts) starts->push_back((int)t);
+            }
+            const int64_t room = cap - cost - (entered ? 0 : kTableTiles);
+            if (room <= 0) {
+                open = false;
+                continue;
+            }
+            const int64_t take = rem < room ? rem : room;
+            cost += take + (entered ? 0 : kTableTiles);
+            entered = true;
+            rem -= take;
+            t += take;
+            if (cost >= cap) open = false;
+        }
+    }
+    return ctas;
+}
+
+static void balance_ranges(const std::vector<int>& seg, int grid, std::vector<int>* r) {
+    int64_t total = 0;
+    for (const int z : seg) total += z;
+    int64_t lo = kTableTiles + 1, hi = kTableTiles + total + 1;
+    while (lo < hi) {
+        const int64_t mid = lo + (hi - lo) / 2;
+        if (pack_ranges(seg, mid, nullptr) <= grid) hi = mid;
+        else lo = mid + 1;
+    }
+    std::vector<int> starts;
+    pack_ranges(seg, lo, &starts);
+    r->assign(grid + 1, (int)total);
+    for (size_t c = 0; c < starts.size() && (int)c < grid; ++c) (*r)[c] = starts[c];
+    (*r)[0] = 0;
+}
+
 // Host-side description of a chain (validated) and its workspace layout.
 struct StoreArr {
     StoreD s[kLutMaxStores];
 };
 
 int chain_layout(const StoreArr* st, const int* counts, const int* feeds, int n_steps,
-                 int grid, std::vector<ChainStepD>* out_steps, ChainHeaderD* hdr, int64_t* ws_bytes) {
+                 int grid, std::vector<ChainStepD>* out_steps, ChainHeaderD* hdr, int64_t* ws_bytes,
+                 std::vector<int>* out_ranges) {
     if (n_steps < 1) return set_error(EPQ_EINVAL, "chain: n_steps=%d", n_steps);
     std::vector<ChainStepD> steps(n_steps);
     int64_t part_floats = 0;
@@ -571,7 +631,6 @@ int chain_layout(const StoreArr* st, const int* counts, const int* feeds, int n_
         D.k = (int)st[j].s[0].k;
         D.kpos = (int)(st[j].s[0].k / 4);
         D.total_tiles = (int)tiles;
-        D.tiles_per_cta = (int)cdiv(tiles, grid);
         if (j > 0 && st[j - 1].s[feeds[j - 1]].n != st[j].s[0].k)
             return set_error(EPQ_ESHAPE, "chain: step %d input width %lld != step %d feed output %lld", j,
                              (long long)st[j].s[0].k, j - 1, (long long)st[j - 1].s[feeds[j - 1]].n);
@@ -582,7 +641,19 @@ int chain_layout(const StoreArr* st, const int* counts, const int* feeds, int n_
     H.grid = grid;
     H.part_floats = part_floats;
     H.steps_off = 256;
-    H.ctr_off = al256(H.steps_off + (int64_t)sizeof(ChainStepD) * n_steps);
+    const int64_t ranges_off = al256(H.steps_off + (int64_t)sizeof(ChainStepD) * n_steps);
+    for (int j = 0; j < n_steps; ++j) steps[j].range_off = ranges_off + 4 * (int64_t)(grid + 1) * j;
+    if (out_ranges) {
+        out_ranges->clear();
+        for (int j = 0; j < n_steps; ++j) {
+            std::vector<int> seg, r;
+            for (int i = 0; i < steps[j].count; ++i)
+                for (int g = 0; g < steps[j].st[i].ng; ++g) seg.push_back(steps[j].st[i].rb);
+            balance_ranges(seg, grid, &r);
+            out_ranges->insert(out_ranges->end(), r.begin(), r.end());
+        }
+    }
+    H.ctr_off = al256(ranges_off + 4 * (int64_t)(grid + 1) * n_steps);
     H.part_off0 = al256(H.ctr_off + 4 * (n_steps + 2));
     H.part_off1 = al256(H.part_off0 + 4 * part_floats);
     *ws_bytes = al256(H.part_off1 + 4 * part_floats);
@@ -612,10 +683,13 @@ int chain_grid(int* grid) {
     return EPQ_OK;
 }
 
-int chain_write(const std::vector<ChainStepD>& steps, const ChainHeaderD& H, void* ws, cudaStream_t st) {
+int chain_write(const std::vector<ChainStepD>& steps, const std::vector<int>& ranges, const ChainHeaderD& H,
+                void* ws, cudaStream_t st) {
     std::vector<uint8_t> host(H.part_off0, 0);
     memcpy(host.data(), &H, sizeof(H));
     memcpy(host.data() + H.steps_off, steps.data(), sizeof(ChainStepD) * steps.size());
+    if (!steps.empty())
+        memcpy(host.data() + steps[0].range_off, ranges.data(), sizeof(int) * ranges.size());
     // counters (and the run generation) start at zero
     if (cudaMemcpyAsync(ws, host.data(), host.size(), cudaMemcpyHostToDevice, st) != cudaSuccess)
         return check_launch("chain: write descriptors");
@@ -665,7 +739,7 @@ int epq_chain_workspace_bytes(const epq_chain_step* steps, int32_t n_steps, int6
     rc = chain_grid(&grid);
     if (rc) return rc;
     ChainHeaderD H;
-    return chain_layout(st.data(), counts.data(), feeds.data(), n_steps, grid, nullptr, &H, bytes);
+    return chain_layout(st.data(), counts.data(), feeds.data(), n_steps, grid, nullptr, &H, bytes, nullptr);
 }
 
 int epq_chain_prepare(const epq_chain_step* steps, int32_t n_steps, void* workspace,
@@ -682,14 +756,15 @@ int epq_chain_prepare(const epq_chain_step* steps, int32_t n_steps, void* worksp
     rc = chain_grid(&grid);
     if (rc) return rc;
     std::vector<ChainStepD> desc;
+    std::vector<int> ranges;
     ChainHeaderD H;
     int64_t need = 0;
-    rc = chain_layout(st.data(), counts.data(), feeds.data(), n_steps, grid, &desc, &H, &need);
+    rc = chain_layout(st.data(), counts.data(), feeds.data(), n_steps, grid, &desc, &H, &need, &ranges);
     if (rc) return rc;
     if (workspace_bytes < need)
         return set_error(EPQ_EWORKSPACE, "chain_prepare: workspace of %lld bytes needed, %lld given",
                          (long long)need, (long long)workspace_bytes);
-    return chain_write(desc, H, workspace, static_cast<cudaStream_t>(stream));
+    return chain_write(desc, ranges, H, workspace, static_cast<cudaStream_t>(stream));
 }
 
 int epq_chain_run(const void* workspace, const void* x, int32_t x_dtype, void* out, int32_t out_dtype,
