@@ -84,6 +84,7 @@ constexpr uint32_t kXsOff = 8192;      // from base: 2 x codebook [1024] fp32 be
                                        // 2 x activation slice sums [kXGroups][128] fp32
 constexpr uint32_t kBarOff = kXsOff + 2 * kXGroups * 512;  // from base: full[kRing], empty[kRing]
 constexpr uint32_t kMiscOff = kBarOff + 128;               // from base: broadcast words
+constexpr uint32_t kDescOff = kMiscOff + 64;               // from base: 3 step descriptors (ring)
 constexpr uint32_t kLowStages = 26624; // window address of stage 0
 constexpr uint32_t kTBase = 65536;     // window address of T (low 16 bits zero for the PRMT trick)
 constexpr uint32_t kHighStages = 131072;   // window address of stages 1..2
@@ -178,20 +179,37 @@ __device__ __forceinline__ void grid_wait(const unsigned* c, unsigned target) {
     atomicExch(&g_chain_error, 1);
 }
 
-// Chunk iterator over a CTA's tile range of one step (identical in producer and consumers).
+// Chunk iterator over a CTA's tile range of one step (identical in producer and
+// consumers).  Tiles run (store, group, row block); a chunk never crosses a
+// (store, group) boundary.  The position is kept incrementally (one division
+// per step, at the start).
 struct ChunkIt {
-    int t, t_end;
-    __device__ bool next(const ChainStepD& S, int& si, int& g, int& rb0, int& nt) {
-        if (t >= t_end) return false;
+    int t, t_end, si, g, rb;
+    __device__ void start(const ChainStepD& S, int t0, int t1) {
+        t = t0;
+        t_end = t1;
         si = 0;
-        while (si + 1 < S.count && t >= S.st[si + 1].tile0) ++si;
-        const ChainStoreD& C = S.st[si];
-        const int local = t - C.tile0;
-        g = local / C.rb;
-        rb0 = local - g * C.rb;
-        const int seg_end = min(t_end, C.tile0 + (g + 1) * C.rb);
-        nt = min(kChunkTiles, seg_end - t);
+        while (si + 1 < S.count && t0 >= S.st[si + 1].tile0) ++si;
+        const int local = t0 - S.st[si].tile0;
+        g = local / S.st[si].rb;
+        rb = local - g * S.st[si].rb;
+    }
+    __device__ bool next(const ChainStepD& S, int& csi, int& cg, int& rb0, int& nt) {
+        if (t >= t_end) return false;
+        const int crb = S.st[si].rb;
+        csi = si;
+        cg = g;
+        rb0 = rb;
+        nt = min(kChunkTiles, min(t_end - t, crb - rb));
         t += nt;
+        rb += nt;
+        if (rb == crb) {
+            rb = 0;
+            if (++g == S.st[si].ng) {
+                g = 0;
+                ++si;
+            }
+        }
         return true;
     }
 };
@@ -200,7 +218,8 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
                                                             int x_dtype, void* out, int out_dtype) {
     extern __shared__ __align__(128) uint8_t smem[];
     const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
-    if (base + kMiscOff + 64 > kLowStages || (int)gridDim.x != reinterpret_cast<const int*>(ws)[1]) {
+    if (base + kDescOff + 3 * (uint32_t)sizeof(ChainStepD) > kLowStages ||
+        (int)gridDim.x != reinterpret_cast<const int*>(ws)[1]) {
         // placement the addresses below rely on, or a grid other than the one
         // the descriptors were built for
         if (threadIdx.x == 0) atomicExch(&g_chain_error, 2);
@@ -234,7 +253,8 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
         for (int j = 0; j < n_steps; ++j) {
             const ChainStepD& S = steps[j];
             const int* rg = reinterpret_cast<const int*>(ws + S.range_off);
-            ChunkIt it{rg[blockIdx.x], rg[blockIdx.x + 1]};
+            ChunkIt it;
+            it.start(S, rg[blockIdx.x], rg[blockIdx.x + 1]);
             int si, g, rb0, nt;
             while (it.next(S, si, g, rb0, nt)) {
                 const int stage = i % kRing;
@@ -268,11 +288,19 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
     // each store of the step), so building a table never waits on DRAM.
     uint2 cb_raw[kLutMaxStores];
     float2 cb_cur[kLutMaxStores];
+    // Step descriptors are read from a 3-slot ring in shared memory (slot j % 3):
+    // each is loaded into registers two steps ahead and stored one step ahead, so
+    // no consumer waits on the workspace for them.
+    const ChainStepD* sdesc = reinterpret_cast<const ChainStepD*>(smem + kDescOff);
+    uint32_t* sdw = reinterpret_cast<uint32_t*>(smem + kDescOff);
+    constexpr int kDescWords = (int)(sizeof(ChainStepD) / 4);
+    static_assert(sizeof(ChainStepD) % 4 == 0 && kDescWords <= kConsumers, "descriptor words");
+    const uint32_t* gsteps = reinterpret_cast<const uint32_t*>(steps);
     auto cb_prefetch = [&](int jj) {
 #pragma unroll
         for (int q = 0; q < kLutMaxStores; ++q) cb_raw[q] = make_uint2(0u, 0u);
         if (jj >= n_steps) return;
-        const ChainStepD& N = steps[jj];
+        const ChainStepD& N = sdesc[jj % 3];
         const int e = 2 * threadIdx.x;
 #pragma unroll
         for (int q = 0; q < kLutMaxStores; ++q) {
@@ -287,7 +315,7 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
         }
     };
     auto cb_promote = [&](int jj) {
-        const ChainStepD& N = steps[jj];
+        const ChainStepD& N = sdesc[jj % 3];
 #pragma unroll
         for (int q = 0; q < kLutMaxStores; ++q) {
             const int dt = q < N.count ? N.st[q].cb_dtype : EPQ_F32;
@@ -302,26 +330,39 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
             }
         }
     };
+    uint32_t dreg = 0;
+    if (threadIdx.x < kDescWords) {
+        sdw[threadIdx.x] = gsteps[threadIdx.x];
+        if (n_steps > 1) sdw[kDescWords + threadIdx.x] = gsteps[kDescWords + threadIdx.x];
+        if (n_steps > 2) dreg = __ldg(gsteps + 2 * kDescWords + threadIdx.x);
+    }
+    consumers_sync();
     cb_prefetch(0);
 
     int i = 0, slot = 0;
     for (int j = 0; j < n_steps; ++j) {
-        const ChainStepD& S = steps[j];
+        const ChainStepD& S = sdesc[j % 3];
         cb_promote(j);
-        cb_prefetch(j + 1);
+        if (j >= 1 && j + 1 < n_steps && threadIdx.x < kDescWords) {
+            // step j+1 into the slot of step j-2 (no longer read); published by the barrier below
+            sdw[((j + 1) % 3) * kDescWords + threadIdx.x] = dreg;
+            if (j + 2 < n_steps) dreg = __ldg(gsteps + (j + 2) * kDescWords + threadIdx.x);
+        }
         if (j > 0) {
             if (threadIdx.x == 0) grid_wait(&ctr[j - 1], target);   // every CTA finished step j-1
             consumers_sync();
         }
+        cb_prefetch(j + 1);
         // Input of this step: x0 (step 0) or the partials of step j-1's feed store.
-        const ChainStepD* P = j > 0 ? &steps[j - 1] : nullptr;
+        const ChainStepD* P = j > 0 ? &sdesc[(j - 1) % 3] : nullptr;
         const float* pin = j > 0 ? part[(j - 1) & 1] + P->st[P->feed].part_off : nullptr;
         const int64_t pin_stride = j > 0 ? (int64_t)P->st[P->feed].rb * 16 : 0;
         const int pin_ng = j > 0 ? P->st[P->feed].ng : 0;
         float* pout = part[j & 1];
 
         const int* rg = reinterpret_cast<const int*>(ws + S.range_off);
-        ChunkIt it{rg[blockIdx.x], rg[blockIdx.x + 1]};
+        ChunkIt it;
+        it.start(S, rg[blockIdx.x], rg[blockIdx.x + 1]);
         int si, g, rb0, nt, cur_s = -1, cur_g = -1;
         while (it.next(S, si, g, rb0, nt)) {
             const ChainStoreD& C = S.st[si];
