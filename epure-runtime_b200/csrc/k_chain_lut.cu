@@ -338,6 +338,13 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
     }
     consumers_sync();
     cb_prefetch(0);
+    // This CTA's tile range of the current and of the next step (loaded a step ahead).
+    int rcur0, rcur1, rnext0 = 0, rnext1 = 0;
+    {
+        const int* rg = reinterpret_cast<const int*>(ws + sdesc[0].range_off);
+        rcur0 = __ldg(rg + blockIdx.x);
+        rcur1 = __ldg(rg + blockIdx.x + 1);
+    }
 
     int i = 0, slot = 0;
     for (int j = 0; j < n_steps; ++j) {
@@ -353,6 +360,11 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
             consumers_sync();
         }
         cb_prefetch(j + 1);
+        if (j + 1 < n_steps) {
+            const int* rgn = reinterpret_cast<const int*>(ws + sdesc[(j + 1) % 3].range_off);
+            rnext0 = __ldg(rgn + blockIdx.x);
+            rnext1 = __ldg(rgn + blockIdx.x + 1);
+        }
         // Input of this step: x0 (step 0) or the partials of step j-1's feed store.
         const ChainStepD* P = j > 0 ? &sdesc[(j - 1) % 3] : nullptr;
         const float* pin = j > 0 ? part[(j - 1) & 1] + P->st[P->feed].part_off : nullptr;
@@ -360,9 +372,8 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
         const int pin_ng = j > 0 ? P->st[P->feed].ng : 0;
         float* pout = part[j & 1];
 
-        const int* rg = reinterpret_cast<const int*>(ws + S.range_off);
         ChunkIt it;
-        it.start(S, rg[blockIdx.x], rg[blockIdx.x + 1]);
+        it.start(S, rcur0, rcur1);
         int si, g, rb0, nt, cur_s = -1, cur_g = -1;
         while (it.next(S, si, g, rb0, nt)) {
             const ChainStoreD& C = S.st[si];
@@ -512,6 +523,8 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
             if (lane == 0) mbar_arrive(bar_empty + 8 * stage);
             ++i;
         }
+        rcur0 = rnext0;
+        rcur1 = rnext1;
         consumers_sync();                  // all of this CTA's partials for step j are written
         if (threadIdx.x == 0) {
             __threadfence();
