@@ -9,11 +9,10 @@
 // kernel that streams that much spends a fixed ~3 us filling and draining the
 // memory pipeline, which for 128 dependent launches per token costs more than
 // the whole HBM roofline.  Here a producer warp per SM streams the weights of
-// every step through a 6-stage TMA ring (cp.async.bulk + mbarriers, each copy to
+// every step through a 3-stage TMA ring (cp.async.bulk + mbarriers, each copy to
 // this CTA only) without ever waiting for activations -- weights are static -- so
-// HBM keeps streaming across step boundaries; only the consumers wait for the
-// previous step to finish (a grid barrier: a per-step arrival counter in the
-// workspace, bounded spin).
+// HBM keeps streaming across step boundaries; only the consumers wait for their
+// inputs from the previous step (see "Synchronisation" below).
 //
 // Inner loop (per index byte: one PRMT, one LDS.32, one FADD).  For one scale
 // group (32 index positions) the consumers build an activation table
@@ -23,6 +22,14 @@
 // (16 rows x 32 positions per 512-byte tile); a team of 8 lanes owns a tile,
 // each lane 4 positions (rotated per team: the 32 lanes of a warp always hit 32
 // different banks), and a 3-step butterfly leaves each lane with 2 row sums.
+//
+// Synchronisation without a grid barrier on the critical path.  Partial sums
+// are written as 8-byte (value, step tag) elements into a ring of three
+// buffers; a consumer polls exactly the partials its input slice needs until
+// they carry the previous step's tag (an aligned 8-byte access is single-copy
+// atomic), so a step starts as soon as its own inputs exist.  A per-step
+// arrival counter, bumped (relaxed) when a CTA has consumed its inputs, is
+// checked only before a CTA first writes a buffer again, two steps later.
 //
 // Split over k without a reduction tail.  A step's tiles are ordered (store,
 // group, row block) and each CTA takes a contiguous range, chosen on the host
@@ -34,7 +41,7 @@
 // last step all CTAs reduce the final output rows.  Partial buffers ping-pong
 // between steps.
 //
-// Safety: every mbarrier wait and every grid-barrier spin is bounded; a wait
+// Safety: every mbarrier wait, tag poll and counter spin is bounded; a wait
 // that gives up sets g_chain_error (read by epq_device_error) and the kernel
 // runs to completion.  The launch is cooperative, so all CTAs are co-resident.
 #include <climits>
@@ -64,8 +71,8 @@ struct ChainStepD {
 
 struct ChainHeaderD {
     int n_steps, grid;
-    int64_t part_floats;              // floats per partial buffer
-    int64_t steps_off, ctr_off, part_off0, part_off1;   // byte offsets in the workspace
+    int64_t part_floats;              // elements per partial buffer (8 bytes each: value, tag)
+    int64_t steps_off, ctr_off, part_off0, part_off1, part_off2;   // byte offsets in the workspace
 };
 
 namespace {
@@ -162,6 +169,29 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
         "l"(src), "r"(bytes), "r"(bar)
         : "memory");
 }
+// Partial sums travel as 8-byte elements (fp32 value, 32-bit step tag); an aligned
+// 8-byte access is single-copy atomic, so a reader that sees the expected tag sees
+// the value written with it.
+__device__ __forceinline__ uint64_t tagged(float v, uint32_t tag) {
+    return (uint64_t)__float_as_uint(v) | ((uint64_t)tag << 32);
+}
+__device__ __forceinline__ ulonglong2 ldcg_u64x2(const uint64_t* p) {
+    ulonglong2 v;
+    asm volatile("ld.global.cg.v2.u64 {%0,%1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint64_t ldcg_u64(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.global.cg.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void stg_u64x2(uint64_t* p, uint64_t a, uint64_t b) {
+    asm volatile("st.global.v2.u64 [%0], {%1,%2};" ::"l"(p), "l"(a), "l"(b) : "memory");
+}
+__device__ __forceinline__ uint32_t tag_of(uint64_t v) { return (uint32_t)(v >> 32); }
+__device__ __forceinline__ float val_of(uint64_t v) { return __uint_as_float((uint32_t)v); }
+constexpr uint32_t kTagSpinLimit = 1u << 22;   // polls of one not-yet-written partial
+
 __device__ __forceinline__ void consumers_sync() {
     asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory");
 }
@@ -228,8 +258,9 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
     const ChainHeaderD& H = *reinterpret_cast<const ChainHeaderD*>(ws);
     const ChainStepD* steps = reinterpret_cast<const ChainStepD*>(ws + H.steps_off);
     unsigned* ctr = reinterpret_cast<unsigned*>(const_cast<uint8_t*>(ws) + H.ctr_off);  // [n_steps] + done + gen
-    float* part[2] = {reinterpret_cast<float*>(const_cast<uint8_t*>(ws) + H.part_off0),
-                      reinterpret_cast<float*>(const_cast<uint8_t*>(ws) + H.part_off1)};
+    uint64_t* part[3] = {reinterpret_cast<uint64_t*>(const_cast<uint8_t*>(ws) + H.part_off0),
+                         reinterpret_cast<uint64_t*>(const_cast<uint8_t*>(ws) + H.part_off1),
+                         reinterpret_cast<uint64_t*>(const_cast<uint8_t*>(ws) + H.part_off2)};
     const int n_steps = H.n_steps;
     const int G = gridDim.x;
     const uint32_t bar_full = base + kBarOff, bar_empty = bar_full + 8 * kRing;
@@ -246,6 +277,8 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
     }
     __syncthreads();
     const unsigned target = (misc[0] + 1u) * (unsigned)G;
+    // Step j's partials carry tag gen * n_steps + j + 1 (never 0: buffers start zeroed).
+    const unsigned tag_base = misc[0] * (unsigned)n_steps + 1u;
 
     if (warp == kConsumerWarps) {
         // ---------------- producer: stream every step's tiles into the ring ----------------
@@ -355,10 +388,7 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
             sdw[((j + 1) % 3) * kDescWords + threadIdx.x] = dreg;
             if (j + 2 < n_steps) dreg = __ldg(gsteps + (j + 2) * kDescWords + threadIdx.x);
         }
-        if (j > 0) {
-            if (threadIdx.x == 0) grid_wait(&ctr[j - 1], target);   // every CTA finished step j-1
-            consumers_sync();
-        }
+        if (j > 0) consumers_sync();   // publishes the descriptor slot written above
         cb_prefetch(j + 1);
         if (j + 1 < n_steps) {
             const int* rgn = reinterpret_cast<const int*>(ws + sdesc[(j + 1) % 3].range_off);
@@ -367,10 +397,12 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
         }
         // Input of this step: x0 (step 0) or the partials of step j-1's feed store.
         const ChainStepD* P = j > 0 ? &sdesc[(j - 1) % 3] : nullptr;
-        const float* pin = j > 0 ? part[(j - 1) & 1] + P->st[P->feed].part_off : nullptr;
+        const uint64_t* pin = j > 0 ? part[(j - 1) % 3] + P->st[P->feed].part_off : nullptr;
+        const uint32_t want = tag_base + (uint32_t)(j - 1);
         const int64_t pin_stride = j > 0 ? (int64_t)P->st[P->feed].rb * 16 : 0;
         const int pin_ng = j > 0 ? P->st[P->feed].ng : 0;
-        float* pout = part[j & 1];
+        uint64_t* pout = part[j % 3];
+        const uint32_t tag = tag_base + (uint32_t)j;
 
         ChunkIt it;
         it.start(S, rcur0, rcur1);
@@ -407,15 +439,39 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
                                 v = make_float4(load_f(x0, x_dtype, c), load_f(x0, x_dtype, c + 1),
                                                 load_f(x0, x_dtype, c + 2), load_f(x0, x_dtype, c + 3));
                         } else {
-                            const float4* col = reinterpret_cast<const float4*>(pin + c);
-                            const int64_t st4 = pin_stride >> 2;
-#pragma unroll 8
-                            for (int gp = part; gp < pin_ng; gp += 16) {
-                                const float4 u = __ldcg(col + gp * st4);
-                                v.x += u.x;
-                                v.y += u.y;
-                                v.z += u.z;
-                                v.w += u.w;
+                            // Poll the 4 values of each input slice until they carry step
+                            // j-1's tag (4 slices in flight per round; bounded).
+                            const uint64_t* col = pin + c;
+                            for (int gp0 = part; gp0 < pin_ng; gp0 += 64) {
+                                ulonglong2 a[4], b[4];
+#pragma unroll
+                                for (int q = 0; q < 4; ++q) {
+                                    const int gp = gp0 + 16 * q;
+                                    if (gp < pin_ng) {
+                                        a[q] = ldcg_u64x2(col + gp * pin_stride);
+                                        b[q] = ldcg_u64x2(col + gp * pin_stride + 2);
+                                    }
+                                }
+#pragma unroll
+                                for (int q = 0; q < 4; ++q) {
+                                    const int gp = gp0 + 16 * q;
+                                    if (gp >= pin_ng) continue;
+                                    uint32_t spins = 0;
+                                    while ((tag_of(a[q].x) != want) | (tag_of(a[q].y) != want) |
+                                           (tag_of(b[q].x) != want) | (tag_of(b[q].y) != want)) {
+                                        if (++spins > kTagSpinLimit ||
+                                            *reinterpret_cast<volatile int*>(&g_chain_error)) {
+                                            atomicExch(&g_chain_error, 1);
+                                            break;
+                                        }
+                                        a[q] = ldcg_u64x2(col + gp * pin_stride);
+                                        b[q] = ldcg_u64x2(col + gp * pin_stride + 2);
+                                    }
+                                    v.x += val_of(a[q].x);
+                                    v.y += val_of(a[q].y);
+                                    v.z += val_of(b[q].x);
+                                    v.w += val_of(b[q].y);
+                                }
                             }
                         }
                     }
@@ -428,6 +484,9 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
                     }
                     if (lane < 8) reinterpret_cast<float4*>(xs)[(warp >> 2) * 32 + c4] = v;
                 }
+                // This step overwrites buffer j % 3, last read during step j-2's staging:
+                // before the first write, every CTA must have finished step j-2.
+                if (cur_s < 0 && j >= 3 && threadIdx.x == 0) grid_wait(&ctr[j - 2], target);
                 cur_s = si;
                 cur_g = g;
                 consumers_sync();
@@ -516,8 +575,8 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
                 const uint32_t sa = sdst + kStageIdx + tile * 16 * esz + 2 * tl * esz;
                 const float s0 = lds_scale(sa, f32), s1 = lds_scale(sa + esz, f32);
                 const int64_t row = (int64_t)(rb0 + tile) * 16 + 2 * tl;
-                *reinterpret_cast<float2*>(pout + C.part_off + (int64_t)g * C.rb * 16 + row) =
-                    make_float2(a3[0] * s0, a3[1] * s1);
+                stg_u64x2(pout + C.part_off + (int64_t)g * C.rb * 16 + row, tagged(a3[0] * s0, tag),
+                          tagged(a3[1] * s1, tag));
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(bar_empty + 8 * stage);
@@ -526,19 +585,18 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
         rcur0 = rnext0;
         rcur1 = rnext1;
         consumers_sync();                  // all of this CTA's partials for step j are written
-        if (threadIdx.x == 0) {
-            __threadfence();
-            atomicAdd(&ctr[j], 1u);
-        }
+        // This CTA is done reading step j-1's partials (their values have been
+        // consumed before the barrier above); no fence is needed for that.
+        if (threadIdx.x == 0) atomicAdd(&ctr[j], 1u);
     }
 
-    // Final output: the last step's feed store, rows split over the CTAs.
-    if (threadIdx.x == 0) grid_wait(&ctr[n_steps - 1], target);
-    consumers_sync();
+    // Final output: the last step's feed store, rows split over the CTAs (each
+    // partial polled until it carries the last step's tag).
     {
         const ChainStepD& L = steps[n_steps - 1];
         const ChainStoreD& F = L.st[L.feed];
-        const float* pl = part[(n_steps - 1) & 1] + F.part_off;
+        const uint64_t* pl = part[(n_steps - 1) % 3] + F.part_off;
+        const uint32_t want = tag_base + (uint32_t)(n_steps - 1);
         const int64_t stride = (int64_t)F.rb * 16;
         const int r0 = (int)((int64_t)F.n * blockIdx.x / G), r1 = (int)((int64_t)F.n * (blockIdx.x + 1) / G);
         // 8 lanes per row, each adding every 8th slice; a 3-step shuffle combines them.
@@ -547,8 +605,18 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
             const int r = rbase + (threadIdx.x >> 3);
             float v = 0.f;
             if (r < r1) {
-#pragma unroll 4
-                for (int gg = sub8; gg < F.ng; gg += 8) v += __ldcg(pl + gg * stride + r);
+                for (int gg = sub8; gg < F.ng; gg += 8) {
+                    uint64_t e = ldcg_u64(pl + gg * stride + r);
+                    uint32_t spins = 0;
+                    while (tag_of(e) != want) {
+                        if (++spins > kTagSpinLimit || *reinterpret_cast<volatile int*>(&g_chain_error)) {
+                            atomicExch(&g_chain_error, 1);
+                            break;
+                        }
+                        e = ldcg_u64(pl + gg * stride + r);
+                    }
+                    v += val_of(e);
+                }
             }
             v += __shfl_xor_sync(0xffffffffu, v, 1);
             v += __shfl_xor_sync(0xffffffffu, v, 2);
@@ -709,8 +777,9 @@ int chain_layout(const StoreArr* st, const int* counts, const int* feeds, int n_
     }
     H.ctr_off = al256(ranges_off + 4 * (int64_t)(grid + 1) * n_steps);
     H.part_off0 = al256(H.ctr_off + 4 * (n_steps + 2));
-    H.part_off1 = al256(H.part_off0 + 4 * part_floats);
-    *ws_bytes = al256(H.part_off1 + 4 * part_floats);
+    H.part_off1 = al256(H.part_off0 + 8 * part_floats);
+    H.part_off2 = al256(H.part_off1 + 8 * part_floats);
+    *ws_bytes = al256(H.part_off2 + 8 * part_floats);
     *hdr = H;
     if (out_steps) *out_steps = std::move(steps);
     return EPQ_OK;
@@ -747,6 +816,10 @@ int chain_write(const std::vector<ChainStepD>& steps, const std::vector<int>& ra
     // counters (and the run generation) start at zero
     if (cudaMemcpyAsync(ws, host.data(), host.size(), cudaMemcpyHostToDevice, st) != cudaSuccess)
         return check_launch("chain: write descriptors");
+    // partial buffers start with tag 0, which no step uses
+    const int64_t part_end = al256(H.part_off2 + 8 * H.part_floats);
+    if (cudaMemsetAsync(static_cast<uint8_t*>(ws) + H.part_off0, 0, part_end - H.part_off0, st) != cudaSuccess)
+        return check_launch("chain: clear partial buffers");
     if (cudaStreamSynchronize(st) != cudaSuccess) return check_launch("chain: write descriptors");
     return EPQ_OK;
 }
