@@ -652,7 +652,7 @@ static int64_t al256(int64_t v) { return (v + 255) & ~int64_t(255); }
 // The ranges stay contiguous in (store, group, row block) order and minimise the
 // largest per-CTA cost (binary search on the cost; greedy packing); CTAs left
 // over get empty ranges.
-constexpr int kTableTiles = 96;
+constexpr int kTableTiles = 160;
 
 static int pack_ranges(const std::vector<int>& seg, int64_t cap, std::vector<int>* starts) {
     int ctas = 0;
