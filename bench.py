@@ -64,14 +64,15 @@ WORKLOAD = "llama3-8b packed linears, batch-1 decode token (224 linears)"
 #     (profiles/gemv_mma_kernel_llama3-8b_gateup_b1.md): 31,236,352 B of
 #     dram__bytes_read.sum + dram__bytes_write.sum against 31,264,768 B.
 #   chain: chain_kernel on a 4-layer Llama-3-8B chain
-#     (profiles/chain_kernel_llama3-8b_decode_b1.md): 232,160,256 B read +
-#     5,267,712 B written against 232,349,696 algorithmic bytes.
+#     (profiles/chain_kernel_llama3-8b_decode_b1.md): 232,937,728 B read +
+#     24,145,664 B written against 232,349,696 algorithmic bytes.
 NCU_TRAFFIC_RATIO = {"per-linear": 31236352 / 31264768,
-                     "chain": (232160256 + 5267712) / 232349696}
+                     "chain": (232937728 + 24145664) / 232349696}
 TRAFFIC_NOTE = {"per-linear": "per step, scaled from one ncu capture of the gate+up launch "
                               "(traffic/algorithmic = 0.999)",
                 "chain": "per step, scaled from one ncu capture of a 4-layer chain "
-                         "(traffic/algorithmic = 1.022; the extra bytes are split-k partials)"}
+                         "(traffic/algorithmic = 1.106; the extra bytes are the tagged split-k "
+                         "partial sums written back to DRAM)"}
 
 
 def _peaks():
