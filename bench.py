@@ -31,8 +31,10 @@ Other workloads (not the headline; each prints its own metric):
   --model qwen3-1.7b|llama3-8b|llama3-70b picks the decoder shapes;
   --layers L keeps the first L layers (small cases for profiling);
   --tp (with N > 1): one model tensor-parallel over the N GPUs (column-parallel
-      q/k/v and gate/up, row-parallel o and down, an NCCL all-reduce after o and
-      after down), one token stream, strong scaling;
+      q/k/v and gate/up, row-parallel o and down), one token stream, strong
+      scaling; in the default chain mode the all-reduce of o and down happens
+      inside the persistent kernel over NVLink, with --mode per-linear it is an
+      NCCL all-reduce after each row-parallel launch;
   --fallback also times the reference's bf16 fallback path on the GPU
       (F.linear(x, materialize(bf16)) store by store, torch ops) on the same step.
 
@@ -404,17 +406,22 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.set_device(dev)
     shapes = synthetic.SHAPES[args.model]
     use_tp = args.tp and world > 1
-    chain = args.mode == "chain" and not use_tp
+    chain = args.mode == "chain"
     prefill = args.mode == "prefill"
     m = args.tokens if prefill else 1
     if use_tp:
         # every rank draws its own shards of one model (same seed on every rank)
         stack = synthetic.LinearStack(shapes, layers=args.layers, device=dev, seed=1000,
-                                      gpu_layout="mma16", tp=(rank, world))
+                                      gpu_layout="tiled" if chain else "mma16", tp=(rank, world))
     else:
         stack = synthetic.LinearStack(shapes, layers=args.layers, device=dev, seed=1000 * rank,
                                       gpu_layout="tiled" if chain else "mma16")
-    if use_tp:
+    if use_tp and chain:
+        from epure.tp import TPChainedLinearStack
+        runner = TPChainedLinearStack(stack, dtype=torch.bfloat16, device=dev).capture()
+        kernel_name = (f"chain_kernel on 1/{world} shards, all-reduce of o and down inside the "
+                       "kernel (peer NVLink loads)")
+    elif use_tp:
         from epure.tp import TPLinearStack
         runner = TPLinearStack(stack.blocks, m=m, dtype=torch.bfloat16, device=dev).capture()
         kernel_name = (("gemm_tc_kernel" if prefill else "gemv_mma_kernel") +
@@ -537,7 +544,7 @@ def run_ours(args, rank, world, local_rank):
             "dtype": "bf16",
             "data": "synthetic",
             "config": {"workload": workload,
-                       "mode": ("tp-" + ("prefill" if prefill else "per-linear")) if use_tp else args.mode,
+                       "mode": ("tp-" + args.mode) if use_tp else args.mode,
                        "global_batch": streams * m,
                        "seq_len": m,
                        "parallelism": (f"tp{world}" if use_tp else

@@ -65,14 +65,22 @@ struct ChainStoreD {
 struct ChainStepD {
     ChainStoreD st[kLutMaxStores];
     int count, feed, k, kpos;
-    int total_tiles, pad0;
+    int total_tiles;
+    int remote;           // tensor parallel: this step's input is summed over every rank
     int64_t range_off;    // workspace offset of int32 [grid + 1]: CTA c takes tiles [r[c], r[c+1])
 };
+
+constexpr int kMaxTp = 8;
 
 struct ChainHeaderD {
     int n_steps, grid;
     int64_t part_floats;              // elements per partial buffer (8 bytes each: value, tag)
     int64_t steps_off, ctr_off, part_off0, part_off1, part_off2;   // byte offsets in the workspace
+    int64_t xred_off, xred_elems;     // 3 buffers of per-rank input-slice sums (tensor parallel)
+    int64_t xfin_off, xfin_elems;     // per-rank sums of the final output rows (tensor parallel)
+    int tp_world, tp_rank;            // 1, 0 without tensor parallelism
+    int final_remote, pad;
+    int64_t peer_ws[kMaxTp];          // every rank's workspace as mapped in this process
 };
 
 namespace {
@@ -188,6 +196,19 @@ __device__ __forceinline__ uint64_t ldcg_u64(const uint64_t* p) {
 __device__ __forceinline__ void stg_u64x2(uint64_t* p, uint64_t a, uint64_t b) {
     asm volatile("st.global.v2.u64 [%0], {%1,%2};" ::"l"(p), "l"(a), "l"(b) : "memory");
 }
+__device__ __forceinline__ ulonglong2 ldsys_u64x2(const uint64_t* p) {   // peer or own memory, no caching
+    ulonglong2 v;
+    asm volatile("ld.volatile.global.v2.u64 {%0,%1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint64_t ldsys_u64(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void red_sys_add(unsigned* p, unsigned v) {
+    asm volatile("red.relaxed.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 __device__ __forceinline__ uint32_t tag_of(uint64_t v) { return (uint32_t)(v >> 32); }
 __device__ __forceinline__ float val_of(uint64_t v) { return __uint_as_float((uint32_t)v); }
 constexpr uint32_t kTagSpinLimit = 1u << 22;   // polls of one not-yet-written partial
@@ -197,7 +218,7 @@ __device__ __forceinline__ void consumers_sync() {
 }
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
     unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
 // Grid barrier: until every CTA has counted step `c` for this run (bounded).
@@ -276,7 +297,8 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
         misc[0] = *reinterpret_cast<volatile unsigned*>(&ctr[n_steps + 1]);   // run generation
     }
     __syncthreads();
-    const unsigned target = (misc[0] + 1u) * (unsigned)G;
+    const int world = H.tp_world, my_rank = H.tp_rank;
+    const unsigned target = (misc[0] + 1u) * (unsigned)G * (unsigned)world;
     // Step j's partials carry tag gen * n_steps + j + 1 (never 0: buffers start zeroed).
     const unsigned tag_base = misc[0] * (unsigned)n_steps + 1u;
 
@@ -487,9 +509,62 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
                 // This step overwrites buffer j % 3, last read during step j-2's staging:
                 // before the first write, every CTA must have finished step j-2.
                 if (cur_s < 0 && j >= 3 && threadIdx.x == 0) grid_wait(&ctr[j - 2], target);
+                const bool new_g = g != cur_g;
                 cur_s = si;
                 cur_g = g;
                 consumers_sync();
+                if (j > 0 && S.remote && new_g) {
+                    // Tensor parallel: this rank's sum of the slice is published (tagged) in
+                    // xred; every rank adds all ranks' sums in rank order, so all ranks build
+                    // the same table from the same x.
+                    if (warp == 0) {
+                        float* xsl = xs_buf + xsp * (kXGroups * 128);
+                        const float4* x4 = reinterpret_cast<const float4*>(xsl);
+                        float4 loc = x4[lane];
+#pragma unroll
+                        for (int h = 1; h < kXGroups; ++h) {
+                            const float4 u = x4[h * 32 + lane];
+                            loc.x += u.x;
+                            loc.y += u.y;
+                            loc.z += u.z;
+                            loc.w += u.w;
+                        }
+                        const int64_t e0 = (int64_t)((j - 1) % 3) * H.xred_elems + (int64_t)g * 128 + 4 * lane;
+                        uint64_t* mine = reinterpret_cast<uint64_t*>(const_cast<uint8_t*>(ws) + H.xred_off) + e0;
+                        stg_u64x2(mine, tagged(loc.x, want), tagged(loc.y, want));
+                        stg_u64x2(mine + 2, tagged(loc.z, want), tagged(loc.w, want));
+                        float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+                        for (int rk = 0; rk < world; ++rk) {
+                            float4 r4 = loc;
+                            if (rk != my_rank) {
+                                const uint64_t* src =
+                                    reinterpret_cast<const uint64_t*>(H.peer_ws[rk] + H.xred_off) + e0;
+                                ulonglong2 a = ldsys_u64x2(src), b = ldsys_u64x2(src + 2);
+                                uint32_t spins = 0;
+                                while ((tag_of(a.x) != want) | (tag_of(a.y) != want) | (tag_of(b.x) != want) |
+                                       (tag_of(b.y) != want)) {
+                                    if (++spins > kTagSpinLimit ||
+                                        *reinterpret_cast<volatile int*>(&g_chain_error)) {
+                                        atomicExch(&g_chain_error, 1);
+                                        break;
+                                    }
+                                    a = ldsys_u64x2(src);
+                                    b = ldsys_u64x2(src + 2);
+                                }
+                                r4 = make_float4(val_of(a.x), val_of(a.y), val_of(b.x), val_of(b.y));
+                            }
+                            x.x += r4.x;
+                            x.y += r4.y;
+                            x.z += r4.z;
+                            x.w += r4.w;
+                        }
+                        float4* xw = reinterpret_cast<float4*>(xsl);
+                        xw[lane] = x;
+#pragma unroll
+                        for (int h = 1; h < kXGroups; ++h) xw[h * 32 + lane] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+                    consumers_sync();
+                }
                 {
                     const float* xs = xs_buf + xsp * (kXGroups * 128);
                     float4 xv = reinterpret_cast<const float4*>(xs)[lane];
@@ -587,7 +662,14 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
         consumers_sync();                  // all of this CTA's partials for step j are written
         // This CTA is done reading step j-1's partials (their values have been
         // consumed before the barrier above); no fence is needed for that.
-        if (threadIdx.x == 0) atomicAdd(&ctr[j], 1u);
+        if (threadIdx.x == 0) {
+            if (world == 1) {
+                atomicAdd(&ctr[j], 1u);
+            } else {
+                for (int rk = 0; rk < world; ++rk)
+                    red_sys_add(reinterpret_cast<unsigned*>(H.peer_ws[rk] + H.ctr_off) + j, 1u);
+            }
+        }
     }
 
     // Final output: the last step's feed store, rows split over the CTAs (each
@@ -621,14 +703,40 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
             v += __shfl_xor_sync(0xffffffffu, v, 1);
             v += __shfl_xor_sync(0xffffffffu, v, 2);
             v += __shfl_xor_sync(0xffffffffu, v, 4);
-            if (r < r1 && sub8 == 0) store_f(out, out_dtype, r, v);
+            if (r < r1 && sub8 == 0) {
+                if (world > 1 && H.final_remote) {
+                    const uint32_t tfin = tag_base + (uint32_t)n_steps;
+                    uint64_t* mine = reinterpret_cast<uint64_t*>(const_cast<uint8_t*>(ws) + H.xfin_off) + r;
+                    asm volatile("st.global.u64 [%0], %1;" ::"l"(mine), "l"(tagged(v, tfin)) : "memory");
+                    float x = 0.f;
+                    for (int rk = 0; rk < world; ++rk) {
+                        float rv = v;
+                        if (rk != my_rank) {
+                            const uint64_t* src = reinterpret_cast<const uint64_t*>(H.peer_ws[rk] + H.xfin_off) + r;
+                            uint64_t e = ldsys_u64(src);
+                            uint32_t spins = 0;
+                            while (tag_of(e) != tfin) {
+                                if (++spins > kTagSpinLimit || *reinterpret_cast<volatile int*>(&g_chain_error)) {
+                                    atomicExch(&g_chain_error, 1);
+                                    break;
+                                }
+                                e = ldsys_u64(src);
+                            }
+                            rv = val_of(e);
+                        }
+                        x += rv;
+                    }
+                    v = x;
+                }
+                store_f(out, out_dtype, r, v);
+            }
         }
     }
     consumers_sync();
     if (threadIdx.x == 0) {
         __threadfence();
         // The last CTA to finish advances the run generation for the next launch.
-        if (atomicAdd(&ctr[n_steps], 1u) == target - 1u) atomicAdd(&ctr[n_steps + 1], 1u);
+        if (atomicAdd(&ctr[n_steps], 1u) == (misc[0] + 1u) * (unsigned)G - 1u) atomicAdd(&ctr[n_steps + 1], 1u);
     }
 }
 
@@ -779,7 +887,15 @@ int chain_layout(const StoreArr* st, const int* counts, const int* feeds, int n_
     H.part_off0 = al256(H.ctr_off + 4 * (n_steps + 2));
     H.part_off1 = al256(H.part_off0 + 8 * part_floats);
     H.part_off2 = al256(H.part_off1 + 8 * part_floats);
-    *ws_bytes = al256(H.part_off2 + 8 * part_floats);
+    int64_t kmax = 0;
+    for (int j = 0; j < n_steps; ++j) kmax = steps[j].k > kmax ? steps[j].k : kmax;
+    H.xred_elems = al256(kmax);
+    H.xred_off = al256(H.part_off2 + 8 * part_floats);
+    H.xfin_elems = st[n_steps - 1].s[feeds[n_steps - 1]].n;
+    H.xfin_off = al256(H.xred_off + 3 * 8 * H.xred_elems);
+    H.tp_world = 1;
+    H.tp_rank = 0;
+    *ws_bytes = al256(H.xfin_off + 8 * H.xfin_elems);
     *hdr = H;
     if (out_steps) *out_steps = std::move(steps);
     return EPQ_OK;
@@ -816,8 +932,8 @@ int chain_write(const std::vector<ChainStepD>& steps, const std::vector<int>& ra
     // counters (and the run generation) start at zero
     if (cudaMemcpyAsync(ws, host.data(), host.size(), cudaMemcpyHostToDevice, st) != cudaSuccess)
         return check_launch("chain: write descriptors");
-    // partial buffers start with tag 0, which no step uses
-    const int64_t part_end = al256(H.part_off2 + 8 * H.part_floats);
+    // partial and exchange buffers start with tag 0, which no step uses
+    const int64_t part_end = al256(H.xfin_off + 8 * H.xfin_elems);
     if (cudaMemsetAsync(static_cast<uint8_t*>(ws) + H.part_off0, 0, part_end - H.part_off0, st) != cudaSuccess)
         return check_launch("chain: clear partial buffers");
     if (cudaStreamSynchronize(st) != cudaSuccess) return check_launch("chain: write descriptors");
@@ -892,6 +1008,43 @@ int epq_chain_prepare(const epq_chain_step* steps, int32_t n_steps, void* worksp
         return set_error(EPQ_EWORKSPACE, "chain_prepare: workspace of %lld bytes needed, %lld given",
                          (long long)need, (long long)workspace_bytes);
     return chain_write(desc, ranges, H, workspace, static_cast<cudaStream_t>(stream));
+}
+
+int epq_chain_set_tp(void* workspace, int32_t rank, int32_t world, const void* const* peer_workspaces,
+                     const uint8_t* remote_input, int32_t n_flags, void* stream) {
+    if (!workspace || world < 1 || world > kMaxTp || rank < 0 || rank >= world || (world > 1 && !peer_workspaces))
+        return set_error(EPQ_EINVAL, "chain_set_tp: rank=%d world=%d (1..%d) / NULL peers", rank, world, kMaxTp);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    ChainHeaderD H;
+    if (cudaMemcpyAsync(&H, workspace, sizeof(H), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+        return check_launch("chain_set_tp: read header");
+    if (H.n_steps < 1 || H.n_steps > 4096 || H.steps_off != 256)
+        return set_error(EPQ_EINVAL, "chain_set_tp: workspace not prepared by epq_chain_prepare");
+    if (!remote_input || n_flags != H.n_steps + 1)
+        return set_error(EPQ_EINVAL, "chain_set_tp: %d flags given, n_steps + 1 = %d needed", n_flags,
+                         H.n_steps + 1);
+    if (remote_input[0])
+        return set_error(EPQ_EINVAL, "chain_set_tp: the first step reads the caller's x, not partial sums");
+    std::vector<ChainStepD> steps(H.n_steps);
+    if (cudaMemcpyAsync(steps.data(), static_cast<uint8_t*>(workspace) + H.steps_off,
+                        sizeof(ChainStepD) * H.n_steps, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+        return check_launch("chain_set_tp: read steps");
+    for (int j = 0; j < H.n_steps; ++j) steps[j].remote = world > 1 && remote_input[j];
+    H.tp_world = world;
+    H.tp_rank = rank;
+    H.final_remote = world > 1 && remote_input[H.n_steps];
+    for (int r = 0; r < kMaxTp; ++r)
+        H.peer_ws[r] = r < world ? reinterpret_cast<int64_t>(world > 1 ? peer_workspaces[r] : workspace) : 0;
+    if (world > 1 && peer_workspaces[rank] != workspace)
+        return set_error(EPQ_EINVAL, "chain_set_tp: peer_workspaces[rank] must be this workspace");
+    if (cudaMemcpyAsync(workspace, &H, sizeof(H), cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(static_cast<uint8_t*>(workspace) + H.steps_off, steps.data(),
+                        sizeof(ChainStepD) * H.n_steps, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+        return check_launch("chain_set_tp: write");
+    return EPQ_OK;
 }
 
 int epq_chain_run(const void* workspace, const void* x, int32_t x_dtype, void* out, int32_t out_dtype,

@@ -51,7 +51,7 @@ EXPORTS = (
     "epq_abi_version", "epq_last_error", "epq_device_error", "epq_layout_bytes",
     "epq_relayout", "epq_linear_workspace_bytes", "epq_linear_multi", "epq_linear",
     "epq_linear_bwd", "epq_materialize", "epq_linear_noalloc", "epq_linear_noalloc_max_scratch",
-    "epq_chain_workspace_bytes", "epq_chain_prepare", "epq_chain_run",
+    "epq_chain_workspace_bytes", "epq_chain_prepare", "epq_chain_run", "epq_chain_set_tp",
 )
 
 _lib = None
@@ -89,6 +89,8 @@ def load_library(path=None):
         lib.epq_chain_workspace_bytes.argtypes = [CP, I32, ctypes.POINTER(I64)]
         lib.epq_chain_prepare.argtypes = [CP, I32, P, I64, P]
         lib.epq_chain_run.argtypes = [P, P, I32, P, I32, P]
+        lib.epq_chain_set_tp.argtypes = [P, I32, I32, ctypes.POINTER(P), ctypes.POINTER(ctypes.c_uint8),
+                                         I32, P]
         for name in EXPORTS:
             getattr(lib, name)          # every declared entry point must be exported
         if lib.epq_abi_version() != 1:
@@ -294,6 +296,15 @@ def chain_prepare(steps):
     _check(lib.epq_chain_prepare(arr, len(steps), ws.data_ptr(), ws.numel(), _stream_ptr(dev)),
            "epq_chain_prepare")
     return ws
+
+
+def chain_set_tp(ws, rank, world, peer_ptrs, remote_input):
+    """Tensor-parallel chain: peer_ptrs[r] = rank r's workspace as mapped here (ints)."""
+    lib = load_library()
+    peers = (ctypes.c_void_p * world)(*peer_ptrs)
+    flags = (ctypes.c_uint8 * len(remote_input))(*[1 if f else 0 for f in remote_input])
+    _check(lib.epq_chain_set_tp(ws.data_ptr(), rank, world, peers, flags, len(remote_input),
+                                _stream_ptr(ws.device)), "epq_chain_set_tp")
 
 
 def chain_run(ws, x, out):

@@ -111,6 +111,14 @@ class LinearStack:
                 s += 1
             self.blocks.append(blk)
 
+    @classmethod
+    def from_blocks(cls, shapes, blocks, device):
+        """A stack over given per-layer stores (e.g. tensor-parallel shards of another stack)."""
+        self = cls.__new__(cls)
+        self.shapes, self.blocks, self.layers = shapes, blocks, len(blocks)
+        self.device = torch.device(device)
+        return self
+
     def chain_steps(self):
         """(stores, feed) per launch: the store that feeds the next launch.
 

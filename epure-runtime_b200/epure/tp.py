@@ -189,5 +189,123 @@ def full_step_reference(blocks, x, linear_fn, out_dtype=None):
     return h
 
 
-__all__ = ["shard_store", "shard_blocks", "split_range", "TPLinearStack", "full_step_reference",
-           "COLUMN", "ROW"]
+def exchange_peer_pointers(t, group=None):
+    """Map every rank's allocation holding tensor `t` into this process (CUDA IPC).
+
+    Returns, per rank, the address of that rank's `t` as seen here (this
+    rank's own pointer unchanged) and the mapped bases to release with
+    ``close_peer_pointers``.  One process per GPU; the GPUs must reach each
+    other over NVLink (peer access)."""
+    import torch.distributed as dist
+    from cuda.bindings import driver as cu
+    from cuda.bindings import runtime as rt
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    ptr = t.data_ptr()
+    err, base, _size = cu.cuMemGetAddressRange(ptr)
+    if err != cu.CUresult.CUDA_SUCCESS:
+        raise RuntimeError(f"epure: cuMemGetAddressRange failed ({err})")
+    base = int(base)
+    err, handle = rt.cudaIpcGetMemHandle(base)
+    if err != rt.cudaError_t.cudaSuccess:
+        raise RuntimeError(f"epure: cudaIpcGetMemHandle failed ({err})")
+    mine = (bytes(handle.reserved), ptr - base)
+    allv = [None] * world
+    dist.all_gather_object(allv, mine, group=group)
+    ptrs, opened = [], []
+    for r, (hbytes, off) in enumerate(allv):
+        if r == rank:
+            ptrs.append(ptr)
+            continue
+        h = rt.cudaIpcMemHandle_t()
+        h.reserved = hbytes
+        err, pbase = rt.cudaIpcOpenMemHandle(h, rt.cudaIpcMemLazyEnablePeerAccess)
+        if err != rt.cudaError_t.cudaSuccess:
+            raise RuntimeError(f"epure: cudaIpcOpenMemHandle of rank {r} failed ({err})")
+        opened.append(int(pbase))
+        ptrs.append(int(pbase) + off)
+    return ptrs, opened
+
+
+def close_peer_pointers(opened):
+    from cuda.bindings import runtime as rt
+    for b in opened:
+        rt.cudaIpcCloseMemHandle(b)
+
+
+class TPChainedLinearStack:
+    """The decode chain of a tensor-parallel shard stack as ONE persistent launch per rank.
+
+    Each rank prepares the chain kernel's workspace over its shards
+    (``LinearStack(..., tp=(rank, world), gpu_layout="tiled")``), maps every
+    rank's workspace (CUDA IPC) and marks the steps whose input is summed over
+    ranks: the q/k/v step of every layer after the first (down is
+    row-parallel), every gate/up step (o is row-parallel), and the final
+    output.  Inside the kernel each rank publishes its sum of every input slice
+    it stages and adds the peers' over NVLink -- the all-reduce after o and
+    down happens in the decode kernel itself, with no collective launch.
+    """
+
+    def __init__(self, stack, group=None, dtype=torch.bfloat16, device=None):
+        import torch.distributed as dist
+        from . import _native
+        self.stack = stack
+        self.device = torch.device(device or stack.device)
+        steps = stack.chain_steps()
+        self.ws = _native.chain_prepare(steps)
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        ptrs, self._opened = exchange_peer_pointers(self.ws, group)
+        # per layer: qkv (input = previous down, row-parallel, except the very first), o, gate/up, down
+        remote = []
+        for li in range(len(stack.blocks)):
+            remote += [li > 0, False, True, False]
+        remote.append(True)        # final output = down (row-parallel)
+        _native.chain_set_tp(self.ws, self.rank, self.world, ptrs, remote)
+        dist.barrier(group)        # every rank's workspace is ready before any run
+        k0 = steps[0][0][0].in_features
+        last, feed = steps[-1]
+        self.x = torch.zeros((1, k0), dtype=dtype, device=self.device)
+        self.out = torch.zeros((1, last[feed].out_features), dtype=dtype, device=self.device)
+        self.graph = None
+        self.stream = torch.cuda.Stream(device=self.device)
+        self.launches_per_step = 1
+
+    def step_eager(self):
+        from . import _native
+        _native.chain_run(self.ws, self.x, self.out)
+        return self.out
+
+    def capture(self):
+        with torch.cuda.stream(self.stream):
+            self.step_eager()
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=self.stream):
+            self.step_eager()
+        self.graph = g
+        return self
+
+    def replay(self):
+        self.graph.replay()
+        return self.out
+
+    def release(self):
+        self.graph = None
+        torch.cuda.synchronize(self.device)
+        close_peer_pointers(self._opened)
+        self._opened = []
+
+    def __call__(self, x_host, out_host=None):
+        if self.graph is None:
+            self.capture()
+        self.x.copy_(x_host, non_blocking=True)
+        self.graph.replay()
+        if out_host is None:
+            out_host = torch.empty(self.out.shape, dtype=self.out.dtype, pin_memory=True)
+        out_host.copy_(self.out, non_blocking=True)
+        return out_host
+
+
+__all__ = ["shard_store", "shard_blocks", "split_range", "TPLinearStack", "TPChainedLinearStack",
+           "full_step_reference", "exchange_peer_pointers", "close_peer_pointers", "COLUMN", "ROW"]

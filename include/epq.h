@@ -222,6 +222,23 @@ int epq_chain_workspace_bytes(const epq_chain_step* steps, int32_t n_steps, int6
 int epq_chain_prepare(const epq_chain_step* steps, int32_t n_steps, void* workspace,
                       int64_t workspace_bytes, void* stream);
 
+/* Tensor parallelism inside the chain (no reference counterpart: the
+ * reference has no multi-GPU path; it replaces, for a sharded model, the
+ * per-linear launches + NCCL all-reduce after every row-parallel linear).
+ * Each of `world` ranks (one GPU each, one process each) prepares a chain over
+ * its shards with identical shapes, maps every rank's workspace into its
+ * address space (CUDA IPC), and calls this once: peer_workspaces[r] is rank
+ * r's workspace as mapped here (peer_workspaces[rank] == workspace).
+ * remote_input[j] = 1 marks step j whose input is the output of a
+ * row-parallel step (a sum over ranks); remote_input[n_steps] marks the final
+ * output likewise.  Inside the kernel each rank publishes its sum of every
+ * input slice it stages and adds the other ranks' over NVLink (plain peer
+ * loads of tagged values, bounded polling) -- no collective launch, no
+ * barrier.  All ranks must run their chains concurrently (one run per token
+ * each).  Synchronous. */
+int epq_chain_set_tp(void* workspace, int32_t rank, int32_t world, const void* const* peer_workspaces,
+                     const uint8_t* remote_input, int32_t n_flags, void* stream);
+
 /* Runs a prepared chain on x (k0 values) into out.  One cooperative launch;
  * capturable in a CUDA graph.  Runs on one workspace must be ordered (same
  * stream); each run leaves the workspace ready for the next. */

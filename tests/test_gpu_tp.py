@@ -71,3 +71,65 @@ def test_tp2_matches_single_gpu(m):
     for rank, err, derr in res:
         assert derr == 0
         assert err <= 1e-2, (rank, err)
+
+
+def _chain_worker(rank, world, port, q):
+    import torch.distributed as dist
+    from epure import synthetic, tp, _native
+    from epure.decode import ChainedLinearStack
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
+    runner = None
+    try:
+        full = synthetic.LinearStack(synthetic.LLAMA3_8B, layers=2, device=dev, seed=31,
+                                     gpu_layout="tiled")
+        shards = synthetic.LinearStack.from_blocks(
+            synthetic.LLAMA3_8B, tp.shard_blocks(full.blocks, rank, world, device=dev), dev)
+        runner = tp.TPChainedLinearStack(shards, dtype=torch.float32).capture()
+        g = torch.Generator(device=dev).manual_seed(9)
+        x = torch.randn(1, 4096, generator=g, device=dev)
+        outs = []
+        for r in range(3):                       # consecutive runs on the same workspaces
+            runner.x.copy_(x * (1 + r))
+            outs.append(runner.replay().clone())
+        torch.cuda.synchronize(dev)
+        single = ChainedLinearStack(full, dtype=torch.float32)
+        errs = []
+        for r in range(3):
+            single.x.copy_(x * (1 + r))
+            want = single.step_eager().clone()
+            errs.append(float((outs[r] - want).abs().max() / want.abs().max()))
+        torch.cuda.synchronize(dev)
+        q.put((rank, errs, outs[0].cpu(), _native.device_error()))
+    finally:
+        if runner is not None:
+            runner.release()
+        dist.destroy_process_group()
+
+
+def test_tp2_chain_matches_single_gpu():
+    """TP inside the persistent chain: ranks exchange slice sums over NVLink in the kernel."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import socket
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_chain_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=300) for _ in range(2)], key=lambda t: t[0])
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, errs, _, derr in res:
+        assert derr == 0
+        assert max(errs) <= 1e-4, (rank, errs)
+    assert torch.equal(res[0][2], res[1][2])     # every rank ends with the same output
