@@ -92,8 +92,8 @@ constexpr int kRing = 3;
 constexpr int kChunkTiles = 64;                                    // one tile per 8-lane team
 constexpr uint32_t kStageIdx = kChunkTiles * 512;                  // 32 KB of index tiles
 constexpr uint32_t kStageBytes = kStageIdx + kChunkTiles * 64;     // + scales (<= fp32)
-constexpr int kXGroups = kConsumerWarps / 4;     // activation staging: warp groups of 4 parts
-static_assert(kConsumerWarps == 16, "staging: 4 column-quad groups x 4 part groups of warps");
+constexpr int kXGroups = kConsumerWarps / 2;     // activation staging: parts (warp pairs)
+static_assert(kConsumerWarps == 16, "staging: 2 column halves x 8 parts of warps");
 // Shared-window addresses (the dynamic block starts at a small offset `base`).
 constexpr uint32_t kXsOff = 8192;      // from base: 2 x codebook [1024] fp32 below, then
                                        // 2 x activation slice sums [kXGroups][128] fp32
@@ -404,19 +404,26 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
     int i = 0, slot = 0;
     for (int j = 0; j < n_steps; ++j) {
         const ChainStepD& S = sdesc[j % 3];
-        cb_promote(j);
-        if (j >= 1 && j + 1 < n_steps && threadIdx.x < kDescWords) {
-            // step j+1 into the slot of step j-2 (no longer read); published by the barrier below
-            sdw[((j + 1) % 3) * kDescWords + threadIdx.x] = dreg;
-            if (j + 2 < n_steps) dreg = __ldg(gsteps + (j + 2) * kDescWords + threadIdx.x);
-        }
-        if (j > 0) consumers_sync();   // publishes the descriptor slot written above
-        cb_prefetch(j + 1);
-        if (j + 1 < n_steps) {
-            const int* rgn = reinterpret_cast<const int*>(ws + sdesc[(j + 1) % 3].range_off);
-            rnext0 = __ldg(rgn + blockIdx.x);
-            rnext1 = __ldg(rgn + blockIdx.x + 1);
-        }
+        // The step's bookkeeping (codebooks, descriptor ring, next range) runs once,
+        // after the first poll round of the step's first input slice has been issued,
+        // so that it overlaps that round trip (or at the end for a CTA without tiles).
+        bool booked = false;
+        auto bookkeeping = [&]() {
+            cb_promote(j);
+            if (j >= 1 && j + 1 < n_steps && threadIdx.x < kDescWords) {
+                // step j+1 into the slot of step j-2 (no longer read); published by the barrier below
+                sdw[((j + 1) % 3) * kDescWords + threadIdx.x] = dreg;
+                if (j + 2 < n_steps) dreg = __ldg(gsteps + (j + 2) * kDescWords + threadIdx.x);
+            }
+            if (j > 0) consumers_sync();   // publishes the descriptor slot written above
+            cb_prefetch(j + 1);
+            if (j + 1 < n_steps) {
+                const int* rgn = reinterpret_cast<const int*>(ws + sdesc[(j + 1) % 3].range_off);
+                rnext0 = __ldg(rgn + blockIdx.x);
+                rnext1 = __ldg(rgn + blockIdx.x + 1);
+            }
+            booked = true;
+        };
         // Input of this step: x0 (step 0) or the partials of step j-1's feed store.
         const ChainStepD* P = j > 0 ? &sdesc[(j - 1) % 3] : nullptr;
         const uint64_t* pin = j > 0 ? part[(j - 1) % 3] + P->st[P->feed].part_off : nullptr;
@@ -433,6 +440,26 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
             const ChainStoreD& C = S.st[si];
             if (si != cur_s || g != cur_g) {
                 // New (store, group): stage the codebook / activation slice, build T.
+                // x[128 g + 2 cp .. +2] = sum over the input partial slices.  Warp w
+                // covers column pairs 32 (w % 2) .. +31 -- 512 contiguous bytes of a
+                // slice per load, every sector fetched once -- for part w / 2; part p
+                // adds slices p, p + 8, ... (4 slices in flight per poll round).
+                const bool new_g = g != cur_g;
+                const int cp = 32 * (warp & 1) + lane;
+                const int xpart = warp >> 1;
+                const int64_t c = (int64_t)g * 128 + 2 * cp;
+                const bool poll = new_g && j > 0 && c < S.k;
+                const uint64_t* col = pin + c;
+                ulonglong2 a[4];
+                auto issue_round = [&](int gp0) {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const int gp = gp0 + kXGroups * q;
+                        if (gp < pin_ng) a[q] = ldcg_u64x2(col + gp * pin_stride);
+                    }
+                };
+                if (poll) issue_round(xpart);
+                if (!booked) bookkeeping();
                 if (si != cur_s) {
                     cbp ^= 1;
                     float* cbf = cbf_buf + cbp * 1024;
@@ -443,73 +470,43 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
                         if (q == si) v = cb_cur[q];
                     reinterpret_cast<float2*>(cbf)[threadIdx.x] = v;
                 }
-                if (g != cur_g) {
+                if (new_g) {
                     xsp ^= 1;
                     float* xs = xs_buf + xsp * (kXGroups * 128);
-                    // x[128 g + 4 c4 .. +4] = sum over the input partial slices.  Warp w
-                    // covers column quads 8 (w % 4) .. +7 (128 contiguous bytes per slice)
-                    // for parts 4 (w / 4) + lane / 8; part p adds slices p, p + 16, ...
-                    // Two xor-shuffles sum the warp's 4 parts; the table build adds the
-                    // kXGroups warp-group sums (fixed order throughout).
-                    const int c4 = 8 * (warp & 3) + (lane & 7);
-                    const int part = 4 * (warp >> 2) + (lane >> 3);
-                    const int64_t c = (int64_t)g * 128 + 4 * c4;
-                    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                    // The table build adds the kXGroups part sums (fixed order throughout).
+                    float2 v = make_float2(0.f, 0.f);
                     if (c < S.k) {
                         if (j == 0) {
-                            if (part == 0)
-                                v = make_float4(load_f(x0, x_dtype, c), load_f(x0, x_dtype, c + 1),
-                                                load_f(x0, x_dtype, c + 2), load_f(x0, x_dtype, c + 3));
+                            if (xpart == 0) v = make_float2(load_f(x0, x_dtype, c), load_f(x0, x_dtype, c + 1));
                         } else {
-                            // Poll the 4 values of each input slice until they carry step
-                            // j-1's tag (4 slices in flight per round; bounded).
-                            const uint64_t* col = pin + c;
-                            for (int gp0 = part; gp0 < pin_ng; gp0 += 64) {
-                                ulonglong2 a[4], b[4];
+                            // Each round: wait until the 4 values of each of its slices
+                            // carry step j-1's tag (bounded), add them, issue the next.
+                            for (int gp0 = xpart; gp0 < pin_ng; gp0 += 4 * kXGroups) {
+                                if (gp0 != xpart) issue_round(gp0);
 #pragma unroll
                                 for (int q = 0; q < 4; ++q) {
-                                    const int gp = gp0 + 16 * q;
-                                    if (gp < pin_ng) {
-                                        a[q] = ldcg_u64x2(col + gp * pin_stride);
-                                        b[q] = ldcg_u64x2(col + gp * pin_stride + 2);
-                                    }
-                                }
-#pragma unroll
-                                for (int q = 0; q < 4; ++q) {
-                                    const int gp = gp0 + 16 * q;
+                                    const int gp = gp0 + kXGroups * q;
                                     if (gp >= pin_ng) continue;
                                     uint32_t spins = 0;
-                                    while ((tag_of(a[q].x) != want) | (tag_of(a[q].y) != want) |
-                                           (tag_of(b[q].x) != want) | (tag_of(b[q].y) != want)) {
+                                    while ((tag_of(a[q].x) != want) | (tag_of(a[q].y) != want)) {
                                         if (++spins > kTagSpinLimit ||
                                             *reinterpret_cast<volatile int*>(&g_chain_error)) {
                                             atomicExch(&g_chain_error, 1);
                                             break;
                                         }
                                         a[q] = ldcg_u64x2(col + gp * pin_stride);
-                                        b[q] = ldcg_u64x2(col + gp * pin_stride + 2);
                                     }
                                     v.x += val_of(a[q].x);
                                     v.y += val_of(a[q].y);
-                                    v.z += val_of(b[q].x);
-                                    v.w += val_of(b[q].y);
                                 }
                             }
                         }
                     }
-#pragma unroll
-                    for (int off = 8; off <= 16; off <<= 1) {
-                        v.x += __shfl_xor_sync(0xffffffffu, v.x, off);
-                        v.y += __shfl_xor_sync(0xffffffffu, v.y, off);
-                        v.z += __shfl_xor_sync(0xffffffffu, v.z, off);
-                        v.w += __shfl_xor_sync(0xffffffffu, v.w, off);
-                    }
-                    if (lane < 8) reinterpret_cast<float4*>(xs)[(warp >> 2) * 32 + c4] = v;
+                    reinterpret_cast<float2*>(xs)[xpart * 64 + cp] = v;
                 }
                 // This step overwrites buffer j % 3, last read during step j-2's staging:
                 // before the first write, every CTA must have finished step j-2.
                 if (cur_s < 0 && j >= 3 && threadIdx.x == 0) grid_wait(&ctr[j - 2], target);
-                const bool new_g = g != cur_g;
                 cur_s = si;
                 cur_g = g;
                 consumers_sync();
@@ -657,6 +654,7 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
             if (lane == 0) mbar_arrive(bar_empty + 8 * stage);
             ++i;
         }
+        if (!booked) bookkeeping();
         rcur0 = rnext0;
         rcur1 = rnext1;
         consumers_sync();                  // all of this CTA's partials for step j are written
