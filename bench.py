@@ -12,7 +12,8 @@ part of the packed-linear path and are not in the step.
 
 Our arm runs the step as ONE persistent launch of libepq.so's chain kernel
 (epq_chain_run: every packed linear of the token, weights streamed through a
-TMA ring per SM, grid barriers between dependent linears), replayed from a CUDA
+TMA ring per SM, each linear's input polled from the tagged split-k partial sums
+of the previous one, no grid barrier), replayed from a CUDA
 graph (value), and separately through the public runner with host buffers
 (e2e: pinned H2D copy of the token input, replay, D2H copy of the output, every
 step).  `--mode per-linear` instead replays 128 launches of the single-linear
@@ -28,6 +29,8 @@ Other workloads (not the headline; each prints its own metric):
   --mode prefill [--tokens 2048]: a prompt of `tokens` rows through every packed
       linear (the tensor-core dequant-GEMM, one launch per fused group), metric
       prefill tok/s, roofline against the sustained bf16 tensor peak;
+  --mode per-linear --batch B: a B-token decode step through the per-linear launches
+      (the tensor-core GEMV up to 16 rows, the tcgen05 GEMM above), metric tok/s;
   --model qwen3-1.7b|llama3-8b|llama3-70b picks the decoder shapes;
   --layers L keeps the first L layers (small cases for profiling);
   --tp (with N > 1): one model tensor-parallel over the N GPUs (column-parallel
@@ -408,7 +411,7 @@ def run_ours(args, rank, world, local_rank):
     use_tp = args.tp and world > 1
     chain = args.mode == "chain"
     prefill = args.mode == "prefill"
-    m = args.tokens if prefill else 1
+    m = args.tokens if prefill else args.batch
     if use_tp:
         # every rank draws its own shards of one model (same seed on every rank)
         stack = synthetic.LinearStack(shapes, layers=args.layers, device=dev, seed=1000,
@@ -424,7 +427,7 @@ def run_ours(args, rank, world, local_rank):
     elif use_tp:
         from epure.tp import TPLinearStack
         runner = TPLinearStack(stack.blocks, m=m, dtype=torch.bfloat16, device=dev).capture()
-        kernel_name = (("gemm_tc_kernel" if prefill else "gemv_mma_kernel") +
+        kernel_name = (("gemm_tc_kernel" if m > 16 else "gemv_mma_kernel") +
                        f" on 1/{world} shards + NCCL all-reduce after o and down")
     elif chain:
         runner = ChainedLinearStack(stack, dtype=torch.bfloat16, device=dev).capture()
@@ -433,8 +436,8 @@ def run_ours(args, rank, world, local_rank):
         runner = GraphedLinearStack(stack, m=m, dtype=torch.bfloat16, device=dev).capture()
         kernel_name = "gemm_tc_kernel (all launches of the step)"
     else:
-        runner = GraphedLinearStack(stack, m=1, dtype=torch.bfloat16, device=dev).capture()
-        kernel_name = "gemv_mma_kernel (all launches of the step)"
+        runner = GraphedLinearStack(stack, m=m, dtype=torch.bfloat16, device=dev).capture()
+        kernel_name = ("gemv_mma_kernel" if m <= 16 else "gemm_tc_kernel") + " (all launches of the step)"
     g = torch.Generator(device=dev).manual_seed(rank)
     runner.x.copy_(torch.randn(runner.x.shape, generator=g, device=dev).to(torch.bfloat16))
     step_bytes = stack.algorithmic_bytes(m=m, act_bytes=2)
@@ -497,6 +500,8 @@ def run_ours(args, rank, world, local_rank):
         "224 linears", f"{7 * stack.layers} linears")
     if prefill:
         workload = workload.replace("batch-1 decode token", f"{m}-token prefill")
+    elif m > 1:
+        workload = workload.replace("batch-1 decode token", f"batch-{m} decode step ({m} tokens)")
     if stack.layers != shapes.layers:
         workload += f" (first {stack.layers} of {shapes.layers} layers)"
     if prefill:
@@ -515,7 +520,7 @@ def run_ours(args, rank, world, local_rank):
                     "launch_avg_us": round(ms * 1e3 / launches, 3),
                     "traffic": (int(step_bytes * NCU_TRAFFIC_RATIO[args.mode])
                                 if NCU_TRAFFIC_RATIO.get(args.mode) and stack.layers == 32
-                                and args.model == "llama3-8b" else None),
+                                and args.model == "llama3-8b" and m == 1 else None),
                     "traffic_note": TRAFFIC_NOTE.get(args.mode)}
     streams = 1 if use_tp else world          # independent token streams across the job
     if use_tp:
@@ -528,8 +533,11 @@ def run_ours(args, rank, world, local_rank):
     if rank == 0:
         metric = (f"prefill tok/s @{args.model} ({m}-token prompt, packed linears)"
                   if prefill else METRIC)
+        if not prefill and m > 1:
+            metric = f"decode tok/s bs{m} @{args.model} (packed linears)"
         if use_tp and not prefill:
-            metric = f"decode tok/s bs1 @{args.model}, tensor-parallel over {world} GPUs (packed linears)"
+            metric = (f"decode tok/s bs{m} @{args.model}, tensor-parallel over {world} GPUs "
+                      "(packed linears)")
         line = {
             "metric": metric,
             "value": round(streams * m * 1000.0 / ms, 2),
@@ -583,6 +591,9 @@ def main():
     ap.add_argument("--model", choices=["qwen3-1.7b", "llama3-8b", "llama3-70b"], default=None)
     ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--tokens", type=int, default=None)
+    ap.add_argument("--batch", type=int, default=1,
+                    help="decode batch (tokens per step) for --mode per-linear: M rows through "
+                         "every linear (tensor-core GEMV up to 16, the tcgen05 GEMM above)")
     ap.add_argument("--tp", action="store_true",
                     help="at N > 1: one model tensor-parallel over the N GPUs instead of N replicas")
     ap.add_argument("--fallback", action="store_true",
@@ -595,6 +606,8 @@ def main():
         args.model = "qwen3-1.7b" if args.mode == "finetune" else "llama3-8b"
     if args.tokens is None:
         args.tokens = 8 * 2048 if args.mode == "finetune" else 2048
+    if args.batch != 1 and args.mode != "per-linear":
+        ap.error("--batch applies to --mode per-linear (the chain kernel is batch-1)")
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -106,3 +106,23 @@ def test_chain_rejects_bad_wiring():
     m = __import__("epure").synthetic.make_store(64, 512, device=DEV, seed=3, gpu_layout="mma16")
     with pytest.raises(RuntimeError, match="EPQ_LAYOUT_TILED"):
         _native.chain_prepare([([m], 0)])
+
+
+@pytest.mark.parametrize("n_steps", [1, 2, 3, 4, 5, 6])
+def test_many_consecutive_runs_any_length(n_steps, oracle_mod):
+    """Tagged partials in a ring of three buffers: whatever the chain length, each
+    of many consecutive runs (different inputs) reads only the current step's
+    partials -- a stale word from an earlier step or run would show up here."""
+    from epure import _native
+    widths = [256, 384, 128, 512, 256, 384, 256]
+    stores = [_store(widths[i + 1], widths[i], 40 + i) for i in range(n_steps)]
+    steps = [([st], 0) for st in stores]
+    ws = _native.chain_prepare(steps)
+    for r in range(17):
+        x = (torch.randn(1, widths[0], device=DEV) * (1 + 0.1 * r)).to(torch.bfloat16)
+        out = torch.empty(1, widths[n_steps], device=DEV)
+        _native.chain_run(ws, x, out)
+        h = x.double().cpu().numpy()
+        for st in stores:
+            h = _exact(st, h, oracle_mod)
+        assert oracle_mod.rel_err(out.double().cpu().numpy(), h) <= 1e-4, (n_steps, r)
