@@ -494,6 +494,9 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
                                             atomicExch(&g_chain_error, 1);
                                             break;
                                         }
+                                        // a short back-off keeps waiting CTAs' re-polls from
+                                        // crowding the L2 that the late producers still use
+                                        __nanosleep(100);
                                         a[q] = ldcg_u64x2(col + gp * pin_stride);
                                     }
                                     v.x += val_of(a[q].x);
