@@ -29,6 +29,9 @@ Other workloads (not the headline; each prints its own metric):
   --mode prefill [--tokens 2048]: a prompt of `tokens` rows through every packed
       linear (the tensor-core dequant-GEMM, one launch per fused group), metric
       prefill tok/s, roofline against the sustained bf16 tensor peak;
+  --mode model: greedy decode of the whole model (epure.model.PackedDecoder:
+      packed linears through libepq.so, attention / norms / lm_head in torch, one
+      CUDA graph per token after a 128-token prompt), metric tok/s;
   --mode per-linear --batch B: a B-token decode step through the per-linear launches
       (the tensor-core GEMV up to 16 rows, the tcgen05 GEMM above), metric tok/s;
   --model qwen3-1.7b|llama3-8b|llama3-70b picks the decoder shapes;
@@ -399,6 +402,105 @@ def time_fallback_finetune(stack, x, steps):
             "steps": steps}
 
 
+def run_model(args, rank, world, local_rank):
+    """Greedy decode of the whole model (epure.model.PackedDecoder): packed linears
+    through libepq.so, attention / norms / RoPE / SwiGLU / lm_head in torch, one
+    CUDA graph per token (argmax and position update included)."""
+    import torch
+    import torch.distributed as dist
+    from epure import synthetic
+    from epure.model import PackedDecoder
+    from epure.synthetic import store_bytes
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    shapes = synthetic.SHAPES[args.model]
+    prompt_len = 128
+    max_len = prompt_len + args.warmup + args.steps + 2
+    dec = PackedDecoder(shapes, layers=args.layers, device=dev, seed=1000 * rank, max_len=max_len,
+                        fp32_logits=False).capture()
+    g = torch.Generator().manual_seed(rank)
+    prompt = torch.randint(0, shapes.vocab, (prompt_len,), generator=g)
+
+    def restart():
+        first = int(torch.argmax(dec.prefill(prompt)))
+        dec.tok.fill_(first)
+        dec.pos.fill_(prompt_len)
+        torch.cuda.synchronize(dev)
+
+    restart()
+    for _ in range(args.warmup):
+        dec._graph.replay()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    stream = torch.cuda.current_stream(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            dec._graph.replay()
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+    ms = ev0.elapsed_time(ev1) / args.steps
+    # end to end: each token goes from pinned host memory into the graph's input
+    # and the next token is read back to the host, every step
+    restart()
+    th = torch.empty(1, dtype=torch.long, pin_memory=True)
+    th.copy_(dec.tok.cpu())
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        dec.tok.copy_(th, non_blocking=True)
+        dec._graph.replay()
+        th.copy_(dec.tok, non_blocking=True)
+        stream.synchronize()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms = float(t[0]), float(t[1])
+    # algorithmic bytes of one token: packed stores, lm_head, one embedding row, and
+    # the K/V of the positions attended (averaged over the timed steps)
+    packed = sum(store_bytes(st) for b in dec.stack.blocks for st in b.values())
+    lm = dec.lm_head.numel() * dec.lm_head.element_size()
+    pos_avg = prompt_len + args.warmup + args.steps / 2
+    kv = 2 * dec.layers * pos_avg * shapes.kv_heads * shapes.head_dim * 2
+    step_bytes = int(packed + lm + shapes.hidden * 2 + kv)
+    hbm_peak, peak_kind = _peaks()
+    achieved = step_bytes / (ms * 1e-3) / 1e9
+    if rank == 0:
+        layers_note = (f" (first {dec.layers} of {shapes.layers} layers)"
+                       if dec.layers != shapes.layers else "")
+        line = {
+            "metric": f"greedy decode tok/s bs1 @{args.model} (whole model: packed linears + "
+                      "attention, norms, lm_head)",
+            "value": round(world * 1000.0 / ms, 2), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": f"{args.model} greedy decode after a {prompt_len}-token prompt"
+                                   + layers_note,
+                       "mode": "model", "global_batch": world, "seq_len": max_len,
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "l2": f"inputs larger than L2 ({step_bytes / 1e9:.2f} GB moved per step)",
+                       "bytes_per_step": step_bytes,
+                       "bytes_split": {"packed": packed, "lm_head": lm, "kv": int(kv)}},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak,
+                         "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
+                         "peak_kind": peak_kind,
+                         "kernel": "whole token graph: gemv_mma_kernel (packed) + torch/cuBLAS",
+                         "traffic": None},
+            "e2e": {"value": round(world * 1000.0 / e2e_ms, 2), "unit": UNIT,
+                    "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8},
+            "gpu_launches": 4 * dec.layers * args.steps,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
@@ -587,7 +689,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--mode", choices=["chain", "per-linear", "prefill", "finetune"], default="chain")
+    ap.add_argument("--mode", choices=["chain", "per-linear", "prefill", "finetune", "model"],
+                    default="chain")
     ap.add_argument("--model", choices=["qwen3-1.7b", "llama3-8b", "llama3-70b"], default=None)
     ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--tokens", type=int, default=None)
@@ -626,6 +729,8 @@ def main():
     try:
         if args.mode == "finetune":
             return run_finetune(args, rank, world, local_rank)
+        if args.mode == "model":
+            return run_model(args, rank, world, local_rank)
         return run_ours(args, rank, world, local_rank)
     finally:
         if world > 1:

@@ -1,0 +1,500 @@
+// Decode-step glue around the packed linears: the non-linear parts of a
+// Llama-3 / Qwen3 block for one token, each one small launch instead of the
+// dozen elementwise torch kernels it replaces, so that a whole-token CUDA graph
+// is dominated by the packed linears and the lm_head.
+//
+// Reference counterpart: the reference leaves these to the Hugging Face model
+// around its PackedLinear modules (epure/runtime.py:214-305 swaps only the
+// linears); the arithmetic follows that model's (fp32 math, results rounded to
+// the activation dtype where the model's tensors are in that dtype):
+//
+//   epq_add_rmsnorm  h = x + add (rounded), y = h * rsqrt(mean(h^2) + eps) (weight 1)
+//   epq_rope_kv      optional per-head RMSNorm of q and k (Qwen3), rotate-half RoPE
+//                    at a device-resident position, k / v written into the caches
+//   epq_attn_decode  one query row per head against cache positions 0..pos
+//                    (grouped-query attention, fp32 online softmax)
+//   epq_silu_mul     silu(g) * u
+//
+// All four read positions from device memory, so a decode step captured in a
+// CUDA graph replays at any position.
+#include "epq_common.cuh"
+#include "epq_decode.h"
+
+namespace epq {
+namespace {
+
+template <int kThreads>
+__device__ __forceinline__ float block_sum(float v, float* red) {
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if (kThreads > 32) {
+        if (l == 0) red[w] = v;
+        __syncthreads();
+        v = l < kThreads / 32 ? red[l] : 0.f;
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        __syncthreads();
+    }
+    return v;
+}
+
+constexpr int kNormThreads = 512;
+
+// One CTA per row.  h is kept in shared memory between the two passes.
+__global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(
+    const void* __restrict__ x, const void* __restrict__ add, void* __restrict__ h_out,
+    void* __restrict__ y, int64_t n, float eps, int dtype) {
+    extern __shared__ float hs[];
+    __shared__ float red[32];
+    const int64_t row = blockIdx.x;
+    float ss = 0.f;
+    for (int64_t i = threadIdx.x; i < n; i += kNormThreads) {
+        float h = load_f(x, dtype, row * n + i);
+        if (add) h = round_to(h + load_f(add, dtype, row * n + i), dtype);
+        hs[i] = h;
+        ss += h * h;
+    }
+    ss = block_sum<kNormThreads>(ss, red);
+    const float r = rsqrtf(ss / (float)n + eps);
+    for (int64_t i = threadIdx.x; i < n; i += kNormThreads) {
+        const float h = hs[i];
+        if (h_out) store_f(h_out, dtype, row * n + i, h);
+        store_f(y, dtype, row * n + i, h * r);
+    }
+}
+
+// One CTA of head_dim / 2 threads per (row, head); heads [0, H) are q heads,
+// [H, H + KV) k heads (their v rows are copied alongside).
+__global__ void __launch_bounds__(128) rope_kv_kernel(
+    void* __restrict__ q, const void* __restrict__ k, const void* __restrict__ v,
+    const int64_t* __restrict__ pos, int H, int KV, int hd, const float* __restrict__ cos_t,
+    const float* __restrict__ sin_t, void* __restrict__ k_cache, void* __restrict__ v_cache,
+    int qk_norm, float eps, int dtype) {
+    __shared__ float red[32];
+    const int64_t row = blockIdx.x;
+    const int head = blockIdx.y;
+    const int half = hd / 2, i = threadIdx.x;
+    const bool is_q = head < H;
+    const int kh = head - H;
+    const int64_t p = pos[row];
+    const void* src = is_q ? static_cast<const void*>(q) : k;
+    const int64_t base = is_q ? (row * H + head) * hd : (row * KV + kh) * hd;
+    float x1 = load_f(src, dtype, base + i), x2 = load_f(src, dtype, base + i + half);
+    if (qk_norm) {
+        float ss = x1 * x1 + x2 * x2;
+        if (half == 32) ss = block_sum<32>(ss, red);
+        else if (half == 64) ss = block_sum<64>(ss, red);
+        else ss = block_sum<128>(ss, red);
+        const float r = rsqrtf(ss / (float)hd + eps);
+        x1 = round_to(x1 * r, dtype);
+        x2 = round_to(x2 * r, dtype);
+    }
+    const float c = cos_t[p * half + i], s = sin_t[p * half + i];
+    const float o1 = x1 * c - x2 * s, o2 = x2 * c + x1 * s;
+    if (is_q) {
+        store_f(q, dtype, base + i, o1);
+        store_f(q, dtype, base + i + half, o2);
+    } else {
+        const int64_t dst = (p * KV + kh) * hd;
+        store_f(k_cache, dtype, dst + i, o1);
+        store_f(k_cache, dtype, dst + i + half, o2);
+        store_f(v_cache, dtype, dst + i, load_f(v, dtype, base + i));
+        store_f(v_cache, dtype, dst + i + half, load_f(v, dtype, base + i + half));
+    }
+}
+
+// bf16 rows of n = 8 * blockDim.x values: one 16-byte load per thread, values kept
+// in registers between the sum of squares and the scaling.
+__global__ void __launch_bounds__(1024) add_rmsnorm_bf16x8_kernel(
+    const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ add,
+    __nv_bfloat16* __restrict__ h_out, __nv_bfloat16* __restrict__ y, int64_t n, float eps) {
+    __shared__ float red[32];
+    const int64_t off = blockIdx.x * n + 8 * threadIdx.x;
+    const uint4 xr = *reinterpret_cast<const uint4*>(x + off);
+    const __nv_bfloat16* xv = reinterpret_cast<const __nv_bfloat16*>(&xr);
+    float h[8];
+    if (add) {
+        const uint4 ar = *reinterpret_cast<const uint4*>(add + off);
+        const __nv_bfloat16* av = reinterpret_cast<const __nv_bfloat16*>(&ar);
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+            h[e] = __bfloat162float(__float2bfloat16_rn(__bfloat162float(xv[e]) + __bfloat162float(av[e])));
+    } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) h[e] = __bfloat162float(xv[e]);
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss += h[e] * h[e];
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+    if (l == 0) red[w] = ss;
+    __syncthreads();
+    ss = l < nw ? red[l] : 0.f;
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float r = rsqrtf(ss / (float)n + eps);
+    uint4 hr, yr;
+    __nv_bfloat16* hv = reinterpret_cast<__nv_bfloat16*>(&hr);
+    __nv_bfloat16* yv = reinterpret_cast<__nv_bfloat16*>(&yr);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        hv[e] = __float2bfloat16_rn(h[e]);
+        yv[e] = __float2bfloat16_rn(h[e] * r);
+    }
+    if (h_out) *reinterpret_cast<uint4*>(h_out + off) = hr;
+    *reinterpret_cast<uint4*>(y + off) = yr;
+}
+
+// Split decode attention: CTA (kv head, split) takes a contiguous range of the
+// positions 0..pos[0] for the kGroup query heads that read that kv head (each K/V
+// row is loaded once for all of them); warp w takes every 8th position of the
+// range, softmax is online per (warp, head); the CTA writes (max, sum, acc) per
+// head to the workspace, and the last CTA of the kv head to finish (counter)
+// merges the splits in split order and resets the counter.
+constexpr int kAttnSplits = 16;
+constexpr int kAttnWarps = 8;
+
+template <int kDims, int kGroup>
+__global__ void __launch_bounds__(kAttnWarps * 32) attn_split_kernel(
+    const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k_cache,
+    const __nv_bfloat16* __restrict__ v_cache, const int64_t* __restrict__ pos, int KV, float scale,
+    __nv_bfloat16* __restrict__ out, float* __restrict__ ws, unsigned* __restrict__ counters) {
+    constexpr int hd = kDims * 32;
+    constexpr int kRec = hd + 2;                       // acc[hd], max, sum
+    __shared__ float wm[kAttnWarps][kGroup], wl[kAttnWarps][kGroup];
+    __shared__ float wacc[kAttnWarps][kGroup][hd];
+    __shared__ bool last;
+    const int kvh = blockIdx.x, split = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t n = pos[0] + 1;
+    const int64_t chunk = (n + kAttnSplits - 1) / kAttnSplits;
+    const int64_t t0 = split * chunk, t1 = min(n, t0 + chunk);
+    float qv[kGroup][kDims], acc[kGroup][kDims], m[kGroup], l[kGroup];
+#pragma unroll
+    for (int g = 0; g < kGroup; ++g) {
+        m[g] = -INFINITY;
+        l[g] = 0.f;
+#pragma unroll
+        for (int d = 0; d < kDims; ++d) {
+            qv[g][d] = __bfloat162float(q[(int64_t)(kvh * kGroup + g) * hd + lane * kDims + d]);
+            acc[g][d] = 0.f;
+        }
+    }
+    for (int64_t t = t0 + warp; t < t1; t += kAttnWarps) {
+        const int64_t kb = (t * KV + kvh) * hd + lane * kDims;
+        float kr[kDims], vr[kDims];
+#pragma unroll
+        for (int d = 0; d < kDims; ++d) {
+            kr[d] = __bfloat162float(k_cache[kb + d]);
+            vr[d] = __bfloat162float(v_cache[kb + d]);
+        }
+#pragma unroll
+        for (int g = 0; g < kGroup; ++g) {
+            float s = 0.f;
+#pragma unroll
+            for (int d = 0; d < kDims; ++d) s += qv[g][d] * kr[d];
+            for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+            s *= scale;
+            const float mn = fmaxf(m[g], s);
+            const float corr = expf(m[g] - mn), pw = expf(s - mn);
+            l[g] = l[g] * corr + pw;
+#pragma unroll
+            for (int d = 0; d < kDims; ++d) acc[g][d] = acc[g][d] * corr + pw * vr[d];
+            m[g] = mn;
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < kGroup; ++g) {
+        if (lane == 0) {
+            wm[warp][g] = m[g];
+            wl[warp][g] = l[g];
+        }
+#pragma unroll
+        for (int d = 0; d < kDims; ++d) wacc[warp][g][lane * kDims + d] = acc[g][d];
+    }
+    __syncthreads();
+    float* rec = ws + ((int64_t)(kvh * kAttnSplits + split) * kGroup) * kRec;
+    for (int e = threadIdx.x; e < kGroup * hd; e += kAttnWarps * 32) {
+        const int g = e / hd, d = e - g * hd;
+        float mx = -INFINITY;
+        for (int w = 0; w < kAttnWarps; ++w) mx = fmaxf(mx, wm[w][g]);
+        float num = 0.f, den = 0.f;
+        for (int w = 0; w < kAttnWarps; ++w) {
+            if (wm[w][g] == -INFINITY) continue;   // a warp that saw no position
+            const float f = expf(wm[w][g] - mx);
+            num += f * wacc[w][g][d];
+            den += f * wl[w][g];
+        }
+        rec[g * kRec + d] = num;
+        if (d == 0) {
+            rec[g * kRec + hd] = mx;
+            rec[g * kRec + hd + 1] = den;
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) last = atomicAdd(&counters[kvh], 1u) == kAttnSplits - 1;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    const float* base = ws + (int64_t)kvh * kAttnSplits * kGroup * kRec;
+    for (int e = threadIdx.x; e < kGroup * hd; e += kAttnWarps * 32) {
+        const int g = e / hd, d = e - g * hd;
+        float mx = -INFINITY;
+        for (int sp = 0; sp < kAttnSplits; ++sp) mx = fmaxf(mx, base[(sp * kGroup + g) * kRec + hd]);
+        float num = 0.f, den = 0.f;
+        for (int sp = 0; sp < kAttnSplits; ++sp) {
+            const float* r = base + (sp * kGroup + g) * kRec;
+            if (r[hd] == -INFINITY) continue;      // an empty split
+            const float f = expf(r[hd] - mx);
+            num += f * r[d];
+            den += f * r[hd + 1];
+        }
+        out[(int64_t)(kvh * kGroup + g) * hd + d] = __float2bfloat16_rn(num / den);
+    }
+    if (threadIdx.x == 0) counters[kvh] = 0u;
+}
+
+// Arg-max of n floats (first index of the maximum, as torch.argmax): every CTA
+// reduces a strided share, the last CTA to finish merges the per-CTA results.
+constexpr int kArgBlocks = 64;
+
+__global__ void __launch_bounds__(256) argmax_kernel(const float* __restrict__ x, int64_t n,
+                                                     int64_t* __restrict__ out, float* __restrict__ wv,
+                                                     int64_t* __restrict__ wi, unsigned* __restrict__ counter) {
+    __shared__ float sv[256];
+    __shared__ int64_t si[256];
+    __shared__ bool last;
+    float bv = -INFINITY;
+    int64_t bi = n;
+    for (int64_t i = blockIdx.x * 256 + threadIdx.x; i < n; i += (int64_t)gridDim.x * 256) {
+        const float v = x[i];
+        if (v > bv) {                                   // strided order: indices increase
+            bv = v;
+            bi = i;
+        }
+    }
+    sv[threadIdx.x] = bv;
+    si[threadIdx.x] = bi;
+    __syncthreads();
+    for (int s2 = 128; s2 > 0; s2 >>= 1) {
+        if (threadIdx.x < s2) {
+            const float ov = sv[threadIdx.x + s2];
+            const int64_t oi = si[threadIdx.x + s2];
+            if (ov > sv[threadIdx.x] || (ov == sv[threadIdx.x] && oi < si[threadIdx.x])) {
+                sv[threadIdx.x] = ov;
+                si[threadIdx.x] = oi;
+            }
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        wv[blockIdx.x] = sv[0];
+        wi[blockIdx.x] = si[0];
+        __threadfence();
+        last = atomicAdd(counter, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!last || threadIdx.x != 0) return;
+    __threadfence();
+    float v = wv[0];
+    int64_t id = wi[0];
+    for (unsigned b = 1; b < gridDim.x; ++b) {
+        const float ov = wv[b];
+        const int64_t oi = wi[b];
+        if (ov > v || (ov == v && oi < id)) {
+            v = ov;
+            id = oi;
+        }
+    }
+    *out = id;
+    *counter = 0u;
+}
+
+// One CTA per query head.  Warp w takes positions w, w + 8, ...: a lane holds
+// hd / 32 dimensions, the score is a warp sum, softmax is online per warp and
+// the warps are merged at the end (fixed order).
+template <int kDims>
+__global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(
+    const void* __restrict__ q, const void* __restrict__ k_cache, const void* __restrict__ v_cache,
+    const int64_t* __restrict__ pos, int H, int KV, float scale, void* __restrict__ out, int dtype) {
+    constexpr int hd = kDims * 32;
+    __shared__ float wm[kAttnWarps], wl[kAttnWarps];
+    __shared__ float wacc[kAttnWarps][hd];
+    const int head = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int kvh = head / (H / KV);
+    const int64_t P = pos[0];
+    float qv[kDims];
+#pragma unroll
+    for (int d = 0; d < kDims; ++d) qv[d] = load_f(q, dtype, (int64_t)head * hd + lane * kDims + d);
+    float m = -INFINITY, l = 0.f, acc[kDims];
+#pragma unroll
+    for (int d = 0; d < kDims; ++d) acc[d] = 0.f;
+    for (int64_t t = warp; t <= P; t += kAttnWarps) {
+        const int64_t kb = (t * KV + kvh) * hd + lane * kDims;
+        float s = 0.f;
+#pragma unroll
+        for (int d = 0; d < kDims; ++d) s += qv[d] * load_f(k_cache, dtype, kb + d);
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        s *= scale;
+        const float mn = fmaxf(m, s);
+        const float corr = expf(m - mn), pw = expf(s - mn);
+        l = l * corr + pw;
+#pragma unroll
+        for (int d = 0; d < kDims; ++d) acc[d] = acc[d] * corr + pw * load_f(v_cache, dtype, kb + d);
+        m = mn;
+    }
+    if (lane == 0) {
+        wm[warp] = m;
+        wl[warp] = l;
+    }
+#pragma unroll
+    for (int d = 0; d < kDims; ++d) wacc[warp][lane * kDims + d] = acc[d];
+    __syncthreads();
+    for (int d = threadIdx.x; d < hd; d += kAttnWarps * 32) {
+        float mx = -INFINITY;
+        for (int w = 0; w < kAttnWarps; ++w) mx = fmaxf(mx, wm[w]);
+        float num = 0.f, den = 0.f;
+        for (int w = 0; w < kAttnWarps; ++w) {
+            if (wm[w] == -INFINITY) continue;      // a warp that saw no position
+            const float f = expf(wm[w] - mx);
+            num += f * wacc[w][d];
+            den += f * wl[w];
+        }
+        store_f(out, dtype, (int64_t)head * hd + d, num / den);
+    }
+}
+
+__global__ void silu_mul_kernel(const void* __restrict__ g, const void* __restrict__ u,
+                                void* __restrict__ out, int64_t n, int dtype) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const float gv = load_f(g, dtype, i);
+        store_f(out, dtype, i, gv / (1.f + expf(-gv)) * load_f(u, dtype, i));
+    }
+}
+
+bool glue_dtype_ok(int d) { return d == EPQ_F32 || d == EPQ_F16 || d == EPQ_BF16; }
+
+}  // namespace
+}  // namespace epq
+
+using namespace epq;
+
+extern "C" {
+
+int epq_add_rmsnorm(const void* x, const void* add, void* h_out, void* y, int64_t m, int64_t n,
+                    float eps, int32_t dtype, void* stream) {
+    if (!x || !y || m < 0 || n <= 0) return set_error(EPQ_EINVAL, "epq_add_rmsnorm: bad arguments");
+    if (!glue_dtype_ok(dtype)) return set_error(EPQ_EDTYPE, "epq_add_rmsnorm: dtype %d", dtype);
+    if (n > 12288) return set_error(EPQ_EUNSUPPORTED, "epq_add_rmsnorm: n=%lld > 12288", (long long)n);
+    if (m == 0) return EPQ_OK;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const bool aligned = ((uintptr_t)x | (uintptr_t)add | (uintptr_t)h_out | (uintptr_t)y) % 16 == 0;
+    if (dtype == EPQ_BF16 && aligned && n % 256 == 0 && n / 8 <= 1024) {
+        add_rmsnorm_bf16x8_kernel<<<(unsigned)m, (unsigned)(n / 8), 0, st>>>(
+            static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(add),
+            static_cast<__nv_bfloat16*>(h_out), static_cast<__nv_bfloat16*>(y), n, eps);
+    } else {
+        add_rmsnorm_kernel<<<(unsigned)m, kNormThreads, n * sizeof(float), st>>>(x, add, h_out, y, n, eps,
+                                                                                 dtype);
+    }
+    return check_launch("epq_add_rmsnorm");
+}
+
+int epq_rope_kv(void* q, const void* k, const void* v, const int64_t* pos, int64_t m, int32_t heads,
+                int32_t kv_heads, int32_t head_dim, const float* cos_tab, const float* sin_tab,
+                void* k_cache, void* v_cache, int32_t qk_norm, float eps, int32_t dtype, void* stream) {
+    if (!q || !k || !v || !pos || !cos_tab || !sin_tab || !k_cache || !v_cache || m < 0)
+        return set_error(EPQ_EINVAL, "epq_rope_kv: bad arguments");
+    if (!glue_dtype_ok(dtype)) return set_error(EPQ_EDTYPE, "epq_rope_kv: dtype %d", dtype);
+    if ((head_dim != 64 && head_dim != 128 && head_dim != 256) || heads <= 0 || kv_heads <= 0 ||
+        heads % kv_heads)
+        return set_error(EPQ_EUNSUPPORTED, "epq_rope_kv: head_dim=%d (64, 128 or 256), heads=%d, kv_heads=%d",
+                         head_dim, heads, kv_heads);
+    if (m == 0) return EPQ_OK;
+    rope_kv_kernel<<<dim3((unsigned)m, heads + kv_heads), head_dim / 2, 0, static_cast<cudaStream_t>(stream)>>>(
+        q, k, v, pos, heads, kv_heads, head_dim, cos_tab, sin_tab, k_cache, v_cache, qk_norm, eps, dtype);
+    return check_launch("epq_rope_kv");
+}
+
+int64_t epq_attn_decode_workspace_bytes(int32_t heads, int32_t kv_heads, int32_t head_dim) {
+    if (heads <= 0 || kv_heads <= 0 || heads % kv_heads || head_dim <= 0) return 0;
+    return 256 + (int64_t)kv_heads * kAttnSplits * (heads / kv_heads) * (head_dim + 2) * 4;
+}
+
+int epq_attn_decode(const void* q, const void* k_cache, const void* v_cache, const int64_t* pos,
+                    int32_t heads, int32_t kv_heads, int32_t head_dim, float scale, void* out,
+                    int32_t dtype, void* workspace, int64_t workspace_bytes, void* stream) {
+    if (!q || !k_cache || !v_cache || !pos || !out || heads <= 0 || kv_heads <= 0 || heads % kv_heads)
+        return set_error(EPQ_EINVAL, "epq_attn_decode: bad arguments");
+    if (!glue_dtype_ok(dtype)) return set_error(EPQ_EDTYPE, "epq_attn_decode: dtype %d", dtype);
+    if (head_dim != 64 && head_dim != 128)
+        return set_error(EPQ_EUNSUPPORTED, "epq_attn_decode: head_dim=%d (64 or 128)", head_dim);
+    if (kv_heads > 256) return set_error(EPQ_EUNSUPPORTED, "epq_attn_decode: kv_heads=%d > 256", kv_heads);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int group = heads / kv_heads;
+    const bool split = dtype == EPQ_BF16 && workspace &&
+                       (group == 1 || group == 2 || group == 4 || group == 8);
+    if (split) {
+        if (workspace_bytes < epq_attn_decode_workspace_bytes(heads, kv_heads, head_dim) ||
+            (uintptr_t)workspace % 256)
+            return set_error(EPQ_EWORKSPACE, "epq_attn_decode: workspace of %lld bytes (need %lld, 256-aligned)",
+                             (long long)workspace_bytes,
+                             (long long)epq_attn_decode_workspace_bytes(heads, kv_heads, head_dim));
+        unsigned* ctr = static_cast<unsigned*>(workspace);
+        float* ws = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + 256);
+        const auto* qb = static_cast<const __nv_bfloat16*>(q);
+        const auto* kb = static_cast<const __nv_bfloat16*>(k_cache);
+        const auto* vb = static_cast<const __nv_bfloat16*>(v_cache);
+        auto* ob = static_cast<__nv_bfloat16*>(out);
+        const dim3 grid(kv_heads, kAttnSplits);
+#define EPQ_ATTN_SPLIT(D, G) attn_split_kernel<D, G><<<grid, kAttnWarps * 32, 0, st>>>(qb, kb, vb, pos, kv_heads, \
+                                                                                   scale, ob, ws, ctr)
+        if (head_dim == 128) {
+            if (group == 1) EPQ_ATTN_SPLIT(4, 1);
+            else if (group == 2) EPQ_ATTN_SPLIT(4, 2);
+            else if (group == 4) EPQ_ATTN_SPLIT(4, 4);
+            else EPQ_ATTN_SPLIT(4, 8);
+        } else {
+            if (group == 1) EPQ_ATTN_SPLIT(2, 1);
+            else if (group == 2) EPQ_ATTN_SPLIT(2, 2);
+            else if (group == 4) EPQ_ATTN_SPLIT(2, 4);
+            else EPQ_ATTN_SPLIT(2, 8);
+        }
+#undef EPQ_ATTN_SPLIT
+    } else if (head_dim == 128) {
+        attn_decode_kernel<4><<<heads, kAttnWarps * 32, 0, st>>>(q, k_cache, v_cache, pos, heads, kv_heads,
+                                                                  scale, out, dtype);
+    } else {
+        attn_decode_kernel<2><<<heads, kAttnWarps * 32, 0, st>>>(q, k_cache, v_cache, pos, heads, kv_heads,
+                                                                  scale, out, dtype);
+    }
+    return check_launch("epq_attn_decode");
+}
+
+int64_t epq_argmax_workspace_bytes(void) { return 256 + kArgBlocks * (4 + 8); }
+
+int epq_argmax(const float* x, int64_t n, int64_t* out, void* workspace, int64_t workspace_bytes,
+               void* stream) {
+    if (!x || !out || n <= 0 || !workspace) return set_error(EPQ_EINVAL, "epq_argmax: bad arguments");
+    if (workspace_bytes < epq_argmax_workspace_bytes() || (uintptr_t)workspace % 256)
+        return set_error(EPQ_EWORKSPACE, "epq_argmax: workspace of %lld bytes (need %lld, 256-aligned)",
+                         (long long)workspace_bytes, (long long)epq_argmax_workspace_bytes());
+    uint8_t* w = static_cast<uint8_t*>(workspace);
+    argmax_kernel<<<kArgBlocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        x, n, out, reinterpret_cast<float*>(w + 256), reinterpret_cast<int64_t*>(w + 256 + kArgBlocks * 4),
+        reinterpret_cast<unsigned*>(w));
+    return check_launch("epq_argmax");
+}
+
+int epq_silu_mul(const void* g, const void* u, void* out, int64_t n, int32_t dtype, void* stream) {
+    if (!g || !u || !out || n < 0) return set_error(EPQ_EINVAL, "epq_silu_mul: bad arguments");
+    if (!glue_dtype_ok(dtype)) return set_error(EPQ_EDTYPE, "epq_silu_mul: dtype %d", dtype);
+    if (n == 0) return EPQ_OK;
+    const int64_t blocks = (n + 255) / 256;
+    silu_mul_kernel<<<(unsigned)(blocks < 1184 ? blocks : 1184), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        g, u, out, n, dtype);
+    return check_launch("epq_silu_mul");
+}
+
+}  // extern "C"

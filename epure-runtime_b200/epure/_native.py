@@ -52,6 +52,8 @@ EXPORTS = (
     "epq_relayout", "epq_linear_workspace_bytes", "epq_linear_multi", "epq_linear",
     "epq_linear_bwd", "epq_materialize", "epq_linear_noalloc", "epq_linear_noalloc_max_scratch",
     "epq_chain_workspace_bytes", "epq_chain_prepare", "epq_chain_run", "epq_chain_set_tp",
+    "epq_add_rmsnorm", "epq_rope_kv", "epq_attn_decode", "epq_attn_decode_workspace_bytes",
+    "epq_silu_mul", "epq_argmax", "epq_argmax_workspace_bytes",
 )
 
 _lib = None
@@ -91,6 +93,16 @@ def load_library(path=None):
         lib.epq_chain_run.argtypes = [P, P, I32, P, I32, P]
         lib.epq_chain_set_tp.argtypes = [P, I32, I32, ctypes.POINTER(P), ctypes.POINTER(ctypes.c_uint8),
                                          I32, P]
+        F32 = ctypes.c_float
+        lib.epq_add_rmsnorm.argtypes = [P, P, P, P, I64, I64, F32, I32, P]
+        lib.epq_rope_kv.argtypes = [P, P, P, P, I64, I32, I32, I32, P, P, P, P, I32, F32, I32, P]
+        lib.epq_attn_decode.argtypes = [P, P, P, P, I32, I32, I32, F32, P, I32, P, I64, P]
+        lib.epq_attn_decode_workspace_bytes.restype = I64
+        lib.epq_attn_decode_workspace_bytes.argtypes = [I32, I32, I32]
+        lib.epq_argmax.argtypes = [P, I64, P, P, I64, P]
+        lib.epq_argmax_workspace_bytes.restype = I64
+        lib.epq_argmax_workspace_bytes.argtypes = []
+        lib.epq_silu_mul.argtypes = [P, P, P, I64, I32, P]
         for name in EXPORTS:
             getattr(lib, name)          # every declared entry point must be exported
         if lib.epq_abi_version() != 1:
@@ -319,3 +331,68 @@ def device_error():
     flag = ctypes.c_int(0)
     _check(lib.epq_device_error(ctypes.byref(flag)), "epq_device_error")
     return flag.value
+
+
+# -- decode-step glue (include/epq_decode.h) ------------------------------------------
+
+def _ptr(t):
+    return t.data_ptr() if t is not None else None
+
+
+def add_rmsnorm(x, add=None, h_out=None, eps=1e-6):
+    """(h, y): h = x + add (or x), y = RMSNorm(h) with weight 1, row-wise over the last dim."""
+    lib = load_library()
+    n = x.shape[-1]
+    m = x.numel() // n
+    y = torch.empty_like(x)
+    _check(lib.epq_add_rmsnorm(x.data_ptr(), _ptr(add), _ptr(h_out), y.data_ptr(), m, n, eps,
+                               dtype_code(x.dtype), _stream_ptr(x.device)), "epq_add_rmsnorm")
+    return y
+
+
+def rope_kv(q, k, v, pos, cos, sin, k_cache, v_cache, qk_norm, eps=1e-6):
+    """Rotates q [m, H, hd] in place and writes rotated k and v at ``pos`` into the caches."""
+    lib = load_library()
+    m, H, hd = q.shape
+    _check(lib.epq_rope_kv(q.data_ptr(), k.data_ptr(), v.data_ptr(), pos.data_ptr(), m, H,
+                           k.shape[1], hd, cos.data_ptr(), sin.data_ptr(), k_cache.data_ptr(),
+                           v_cache.data_ptr(), int(qk_norm), eps, dtype_code(q.dtype),
+                           _stream_ptr(q.device)), "epq_rope_kv")
+
+
+def attn_decode_workspace(heads, kv_heads, head_dim, device):
+    """A zeroed workspace for attn_decode (reusable by consecutive calls on one stream)."""
+    n = load_library().epq_attn_decode_workspace_bytes(heads, kv_heads, head_dim)
+    return torch.zeros(n, dtype=torch.uint8, device=device)
+
+
+def attn_decode(q, k_cache, v_cache, pos, scale, ws=None):
+    """One query token against cache positions 0..pos[0]; q [H, hd] -> [H, hd]."""
+    lib = load_library()
+    H, hd = q.shape[-2], q.shape[-1]
+    out = torch.empty((H, hd), dtype=q.dtype, device=q.device)
+    _check(lib.epq_attn_decode(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), pos.data_ptr(),
+                               H, k_cache.shape[-2], hd, scale, out.data_ptr(), dtype_code(q.dtype),
+                               _ptr(ws), ws.numel() if ws is not None else 0,
+                               _stream_ptr(q.device)), "epq_attn_decode")
+    return out
+
+
+def argmax_workspace(device):
+    return torch.zeros(load_library().epq_argmax_workspace_bytes(), dtype=torch.uint8, device=device)
+
+
+def argmax(x, out, ws):
+    """out[0] (int64, device) = the first index of the maximum of the float32 vector x."""
+    lib = load_library()
+    _check(lib.epq_argmax(x.data_ptr(), x.numel(), out.data_ptr(), ws.data_ptr(), ws.numel(),
+                          _stream_ptr(x.device)), "epq_argmax")
+    return out
+
+
+def silu_mul(g, u):
+    lib = load_library()
+    out = torch.empty_like(g)
+    _check(lib.epq_silu_mul(g.data_ptr(), u.data_ptr(), out.data_ptr(), g.numel(), dtype_code(g.dtype),
+                            _stream_ptr(g.device)), "epq_silu_mul")
+    return out

@@ -1,0 +1,65 @@
+/* epq_decode.h -- decode-step glue around the packed linears (libepq.so).
+ *
+ * Not part of the reference's op interface (include/epq.h): the reference leaves
+ * the non-linear parts of a decoder block to the Hugging Face model around its
+ * PackedLinear modules (epure/runtime.py:214-305 swaps only the linears).  These
+ * entry points do those parts for one decode token in one launch each, so a
+ * whole-token CUDA graph is made of the packed linears, these, and the lm_head.
+ * Conventions are those of epq.h: plain pointers, epq_dtype codes, a cudaStream_t
+ * passed as void*, EPQ_OK or a negative status with epq_last_error().  Positions
+ * are read from device memory (int64), so a captured step replays at any position.
+ */
+#ifndef EPQ_DECODE_H
+#define EPQ_DECODE_H
+
+#include <stdint.h>
+
+#include "epq.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* For each of m rows of n values (n <= 12288): h = x + add (rounded to dtype;
+ * add may be NULL), optionally stored to h_out (may be NULL), and
+ * y = h * rsqrt(mean(h^2) + eps) (RMSNorm with weight 1). */
+int epq_add_rmsnorm(const void* x, const void* add, void* h_out, void* y, int64_t m, int64_t n,
+                    float eps, int32_t dtype, void* stream);
+
+/* For m rows at positions pos[m] (device): q [m, heads, head_dim] is rotated in
+ * place; k, v [m, kv_heads, head_dim] are written to k_cache / v_cache
+ * [max_len, kv_heads, head_dim] at those positions, k rotated.  qk_norm != 0
+ * first applies RMSNorm (weight 1, eps) over each head of q and k (Qwen3).
+ * RoPE is rotate-half with cos_tab / sin_tab [max_len, head_dim / 2] (float32).
+ * head_dim 64, 128 or 256. */
+int epq_rope_kv(void* q, const void* k, const void* v, const int64_t* pos, int64_t m, int32_t heads,
+                int32_t kv_heads, int32_t head_dim, const float* cos_tab, const float* sin_tab,
+                void* k_cache, void* v_cache, int32_t qk_norm, float eps, int32_t dtype, void* stream);
+
+/* One query token: out[h] = softmax(scale * q[h] . K[0..pos[0]]) V for every head h
+ * (grouped-query: head h reads kv head h / (heads / kv_heads)); q, out [heads, head_dim],
+ * caches [max_len, kv_heads, head_dim]; head_dim 64 or 128.  With bf16 and a
+ * workspace (heads / kv_heads of 1, 2, 4 or 8) the positions are split over
+ * kv_heads x 16 CTAs and merged by the last one; the workspace
+ * (epq_attn_decode_workspace_bytes, 256-byte aligned) must be zeroed once before
+ * first use and is left ready for the next call.  Without one, one CTA per head. */
+int64_t epq_attn_decode_workspace_bytes(int32_t heads, int32_t kv_heads, int32_t head_dim);
+int epq_attn_decode(const void* q, const void* k_cache, const void* v_cache, const int64_t* pos,
+                    int32_t heads, int32_t kv_heads, int32_t head_dim, float scale, void* out,
+                    int32_t dtype, void* workspace, int64_t workspace_bytes, void* stream);
+
+/* *out = the first index of the maximum of x[0..n) (torch.argmax), on the device.
+ * workspace: epq_argmax_workspace_bytes(), 256-byte aligned, zeroed once before first
+ * use (left ready for the next call). */
+int64_t epq_argmax_workspace_bytes(void);
+int epq_argmax(const float* x, int64_t n, int64_t* out, void* workspace, int64_t workspace_bytes,
+               void* stream);
+
+/* out = silu(g) * u over n values. */
+int epq_silu_mul(const void* g, const void* u, void* out, int64_t n, int32_t dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EPQ_DECODE_H */

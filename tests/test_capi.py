@@ -1,4 +1,4 @@
-"""The C-ABI library loads, exports every entry point include/epq.h declares, and
+"""The C-ABI library loads, exports every entry point include/*.h declares, and
 validates its arguments on the host (no kernel is launched here)."""
 import ctypes
 import os
@@ -10,9 +10,13 @@ from conftest import ROOT
 
 
 def _declared():
-    src = open(os.path.join(ROOT, "include", "epq.h")).read()
-    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
-    return sorted(set(re.findall(r"\b(epq_[a-z0-9_]+)\s*\(", src)))
+    names = set()
+    for h in sorted(os.listdir(os.path.join(ROOT, "include"))):
+        if h.endswith(".h"):
+            src = open(os.path.join(ROOT, "include", h)).read()
+            src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+            names |= set(re.findall(r"\b(epq_[a-z0-9_]+)\s*\(", src))
+    return sorted(names)
 
 
 @pytest.fixture(scope="module")
