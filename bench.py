@@ -418,7 +418,7 @@ def run_model(args, rank, world, local_rank):
     prompt_len = 128
     max_len = prompt_len + args.warmup + args.steps + 2
     dec = PackedDecoder(shapes, layers=args.layers, device=dev, seed=1000 * rank, max_len=max_len,
-                        fp32_logits=False).capture()
+                        fp32_logits=False, gpu_layout=args.layout).capture()
     g = torch.Generator().manual_seed(rank)
     prompt = torch.randint(0, shapes.vocab, (prompt_len,), generator=g)
 
@@ -482,7 +482,7 @@ def run_model(args, rank, world, local_rank):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
             "config": {"workload": f"{args.model} greedy decode after a {prompt_len}-token prompt"
-                                   + layers_note,
+                                   + layers_note, "layout": args.layout,
                        "mode": "model", "global_batch": world, "seq_len": max_len,
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                        "l2": f"inputs larger than L2 ({step_bytes / 1e9:.2f} GB moved per step)",
@@ -491,7 +491,9 @@ def run_model(args, rank, world, local_rank):
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak,
                          "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
                          "peak_kind": peak_kind,
-                         "kernel": "whole token graph: gemv_mma_kernel (packed) + torch/cuBLAS",
+                         "kernel": ("whole token graph: " + ("gemv_mma_kernel" if args.layout == "mma16"
+                                                              else "gemv_lut_kernel") +
+                                    " (packed) + decode glue kernels + cuBLAS lm_head"),
                          "traffic": None},
             "e2e": {"value": round(world * 1000.0 / e2e_ms, 2), "unit": UNIT,
                     "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8},
@@ -697,6 +699,9 @@ def main():
     ap.add_argument("--batch", type=int, default=1,
                     help="decode batch (tokens per step) for --mode per-linear: M rows through "
                          "every linear (tensor-core GEMV up to 16, the tcgen05 GEMM above)")
+    ap.add_argument("--layout", choices=["mma16", "tiled"], default="mma16",
+                    help="--mode model: index layout of the packed stores (tensor-core GEMV or LUT GEMV "
+                         "at batch 1)")
     ap.add_argument("--tp", action="store_true",
                     help="at N > 1: one model tensor-parallel over the N GPUs instead of N replicas")
     ap.add_argument("--fallback", action="store_true",

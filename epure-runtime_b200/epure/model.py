@@ -44,7 +44,7 @@ _EPS = {"qwen3-1.7b": 1e-6, "llama3-8b": 1e-5, "llama3-70b": 1e-5}
 class PackedDecoder:
     def __init__(self, shapes, layers=None, device="cuda", seed=0, max_len=512,
                  linear_mode="ours", stack=None, embed=None, lm_head=None, fp32_logits=True,
-                 fused_glue=True):
+                 fused_glue=True, gpu_layout="mma16"):
         if linear_mode not in ("ours", "reference", "fp32"):
             raise ValueError("linear_mode must be 'ours', 'reference' or 'fp32'")
         self.shapes = shapes
@@ -52,7 +52,7 @@ class PackedDecoder:
         self.mode = linear_mode
         self.dtype = torch.float32 if linear_mode == "fp32" else torch.bfloat16
         self.stack = stack if stack is not None else LinearStack(
-            shapes, layers=layers, device=device, seed=seed, gpu_layout="mma16")
+            shapes, layers=layers, device=device, seed=seed, gpu_layout=gpu_layout)
         self.layers = self.stack.layers
         self.max_len = max_len
         h, hd = shapes.hidden, shapes.head_dim
