@@ -109,6 +109,10 @@ constexpr int kDynSmem = (int)kWindowEnd;
 constexpr uint32_t kWaitLimit = 1u << 22;   // mbarrier polls
 constexpr uint32_t kSpinLimit = 1u << 22;   // grid-barrier polls
 
+// from base: per-rank slice sums of a tensor-parallel step [kMaxTp][128] fp32
+constexpr uint32_t kXrOff = kDescOff + 3 * (uint32_t)sizeof(ChainStepD);
+static_assert(kXrOff % 16 == 0, "rank slice buffer alignment");
+
 __device__ int g_chain_error = 0;
 
 __device__ __forceinline__ uint32_t stage_addr(int s) {
@@ -269,7 +273,7 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
                                                             int x_dtype, void* out, int out_dtype) {
     extern __shared__ __align__(128) uint8_t smem[];
     const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
-    if (base + kDescOff + 3 * (uint32_t)sizeof(ChainStepD) > kLowStages ||
+    if (base + kXrOff + kMaxTp * 512u > kLowStages ||
         (int)gridDim.x != reinterpret_cast<const int*>(ws)[1]) {
         // placement the addresses below rely on, or a grid other than the one
         // the descriptors were built for
@@ -514,11 +518,15 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
                 cur_g = g;
                 consumers_sync();
                 if (j > 0 && S.remote && new_g) {
-                    // Tensor parallel: this rank's sum of the slice is published (tagged) in
-                    // xred; every rank adds all ranks' sums in rank order, so all ranks build
-                    // the same table from the same x.
-                    if (warp == 0) {
-                        float* xsl = xs_buf + xsp * (kXGroups * 128);
+                    // Tensor parallel: every rank publishes its own sum of the slice (tagged)
+                    // in xred and adds all ranks' sums in rank order, so all ranks build the
+                    // same table from the same x.  Warp w brings rank w's sum into shared
+                    // memory (warp my_rank: its own, after publishing it), so the peers'
+                    // NVLink round trips overlap instead of following each other.
+                    float* xsl = xs_buf + xsp * (kXGroups * 128);
+                    float4* xr = reinterpret_cast<float4*>(smem + kXrOff);      // [kMaxTp][32]
+                    const int64_t e0 = (int64_t)((j - 1) % 3) * H.xred_elems + (int64_t)g * 128 + 4 * lane;
+                    if (warp == my_rank) {
                         const float4* x4 = reinterpret_cast<const float4*>(xsl);
                         float4 loc = x4[lane];
 #pragma unroll
@@ -529,30 +537,30 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
                             loc.z += u.z;
                             loc.w += u.w;
                         }
-                        const int64_t e0 = (int64_t)((j - 1) % 3) * H.xred_elems + (int64_t)g * 128 + 4 * lane;
                         uint64_t* mine = reinterpret_cast<uint64_t*>(const_cast<uint8_t*>(ws) + H.xred_off) + e0;
                         stg_u64x2(mine, tagged(loc.x, want), tagged(loc.y, want));
                         stg_u64x2(mine + 2, tagged(loc.z, want), tagged(loc.w, want));
+                        xr[warp * 32 + lane] = loc;
+                    } else if (warp < world) {
+                        const uint64_t* src = reinterpret_cast<const uint64_t*>(H.peer_ws[warp] + H.xred_off) + e0;
+                        ulonglong2 a = ldsys_u64x2(src), b = ldsys_u64x2(src + 2);
+                        uint32_t spins = 0;
+                        while ((tag_of(a.x) != want) | (tag_of(a.y) != want) | (tag_of(b.x) != want) |
+                               (tag_of(b.y) != want)) {
+                            if (++spins > kTagSpinLimit || *reinterpret_cast<volatile int*>(&g_chain_error)) {
+                                atomicExch(&g_chain_error, 1);
+                                break;
+                            }
+                            a = ldsys_u64x2(src);
+                            b = ldsys_u64x2(src + 2);
+                        }
+                        xr[warp * 32 + lane] = make_float4(val_of(a.x), val_of(a.y), val_of(b.x), val_of(b.y));
+                    }
+                    consumers_sync();
+                    if (warp == 0) {
                         float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
                         for (int rk = 0; rk < world; ++rk) {
-                            float4 r4 = loc;
-                            if (rk != my_rank) {
-                                const uint64_t* src =
-                                    reinterpret_cast<const uint64_t*>(H.peer_ws[rk] + H.xred_off) + e0;
-                                ulonglong2 a = ldsys_u64x2(src), b = ldsys_u64x2(src + 2);
-                                uint32_t spins = 0;
-                                while ((tag_of(a.x) != want) | (tag_of(a.y) != want) | (tag_of(b.x) != want) |
-                                       (tag_of(b.y) != want)) {
-                                    if (++spins > kTagSpinLimit ||
-                                        *reinterpret_cast<volatile int*>(&g_chain_error)) {
-                                        atomicExch(&g_chain_error, 1);
-                                        break;
-                                    }
-                                    a = ldsys_u64x2(src);
-                                    b = ldsys_u64x2(src + 2);
-                                }
-                                r4 = make_float4(val_of(a.x), val_of(a.y), val_of(b.x), val_of(b.y));
-                            }
+                            const float4 r4 = xr[rk * 32 + lane];
                             x.x += r4.x;
                             x.y += r4.y;
                             x.z += r4.z;
@@ -704,33 +712,35 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
             v += __shfl_xor_sync(0xffffffffu, v, 1);
             v += __shfl_xor_sync(0xffffffffu, v, 2);
             v += __shfl_xor_sync(0xffffffffu, v, 4);
-            if (r < r1 && sub8 == 0) {
-                if (world > 1 && H.final_remote) {
-                    const uint32_t tfin = tag_base + (uint32_t)n_steps;
-                    uint64_t* mine = reinterpret_cast<uint64_t*>(const_cast<uint8_t*>(ws) + H.xfin_off) + r;
-                    asm volatile("st.global.u64 [%0], %1;" ::"l"(mine), "l"(tagged(v, tfin)) : "memory");
-                    float x = 0.f;
-                    for (int rk = 0; rk < world; ++rk) {
-                        float rv = v;
-                        if (rk != my_rank) {
-                            const uint64_t* src = reinterpret_cast<const uint64_t*>(H.peer_ws[rk] + H.xfin_off) + r;
-                            uint64_t e = ldsys_u64(src);
-                            uint32_t spins = 0;
-                            while (tag_of(e) != tfin) {
-                                if (++spins > kTagSpinLimit || *reinterpret_cast<volatile int*>(&g_chain_error)) {
-                                    atomicExch(&g_chain_error, 1);
-                                    break;
-                                }
-                                e = ldsys_u64(src);
+            if (world > 1 && H.final_remote) {
+                // Sum over ranks: lane sub8 of the row's 8 brings rank sub8's row sum (its
+                // own after publishing it), then every lane adds them in rank order.
+                const uint32_t tfin = tag_base + (uint32_t)n_steps;
+                float rv = 0.f;
+                if (r < r1 && sub8 < world) {
+                    if (sub8 == my_rank) {
+                        uint64_t* mine = reinterpret_cast<uint64_t*>(const_cast<uint8_t*>(ws) + H.xfin_off) + r;
+                        asm volatile("st.global.u64 [%0], %1;" ::"l"(mine), "l"(tagged(v, tfin)) : "memory");
+                        rv = v;
+                    } else {
+                        const uint64_t* src = reinterpret_cast<const uint64_t*>(H.peer_ws[sub8] + H.xfin_off) + r;
+                        uint64_t e = ldsys_u64(src);
+                        uint32_t spins = 0;
+                        while (tag_of(e) != tfin) {
+                            if (++spins > kTagSpinLimit || *reinterpret_cast<volatile int*>(&g_chain_error)) {
+                                atomicExch(&g_chain_error, 1);
+                                break;
                             }
-                            rv = val_of(e);
+                            e = ldsys_u64(src);
                         }
-                        x += rv;
+                        rv = val_of(e);
                     }
-                    v = x;
                 }
-                store_f(out, out_dtype, r, v);
+                float x = 0.f;
+                for (int rk = 0; rk < world; ++rk) x += __shfl_sync(0xffffffffu, rv, (lane & ~7) + rk);
+                v = x;
             }
+            if (r < r1 && sub8 == 0) store_f(out, out_dtype, r, v);
         }
     }
     consumers_sync();
