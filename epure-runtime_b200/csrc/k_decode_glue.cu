@@ -23,6 +23,32 @@
 namespace epq {
 namespace {
 
+// Programmatic dependent launch: every glue kernel is launched allowed to start
+// while the previous kernel in the stream is still running; it lets its own
+// dependents launch at once and waits for the previous grid's completion (and
+// memory) before reading anything that grid wrote.
+__device__ __forceinline__ void pdl_enter() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, const char* what,
+               Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+    return check_launch(what);
+}
+
 template <int kThreads>
 __device__ __forceinline__ float block_sum(float v, float* red) {
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -43,6 +69,7 @@ constexpr int kNormThreads = 512;
 __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(
     const void* __restrict__ x, const void* __restrict__ add, void* __restrict__ h_out,
     void* __restrict__ y, int64_t n, float eps, int dtype) {
+    pdl_enter();
     extern __shared__ float hs[];
     __shared__ float red[32];
     const int64_t row = blockIdx.x;
@@ -69,6 +96,7 @@ __global__ void __launch_bounds__(128) rope_kv_kernel(
     const int64_t* __restrict__ pos, int H, int KV, int hd, const float* __restrict__ cos_t,
     const float* __restrict__ sin_t, void* __restrict__ k_cache, void* __restrict__ v_cache,
     int qk_norm, float eps, int dtype) {
+    pdl_enter();
     __shared__ float red[32];
     const int64_t row = blockIdx.x;
     const int head = blockIdx.y;
@@ -107,6 +135,7 @@ __global__ void __launch_bounds__(128) rope_kv_kernel(
 __global__ void __launch_bounds__(1024) add_rmsnorm_bf16x8_kernel(
     const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ add,
     __nv_bfloat16* __restrict__ h_out, __nv_bfloat16* __restrict__ y, int64_t n, float eps) {
+    pdl_enter();
     __shared__ float red[32];
     const int64_t off = blockIdx.x * n + 8 * threadIdx.x;
     const uint4 xr = *reinterpret_cast<const uint4*>(x + off);
@@ -158,6 +187,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_split_kernel(
     const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k_cache,
     const __nv_bfloat16* __restrict__ v_cache, const int64_t* __restrict__ pos, int KV, float scale,
     __nv_bfloat16* __restrict__ out, float* __restrict__ ws, unsigned* __restrict__ counters) {
+    pdl_enter();
     constexpr int hd = kDims * 32;
     constexpr int kRec = hd + 2;                       // acc[hd], max, sum
     __shared__ float wm[kAttnWarps][kGroup], wl[kAttnWarps][kGroup];
@@ -261,6 +291,7 @@ constexpr int kArgBlocks = 64;
 __global__ void __launch_bounds__(256) argmax_kernel(const float* __restrict__ x, int64_t n,
                                                      int64_t* __restrict__ out, float* __restrict__ wv,
                                                      int64_t* __restrict__ wi, unsigned* __restrict__ counter) {
+    pdl_enter();
     __shared__ float sv[256];
     __shared__ int64_t si[256];
     __shared__ bool last;
@@ -317,6 +348,7 @@ template <int kDims>
 __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(
     const void* __restrict__ q, const void* __restrict__ k_cache, const void* __restrict__ v_cache,
     const int64_t* __restrict__ pos, int H, int KV, float scale, void* __restrict__ out, int dtype) {
+    pdl_enter();
     constexpr int hd = kDims * 32;
     __shared__ float wm[kAttnWarps], wl[kAttnWarps];
     __shared__ float wacc[kAttnWarps][hd];
@@ -366,6 +398,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(
 
 __global__ void silu_mul_kernel(const void* __restrict__ g, const void* __restrict__ u,
                                 void* __restrict__ out, int64_t n, int dtype) {
+    pdl_enter();
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x) {
         const float gv = load_f(g, dtype, i);
@@ -391,14 +424,13 @@ int epq_add_rmsnorm(const void* x, const void* add, void* h_out, void* y, int64_
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const bool aligned = ((uintptr_t)x | (uintptr_t)add | (uintptr_t)h_out | (uintptr_t)y) % 16 == 0;
     if (dtype == EPQ_BF16 && aligned && n % 256 == 0 && n / 8 <= 1024) {
-        add_rmsnorm_bf16x8_kernel<<<(unsigned)m, (unsigned)(n / 8), 0, st>>>(
-            static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(add),
-            static_cast<__nv_bfloat16*>(h_out), static_cast<__nv_bfloat16*>(y), n, eps);
-    } else {
-        add_rmsnorm_kernel<<<(unsigned)m, kNormThreads, n * sizeof(float), st>>>(x, add, h_out, y, n, eps,
-                                                                                 dtype);
+        return launch_pdl(add_rmsnorm_bf16x8_kernel, dim3((unsigned)m), dim3((unsigned)(n / 8)), 0, st,
+                          "epq_add_rmsnorm", static_cast<const __nv_bfloat16*>(x),
+                          static_cast<const __nv_bfloat16*>(add), static_cast<__nv_bfloat16*>(h_out),
+                          static_cast<__nv_bfloat16*>(y), n, eps);
     }
-    return check_launch("epq_add_rmsnorm");
+    return launch_pdl(add_rmsnorm_kernel, dim3((unsigned)m), dim3(kNormThreads), n * sizeof(float), st,
+                      "epq_add_rmsnorm", x, add, h_out, y, n, eps, (int)dtype);
 }
 
 int epq_rope_kv(void* q, const void* k, const void* v, const int64_t* pos, int64_t m, int32_t heads,
@@ -412,9 +444,10 @@ int epq_rope_kv(void* q, const void* k, const void* v, const int64_t* pos, int64
         return set_error(EPQ_EUNSUPPORTED, "epq_rope_kv: head_dim=%d (64, 128 or 256), heads=%d, kv_heads=%d",
                          head_dim, heads, kv_heads);
     if (m == 0) return EPQ_OK;
-    rope_kv_kernel<<<dim3((unsigned)m, heads + kv_heads), head_dim / 2, 0, static_cast<cudaStream_t>(stream)>>>(
-        q, k, v, pos, heads, kv_heads, head_dim, cos_tab, sin_tab, k_cache, v_cache, qk_norm, eps, dtype);
-    return check_launch("epq_rope_kv");
+    return launch_pdl(rope_kv_kernel, dim3((unsigned)m, heads + kv_heads), dim3(head_dim / 2), 0,
+                      static_cast<cudaStream_t>(stream), "epq_rope_kv", q, k, v, pos, (int)heads,
+                      (int)kv_heads, (int)head_dim, cos_tab, sin_tab, k_cache, v_cache, (int)qk_norm, eps,
+                      (int)dtype);
 }
 
 int64_t epq_attn_decode_workspace_bytes(int32_t heads, int32_t kv_heads, int32_t head_dim) {
@@ -448,8 +481,8 @@ int epq_attn_decode(const void* q, const void* k_cache, const void* v_cache, con
         const auto* vb = static_cast<const __nv_bfloat16*>(v_cache);
         auto* ob = static_cast<__nv_bfloat16*>(out);
         const dim3 grid(kv_heads, kAttnSplits);
-#define EPQ_ATTN_SPLIT(D, G) attn_split_kernel<D, G><<<grid, kAttnWarps * 32, 0, st>>>(qb, kb, vb, pos, kv_heads, \
-                                                                                   scale, ob, ws, ctr)
+#define EPQ_ATTN_SPLIT(D, G) return launch_pdl(attn_split_kernel<D, G>, grid, dim3(kAttnWarps * 32), 0, st, \
+                                             "epq_attn_decode", qb, kb, vb, pos, (int)kv_heads, scale, ob, ws, ctr)
         if (head_dim == 128) {
             if (group == 1) EPQ_ATTN_SPLIT(4, 1);
             else if (group == 2) EPQ_ATTN_SPLIT(4, 2);
@@ -463,11 +496,11 @@ int epq_attn_decode(const void* q, const void* k_cache, const void* v_cache, con
         }
 #undef EPQ_ATTN_SPLIT
     } else if (head_dim == 128) {
-        attn_decode_kernel<4><<<heads, kAttnWarps * 32, 0, st>>>(q, k_cache, v_cache, pos, heads, kv_heads,
-                                                                  scale, out, dtype);
+        return launch_pdl(attn_decode_kernel<4>, dim3(heads), dim3(kAttnWarps * 32), 0, st, "epq_attn_decode",
+                          q, k_cache, v_cache, pos, (int)heads, (int)kv_heads, scale, out, (int)dtype);
     } else {
-        attn_decode_kernel<2><<<heads, kAttnWarps * 32, 0, st>>>(q, k_cache, v_cache, pos, heads, kv_heads,
-                                                                  scale, out, dtype);
+        return launch_pdl(attn_decode_kernel<2>, dim3(heads), dim3(kAttnWarps * 32), 0, st, "epq_attn_decode",
+                          q, k_cache, v_cache, pos, (int)heads, (int)kv_heads, scale, out, (int)dtype);
     }
     return check_launch("epq_attn_decode");
 }
@@ -481,10 +514,9 @@ int epq_argmax(const float* x, int64_t n, int64_t* out, void* workspace, int64_t
         return set_error(EPQ_EWORKSPACE, "epq_argmax: workspace of %lld bytes (need %lld, 256-aligned)",
                          (long long)workspace_bytes, (long long)epq_argmax_workspace_bytes());
     uint8_t* w = static_cast<uint8_t*>(workspace);
-    argmax_kernel<<<kArgBlocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        x, n, out, reinterpret_cast<float*>(w + 256), reinterpret_cast<int64_t*>(w + 256 + kArgBlocks * 4),
-        reinterpret_cast<unsigned*>(w));
-    return check_launch("epq_argmax");
+    return launch_pdl(argmax_kernel, dim3(kArgBlocks), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                      "epq_argmax", x, n, out, reinterpret_cast<float*>(w + 256),
+                      reinterpret_cast<int64_t*>(w + 256 + kArgBlocks * 4), reinterpret_cast<unsigned*>(w));
 }
 
 int epq_silu_mul(const void* g, const void* u, void* out, int64_t n, int32_t dtype, void* stream) {
@@ -492,9 +524,8 @@ int epq_silu_mul(const void* g, const void* u, void* out, int64_t n, int32_t dty
     if (!glue_dtype_ok(dtype)) return set_error(EPQ_EDTYPE, "epq_silu_mul: dtype %d", dtype);
     if (n == 0) return EPQ_OK;
     const int64_t blocks = (n + 255) / 256;
-    silu_mul_kernel<<<(unsigned)(blocks < 1184 ? blocks : 1184), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        g, u, out, n, dtype);
-    return check_launch("epq_silu_mul");
+    return launch_pdl(silu_mul_kernel, dim3((unsigned)(blocks < 1184 ? blocks : 1184)), dim3(256), 0,
+                      static_cast<cudaStream_t>(stream), "epq_silu_mul", g, u, out, n, (int)dtype);
 }
 
 }  // extern "C"
