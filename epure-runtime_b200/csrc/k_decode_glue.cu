@@ -284,6 +284,169 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_split_kernel(
     if (threadIdx.x == 0) counters[kvh] = 0u;
 }
 
+// RoPE (rotate-half) of a head vector held 4 (kDims) dims per lane: lane l holds dims
+// kDims*l .. +kDims-1; dim i pairs with i + hd/2, held by lane l ^ 16.  Optional
+// per-head RMSNorm first (rounded to bf16, as the q/k tensors of the model are),
+// result rounded to bf16.
+template <int kDims>
+__device__ __forceinline__ void rope_head(float (&v)[kDims], int lane, int64_t p, const float* cos_t,
+                                          const float* sin_t, int qk_norm, float eps) {
+    constexpr int hd = kDims * 32, half = hd / 2;
+    if (qk_norm) {
+        float ss = 0.f;
+#pragma unroll
+        for (int d = 0; d < kDims; ++d) ss += v[d] * v[d];
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float r = rsqrtf(ss / (float)hd + eps);
+#pragma unroll
+        for (int d = 0; d < kDims; ++d) v[d] = __bfloat162float(__float2bfloat16_rn(v[d] * r));
+    }
+    const bool lo = lane < 16;
+#pragma unroll
+    for (int d = 0; d < kDims; ++d) {
+        const float other = __shfl_xor_sync(0xffffffffu, v[d], 16);
+        const int i = (kDims * lane + d) & (half - 1);
+        const float c = cos_t[p * half + i], s = sin_t[p * half + i];
+        const float x1 = lo ? v[d] : other, x2 = lo ? other : v[d];
+        const float o = lo ? x1 * c - x2 * s : x2 * c + x1 * s;
+        v[d] = __bfloat162float(__float2bfloat16_rn(o));
+    }
+}
+
+// Decode attention with the q/k/v projections of the current token as inputs: the
+// kernel applies (q/k RMSNorm and) RoPE to q and to this position's k itself, uses
+// this position's k / v straight from registers, and split 0 writes them into the
+// caches for later tokens (other CTAs only read earlier positions).  Otherwise as
+// attn_split_kernel; replaces an epq_rope_kv + epq_attn_decode pair.
+template <int kDims, int kGroup>
+__global__ void __launch_bounds__(kAttnWarps * 32) attn_rope_split_kernel(
+    const __nv_bfloat16* __restrict__ q_in, const __nv_bfloat16* __restrict__ k_in,
+    const __nv_bfloat16* __restrict__ v_in, __nv_bfloat16* __restrict__ k_cache,
+    __nv_bfloat16* __restrict__ v_cache, const int64_t* __restrict__ pos, int KV,
+    const float* __restrict__ cos_t, const float* __restrict__ sin_t, int qk_norm, float eps, float scale,
+    __nv_bfloat16* __restrict__ out, float* __restrict__ ws, unsigned* __restrict__ counters) {
+    pdl_enter();
+    constexpr int hd = kDims * 32;
+    constexpr int kRec = hd + 2;
+    __shared__ float wm[kAttnWarps][kGroup], wl[kAttnWarps][kGroup];
+    __shared__ float wacc[kAttnWarps][kGroup][hd];
+    __shared__ bool last;
+    const int kvh = blockIdx.x, split = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t P = pos[0];
+    const int64_t n = P + 1;
+    const int64_t chunk = (n + kAttnSplits - 1) / kAttnSplits;
+    const int64_t t0 = split * chunk, t1 = min(n, t0 + chunk);
+    float qv[kGroup][kDims], acc[kGroup][kDims], m[kGroup], l[kGroup];
+#pragma unroll
+    for (int g = 0; g < kGroup; ++g) {
+        m[g] = -INFINITY;
+        l[g] = 0.f;
+#pragma unroll
+        for (int d = 0; d < kDims; ++d) {
+            qv[g][d] = __bfloat162float(q_in[(int64_t)(kvh * kGroup + g) * hd + lane * kDims + d]);
+            acc[g][d] = 0.f;
+        }
+        rope_head<kDims>(qv[g], lane, P, cos_t, sin_t, qk_norm, eps);
+    }
+    float kc[kDims], vc[kDims];
+#pragma unroll
+    for (int d = 0; d < kDims; ++d) {
+        kc[d] = __bfloat162float(k_in[(int64_t)kvh * hd + lane * kDims + d]);
+        vc[d] = __bfloat162float(v_in[(int64_t)kvh * hd + lane * kDims + d]);
+    }
+    rope_head<kDims>(kc, lane, P, cos_t, sin_t, qk_norm, eps);
+    if (split == 0 && warp == 0) {
+        const int64_t cb = (P * KV + kvh) * hd + lane * kDims;
+#pragma unroll
+        for (int d = 0; d < kDims; ++d) {
+            k_cache[cb + d] = __float2bfloat16_rn(kc[d]);
+            v_cache[cb + d] = __float2bfloat16_rn(vc[d]);
+        }
+    }
+    for (int64_t t = t0 + warp; t < t1; t += kAttnWarps) {
+        float kr[kDims], vr[kDims];
+        if (t == P) {
+#pragma unroll
+            for (int d = 0; d < kDims; ++d) {
+                kr[d] = kc[d];
+                vr[d] = vc[d];
+            }
+        } else {
+            const int64_t kb = (t * KV + kvh) * hd + lane * kDims;
+#pragma unroll
+            for (int d = 0; d < kDims; ++d) {
+                kr[d] = __bfloat162float(k_cache[kb + d]);
+                vr[d] = __bfloat162float(v_cache[kb + d]);
+            }
+        }
+#pragma unroll
+        for (int g = 0; g < kGroup; ++g) {
+            float s = 0.f;
+#pragma unroll
+            for (int d = 0; d < kDims; ++d) s += qv[g][d] * kr[d];
+            for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+            s *= scale;
+            const float mn = fmaxf(m[g], s);
+            const float corr = expf(m[g] - mn), pw = expf(s - mn);
+            l[g] = l[g] * corr + pw;
+#pragma unroll
+            for (int d = 0; d < kDims; ++d) acc[g][d] = acc[g][d] * corr + pw * vr[d];
+            m[g] = mn;
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < kGroup; ++g) {
+        if (lane == 0) {
+            wm[warp][g] = m[g];
+            wl[warp][g] = l[g];
+        }
+#pragma unroll
+        for (int d = 0; d < kDims; ++d) wacc[warp][g][lane * kDims + d] = acc[g][d];
+    }
+    __syncthreads();
+    float* rec = ws + ((int64_t)(kvh * kAttnSplits + split) * kGroup) * kRec;
+    for (int e = threadIdx.x; e < kGroup * hd; e += kAttnWarps * 32) {
+        const int g = e / hd, d = e - g * hd;
+        float mx = -INFINITY;
+        for (int w = 0; w < kAttnWarps; ++w) mx = fmaxf(mx, wm[w][g]);
+        float num = 0.f, den = 0.f;
+        for (int w = 0; w < kAttnWarps; ++w) {
+            if (wm[w][g] == -INFINITY) continue;
+            const float f = expf(wm[w][g] - mx);
+            num += f * wacc[w][g][d];
+            den += f * wl[w][g];
+        }
+        rec[g * kRec + d] = num;
+        if (d == 0) {
+            rec[g * kRec + hd] = mx;
+            rec[g * kRec + hd + 1] = den;
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) last = atomicAdd(&counters[kvh], 1u) == kAttnSplits - 1;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    const float* base = ws + (int64_t)kvh * kAttnSplits * kGroup * kRec;
+    for (int e = threadIdx.x; e < kGroup * hd; e += kAttnWarps * 32) {
+        const int g = e / hd, d = e - g * hd;
+        float mx = -INFINITY;
+        for (int sp = 0; sp < kAttnSplits; ++sp) mx = fmaxf(mx, base[(sp * kGroup + g) * kRec + hd]);
+        float num = 0.f, den = 0.f;
+        for (int sp = 0; sp < kAttnSplits; ++sp) {
+            const float* r = base + (sp * kGroup + g) * kRec;
+            if (r[hd] == -INFINITY) continue;
+            const float f = expf(r[hd] - mx);
+            num += f * r[d];
+            den += f * r[hd + 1];
+        }
+        out[(int64_t)(kvh * kGroup + g) * hd + d] = __float2bfloat16_rn(num / den);
+    }
+    if (threadIdx.x == 0) counters[kvh] = 0u;
+}
+
 // Arg-max of n floats (first index of the maximum, as torch.argmax): every CTA
 // reduces a strided share, the last CTA to finish merges the per-CTA results.
 constexpr int kArgBlocks = 64;
@@ -503,6 +666,48 @@ int epq_attn_decode(const void* q, const void* k_cache, const void* v_cache, con
                           q, k_cache, v_cache, pos, (int)heads, (int)kv_heads, scale, out, (int)dtype);
     }
     return check_launch("epq_attn_decode");
+}
+
+int epq_attn_rope_decode(const void* q, const void* k, const void* v, const int64_t* pos, int32_t heads,
+                         int32_t kv_heads, int32_t head_dim, const float* cos_tab, const float* sin_tab,
+                         void* k_cache, void* v_cache, int32_t qk_norm, float eps, float scale, void* out,
+                         int32_t dtype, void* workspace, int64_t workspace_bytes, void* stream) {
+    if (!q || !k || !v || !pos || !cos_tab || !sin_tab || !k_cache || !v_cache || !out || !workspace ||
+        heads <= 0 || kv_heads <= 0 || heads % kv_heads)
+        return set_error(EPQ_EINVAL, "epq_attn_rope_decode: bad arguments");
+    const int group = heads / kv_heads;
+    if (dtype != EPQ_BF16 || (head_dim != 64 && head_dim != 128) ||
+        !(group == 1 || group == 2 || group == 4 || group == 8))
+        return set_error(EPQ_EUNSUPPORTED, "epq_attn_rope_decode: bf16, head_dim 64/128, heads/kv_heads 1/2/4/8 "
+                         "(got dtype %d, head_dim %d, %d/%d)", dtype, head_dim, heads, kv_heads);
+    if (workspace_bytes < epq_attn_decode_workspace_bytes(heads, kv_heads, head_dim) || (uintptr_t)workspace % 256)
+        return set_error(EPQ_EWORKSPACE, "epq_attn_rope_decode: workspace of %lld bytes (need %lld, 256-aligned)",
+                         (long long)workspace_bytes,
+                         (long long)epq_attn_decode_workspace_bytes(heads, kv_heads, head_dim));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    unsigned* ctr = static_cast<unsigned*>(workspace);
+    float* ws = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + 256);
+    const auto* qb = static_cast<const __nv_bfloat16*>(q);
+    const auto* kb = static_cast<const __nv_bfloat16*>(k);
+    const auto* vb = static_cast<const __nv_bfloat16*>(v);
+    auto* kcb = static_cast<__nv_bfloat16*>(k_cache);
+    auto* vcb = static_cast<__nv_bfloat16*>(v_cache);
+    auto* ob = static_cast<__nv_bfloat16*>(out);
+    const dim3 grid(kv_heads, kAttnSplits);
+#define EPQ_ATTN_ROPE(D, G)                                                                                 \
+    return launch_pdl(attn_rope_split_kernel<D, G>, grid, dim3(kAttnWarps * 32), 0, st, "epq_attn_rope_decode", \
+                      qb, kb, vb, kcb, vcb, pos, (int)kv_heads, cos_tab, sin_tab, (int)qk_norm, eps, scale, ob, ws, ctr)
+    if (head_dim == 128) {
+        if (group == 1) EPQ_ATTN_ROPE(4, 1);
+        if (group == 2) EPQ_ATTN_ROPE(4, 2);
+        if (group == 4) EPQ_ATTN_ROPE(4, 4);
+        EPQ_ATTN_ROPE(4, 8);
+    }
+    if (group == 1) EPQ_ATTN_ROPE(2, 1);
+    if (group == 2) EPQ_ATTN_ROPE(2, 2);
+    if (group == 4) EPQ_ATTN_ROPE(2, 4);
+    EPQ_ATTN_ROPE(2, 8);
+#undef EPQ_ATTN_ROPE
 }
 
 int64_t epq_argmax_workspace_bytes(void) { return 256 + kArgBlocks * (4 + 8); }

@@ -53,7 +53,7 @@ EXPORTS = (
     "epq_linear_bwd", "epq_materialize", "epq_linear_noalloc", "epq_linear_noalloc_max_scratch",
     "epq_chain_workspace_bytes", "epq_chain_prepare", "epq_chain_run", "epq_chain_set_tp",
     "epq_add_rmsnorm", "epq_rope_kv", "epq_attn_decode", "epq_attn_decode_workspace_bytes",
-    "epq_silu_mul", "epq_argmax", "epq_argmax_workspace_bytes",
+    "epq_silu_mul", "epq_argmax", "epq_argmax_workspace_bytes", "epq_attn_rope_decode",
 )
 
 _lib = None
@@ -100,6 +100,8 @@ def load_library(path=None):
         lib.epq_attn_decode_workspace_bytes.restype = I64
         lib.epq_attn_decode_workspace_bytes.argtypes = [I32, I32, I32]
         lib.epq_argmax.argtypes = [P, I64, P, P, I64, P]
+        lib.epq_attn_rope_decode.argtypes = [P, P, P, P, I32, I32, I32, P, P, P, P, I32, F32, F32, P, I32, P,
+                                             I64, P]
         lib.epq_argmax_workspace_bytes.restype = I64
         lib.epq_argmax_workspace_bytes.argtypes = []
         lib.epq_silu_mul.argtypes = [P, P, P, I64, I32, P]
@@ -375,6 +377,19 @@ def attn_decode(q, k_cache, v_cache, pos, scale, ws=None):
                                H, k_cache.shape[-2], hd, scale, out.data_ptr(), dtype_code(q.dtype),
                                _ptr(ws), ws.numel() if ws is not None else 0,
                                _stream_ptr(q.device)), "epq_attn_decode")
+    return out
+
+
+def attn_rope_decode(q, k, v, pos, cos, sin, k_cache, v_cache, qk_norm, eps, scale, ws):
+    """RoPE (and q/k norm) + KV write + attention for one token; q [H, hd], k, v [KV, hd]."""
+    lib = load_library()
+    H, hd = q.shape[-2], q.shape[-1]
+    out = torch.empty((H, hd), dtype=q.dtype, device=q.device)
+    _check(lib.epq_attn_rope_decode(q.data_ptr(), k.data_ptr(), v.data_ptr(), pos.data_ptr(), H,
+                                    k.shape[-2], hd, cos.data_ptr(), sin.data_ptr(), k_cache.data_ptr(),
+                                    v_cache.data_ptr(), int(qk_norm), eps, scale, out.data_ptr(),
+                                    dtype_code(q.dtype), ws.data_ptr(), ws.numel(), _stream_ptr(q.device)),
+           "epq_attn_rope_decode")
     return out
 
 

@@ -118,19 +118,17 @@ class PackedDecoder:
 
     def _decode_fused(self, ids, pos):
         """One token with libepq.so's decode glue (include/epq_decode.h): per layer the
-        packed q/k/v launch, RoPE + KV write, attention, o, residual add fused with the
-        next RMSNorm, gate/up, SiLU * up, down -- 8 launches."""
+        packed q/k/v launch, RoPE + KV write + attention (one launch), o, residual add
+        fused with the next RMSNorm, gate/up, SiLU * up, down -- 7 launches."""
         sh = self.shapes
         H, hd = sh.heads, sh.head_dim
         x = self.embed[ids]                                            # [1, hidden]
         y = _native.add_rmsnorm(x, eps=self.eps)
         for li, b in enumerate(self.stack.blocks):
             q, k, v = _native.linear_multi(y, [b["q_proj"], b["k_proj"], b["v_proj"]])
-            q = q.view(1, H, hd)
-            _native.rope_kv(q, k.view(1, -1, hd), v.view(1, -1, hd), pos, self.cos, self.sin,
-                            self.k_cache[li], self.v_cache[li], self.qk_norm, self.eps)
-            att = _native.attn_decode(q.view(H, hd), self.k_cache[li], self.v_cache[li], pos,
-                                      1.0 / math.sqrt(hd), self.attn_ws)
+            att = _native.attn_rope_decode(q.view(H, hd), k.view(-1, hd), v.view(-1, hd), pos, self.cos,
+                                           self.sin, self.k_cache[li], self.v_cache[li], self.qk_norm,
+                                           self.eps, 1.0 / math.sqrt(hd), self.attn_ws)
             (o,) = _native.linear_multi(att.view(1, H * hd), [b["o_proj"]])
             y = _native.add_rmsnorm(x, add=o, h_out=x, eps=self.eps)   # x += o; y = rms(x)
             g, u = _native.linear_multi(y, [b["gate_proj"], b["up_proj"]])

@@ -48,6 +48,16 @@ int epq_attn_decode(const void* q, const void* k_cache, const void* v_cache, con
                     int32_t heads, int32_t kv_heads, int32_t head_dim, float scale, void* out,
                     int32_t dtype, void* workspace, int64_t workspace_bytes, void* stream);
 
+/* epq_rope_kv + epq_attn_decode in one launch (bf16, head_dim 64 or 128, heads /
+ * kv_heads of 1, 2, 4 or 8): q, k, v [heads or kv_heads, head_dim] are this token's
+ * projections at position pos[0]; q and k get (qk_norm) RMSNorm and RoPE inside,
+ * k and v are written into the caches at pos[0], and out receives the attention
+ * over positions 0..pos[0].  Workspace as for epq_attn_decode (required). */
+int epq_attn_rope_decode(const void* q, const void* k, const void* v, const int64_t* pos, int32_t heads,
+                         int32_t kv_heads, int32_t head_dim, const float* cos_tab, const float* sin_tab,
+                         void* k_cache, void* v_cache, int32_t qk_norm, float eps, float scale, void* out,
+                         int32_t dtype, void* workspace, int64_t workspace_bytes, void* stream);
+
 /* *out = the first index of the maximum of x[0..n) (torch.argmax), on the device.
  * workspace: epq_argmax_workspace_bytes(), 256-byte aligned, zeroed once before first
  * use (left ready for the next call). */

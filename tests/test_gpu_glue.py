@@ -108,3 +108,28 @@ def test_silu_mul_and_rope():
     assert _rel(qq, qw) <= 1e-2
     assert _rel(kc[5], kw[0]) <= 1e-2
     assert torch.equal(vc[5], v[0])
+
+
+@pytest.mark.parametrize("heads,kv,hd,qk", [(32, 8, 128, False), (16, 8, 128, True), (8, 2, 64, True)])
+def test_attn_rope_matches_two_kernels(heads, kv, hd, qk):
+    """epq_attn_rope_decode == epq_rope_kv followed by epq_attn_decode."""
+    from epure import _native
+    g = torch.Generator(device=DEV).manual_seed(heads + hd)
+    L, P = 64, 40
+    q = torch.randn(heads, hd, generator=g, device=DEV).to(torch.bfloat16)
+    k = torch.randn(kv, hd, generator=g, device=DEV).to(torch.bfloat16)
+    v = torch.randn(kv, hd, generator=g, device=DEV).to(torch.bfloat16)
+    kc = torch.randn(L, kv, hd, generator=g, device=DEV).to(torch.bfloat16)
+    vc = torch.randn(L, kv, hd, generator=g, device=DEV).to(torch.bfloat16)
+    inv = 1.0 / (1e6 ** (torch.arange(0, hd, 2, device=DEV, dtype=torch.float64) / hd))
+    ang = torch.arange(L, device=DEV, dtype=torch.float64)[:, None] * inv[None, :]
+    cos, sin = torch.cos(ang).float(), torch.sin(ang).float()
+    pos = torch.tensor([P], device=DEV)
+    ws = _native.attn_decode_workspace(heads, kv, hd, DEV)
+    kc2, vc2, q2 = kc.clone(), vc.clone(), q.clone().view(1, heads, hd)
+    _native.rope_kv(q2, k.view(1, kv, hd), v.view(1, kv, hd), pos, cos, sin, kc2, vc2, qk, 1e-6)
+    want = _native.attn_decode(q2.view(heads, hd), kc2, vc2, pos, 1.0 / math.sqrt(hd), ws)
+    got = _native.attn_rope_decode(q, k, v, pos, cos, sin, kc, vc, qk, 1e-6, 1.0 / math.sqrt(hd), ws)
+    assert _rel(got, want) <= 1e-2
+    assert _rel(kc[P], kc2[P]) <= 1e-2 and torch.equal(vc[P], vc2[P])
+    assert torch.equal(kc[:P], kc2[:P])
