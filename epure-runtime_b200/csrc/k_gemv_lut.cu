@@ -418,7 +418,7 @@ int lut_read_device_error(int* flag) {
 // loads the library holds it until the process exits.
 // ---------------------------------------------------------------------------
 constexpr int64_t kStaticScratchBytes = 4 << 20;   // 4 MiB: counters + partial sums
-__device__ __align__(256) unsigned char g_lut_static_scratch[kStaticScratchBytes];
+static __device__ __align__(256) unsigned char g_lut_static_scratch[kStaticScratchBytes];
 
 namespace {
 std::mutex g_static_mu;
