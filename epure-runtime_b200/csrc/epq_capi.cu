@@ -110,9 +110,14 @@ int epq_device_error(int* flag) {
     bwd = bwd || dxe;
     rc = chain_read_device_error(&chain);
     if (rc) return rc;
+    int emb = 0;
+    rc = embed_read_device_error(&emb);
+    if (rc) return rc;
     // bit 0: LUT placement check; bit 1: a bounded wait gave up (GEMV, GEMM, backward or chain);
-    // bit 2: the chain kernel's placement or grid check failed
-    *flag = (lut ? 1 : 0) | ((mma || tc || bwd || chain == 1) ? 2 : 0) | (chain == 2 ? 4 : 0);
+    // bit 2: the chain kernel's placement or grid check failed; bit 3: an embedding id was
+    // outside the store's rows
+    *flag = (lut ? 1 : 0) | ((mma || tc || bwd || chain == 1) ? 2 : 0) | (chain == 2 ? 4 : 0) |
+            (emb ? 8 : 0);
     return EPQ_OK;
 }
 
@@ -266,6 +271,17 @@ int epq_linear_bwd(const epq_store* store, const void* x, int64_t ldx, const voi
     }
     if (!dx && !dscale && !dcb) return EPQ_OK;
     return launch_bwd_generic(s, x, ldx, dy, ldy, act_dtype, m, dx, lddx, dx_dtype, dscale, dcb, st);
+}
+
+int epq_embedding(const epq_store* store, const int64_t* ids, int64_t n_ids, void* out, int64_t ldo,
+                  int32_t out_dtype, void* stream) {
+    StoreD s;
+    int rc = make_store(store, &s, "embedding");
+    if (rc) return rc;
+    if (!dtype_ok(out_dtype)) return set_error(EPQ_EDTYPE, "embedding: out dtype");
+    if (n_ids < 0) return set_error(EPQ_EINVAL, "embedding: n_ids < 0");
+    if (n_ids * s.k > 0 && (!ids || !out || ldo < s.k)) return set_error(EPQ_EINVAL, "embedding: ids/out/ldo");
+    return launch_embedding(s, ids, n_ids, out, ldo, out_dtype, static_cast<cudaStream_t>(stream));
 }
 
 int epq_materialize(const epq_store* store, void* w, int64_t ldw, int32_t out_dtype, void* stream) {

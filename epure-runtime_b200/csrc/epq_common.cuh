@@ -115,6 +115,9 @@ struct ChainStepD;
 struct ChainHeaderD;
 int chain_grid(int* grid);
 int chain_read_device_error(int* flag);
+int launch_embedding(const StoreD& s, const int64_t* ids, int64_t n_ids, void* out, int64_t ldo,
+                     int out_dtype, cudaStream_t st);
+int embed_read_device_error(int* flag);
 
 // Small-batch tensor-core GEMV over EPQ_LAYOUT_MMA16 stores (k_gemv_mma.cu).
 bool mma_eligible(const StoreD& s, int64_t m, int x_dtype);

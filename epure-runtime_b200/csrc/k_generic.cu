@@ -7,6 +7,7 @@
 // Semantics follow the reference:
 //   forward      out = x @ (cb[idx] * scale)^T            epure/kernels/_triton.py:56-107
 //   materialize  W = cb.to(dt)[idx] * scale.to(dt)        epure/runtime.py:78-89
+//   embedding    rows ids of that W, nothing else built   epure/runtime.py:129-160
 //   backward     dX = dY W; dscale, dcb as the autograd of materialize
 //                (epure/finetune.py:26-28, fine-tuning/README.md:64-68)
 #include "epq_common.cuh"
@@ -200,6 +201,31 @@ __global__ void materialize_kernel(StoreD s, void* __restrict__ w, int64_t ldw, 
     }
 }
 
+// PackedEmbedding.forward: out[i, :] = W[ids[i], :] with materialize's rounding,
+// decoding only the requested rows.  An id outside [0, n) yields a zero row and
+// sets g_embed_bad (reported by epq_device_error).
+__device__ int g_embed_bad = 0;
+
+__global__ void embedding_kernel(StoreD s, const int64_t* __restrict__ ids, int64_t n_ids,
+                                 void* __restrict__ out, int64_t ldo, int out_dtype) {
+    const int64_t total = n_ids * s.k;
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
+         t += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t i = t / s.k, c = t - i * s.k;
+        const int64_t r = ids[i];
+        if (r < 0 || r >= s.n) {
+            if (c == 0) atomicExch(&g_embed_bad, 1);
+            store_f(out, out_dtype, i * ldo + c, 0.f);
+            continue;
+        }
+        const int e = index_at(s, r, c);
+        const float cv = round_to(load_f(s.cb, s.cb_dtype, e * s.vec + (s.vec == 4 ? (c & 3) : 0)),
+                                  out_dtype);
+        const float sv = round_to(scale_at(s, r, c / s.group), out_dtype);
+        store_f(out, out_dtype, i * ldo + c, cv * sv);
+    }
+}
+
 // EPQ_LAYOUT_TILED: one thread per 16-byte chunk (16 rows of one index position).
 __global__ void relayout_tiled_kernel(const uint8_t* __restrict__ src, int64_t n, int64_t kpos,
                                       int64_t p, int64_t rb, int64_t chunks,
@@ -284,6 +310,19 @@ int launch_materialize(const StoreD& s, void* w, int64_t ldw, int out_dtype, cud
     if (s.n * s.k == 0) return EPQ_OK;
     materialize_kernel<<<grid_1d(s.n * s.k, 256), 256, 0, st>>>(s, w, ldw, out_dtype);
     return check_launch("materialize_kernel");
+}
+
+int launch_embedding(const StoreD& s, const int64_t* ids, int64_t n_ids, void* out, int64_t ldo,
+                     int out_dtype, cudaStream_t st) {
+    if (n_ids * s.k == 0) return EPQ_OK;
+    embedding_kernel<<<grid_1d(n_ids * s.k, 256), 256, 0, st>>>(s, ids, n_ids, out, ldo, out_dtype);
+    return check_launch("embedding_kernel");
+}
+
+int embed_read_device_error(int* flag) {
+    if (cudaMemcpyFromSymbol(flag, g_embed_bad, sizeof(int)) != cudaSuccess)
+        return check_launch("read embedding error flag");
+    return EPQ_OK;
 }
 
 int64_t layout_bytes(int layout, int64_t n, int64_t k, int vec, int group) {

@@ -54,6 +54,7 @@ EXPORTS = (
     "epq_chain_workspace_bytes", "epq_chain_prepare", "epq_chain_run", "epq_chain_set_tp",
     "epq_add_rmsnorm", "epq_rope_kv", "epq_attn_decode", "epq_attn_decode_workspace_bytes",
     "epq_silu_mul", "epq_argmax", "epq_argmax_workspace_bytes", "epq_attn_rope_decode",
+    "epq_embedding",
 )
 
 _lib = None
@@ -93,6 +94,7 @@ def load_library(path=None):
         lib.epq_chain_run.argtypes = [P, P, I32, P, I32, P]
         lib.epq_chain_set_tp.argtypes = [P, I32, I32, ctypes.POINTER(P), ctypes.POINTER(ctypes.c_uint8),
                                          I32, P]
+        lib.epq_embedding.argtypes = [SP, P, I64, P, I64, I32, P]
         F32 = ctypes.c_float
         lib.epq_add_rmsnorm.argtypes = [P, P, P, P, I64, I64, F32, I32, P]
         lib.epq_rope_kv.argtypes = [P, P, P, P, I64, I32, I32, I32, P, P, P, P, I32, F32, I32, P]
@@ -268,6 +270,18 @@ def materialize(store, dtype):
     _check(lib.epq_materialize(ctypes.byref(d), w.data_ptr(), w.stride(0), dtype_code(dtype),
                                _stream_ptr(w.device)), "epq_materialize")
     return w
+
+
+def embedding(store, ids, dtype):
+    """Rows ``ids`` (any shape, int64 on the store's device) of the dequantised table,
+    materialize's rounding in ``dtype``: a tensor ``[*ids.shape, in_features]``."""
+    lib = load_library()
+    d = describe_store(store)
+    flat = ids.reshape(-1).to(torch.int64).contiguous()
+    out = torch.empty((flat.numel(), store.in_features), dtype=dtype, device=store.packed.device)
+    _check(lib.epq_embedding(ctypes.byref(d), flat.data_ptr(), flat.numel(), out.data_ptr(), out.stride(0),
+                             dtype_code(dtype), _stream_ptr(out.device)), "epq_embedding")
+    return out.view(*ids.shape, store.in_features)
 
 
 def layout_bytes(layout, n, k, vec, group):

@@ -264,6 +264,10 @@ class PackedEmbedding(nn.Module):
 
     def forward(self, ids):
         s = self.store
+        if ids.is_cuda and s.packed.is_cuda and len(s.shape) == 2:
+            # libepq.so decodes only the requested rows (epq_embedding), same rounding
+            from . import _native
+            return _native.embedding(s, ids, self.dtype)
         flat = ids.reshape(-1)
         n_in = s.in_features
         idx = s.index_rows(flat).to(torch.long)

@@ -34,6 +34,8 @@
  *       backward kernel
  *   epq_materialize
  *       epure/runtime.py:78-89        PackedWeight.materialize(dtype)
+ *   epq_embedding
+ *       epure/runtime.py:129-160      PackedEmbedding.forward(ids)
  *   epq_relayout / epq_layout_bytes
  *       the re-layout step of epure/runtime.py:243-249 (apply_to builds the
  *       store from the container's index stream)
@@ -120,8 +122,10 @@ const char* epq_last_error(void);
 /* Reads (synchronously, on the current device) the flags kernels set when an
  * in-kernel check fails: bit 0 -- the batch-1 LUT kernel found its shared
  * memory placement violated and wrote nothing; bit 1 -- a bounded
- * device-side wait gave up (that call's output is invalid).  *flag = 0
- * means no kernel has reported a failure. */
+ * device-side wait gave up (that call's output is invalid); bit 2 -- the
+ * chain kernel's placement or grid check failed; bit 3 -- epq_embedding was
+ * given an id outside the store's rows (that row of its output is zero).
+ * *flag = 0 means no kernel has reported a failure. */
 int epq_device_error(int* flag);
 
 /* Bytes of an index buffer in `layout` (EPQ_LAYOUT_TILED or EPQ_LAYOUT_MMA16)
@@ -250,6 +254,15 @@ int epq_chain_run(const void* workspace, const void* x, int32_t x_dtype, void* o
  * rounded to out_dtype (runtime.py:85-88). */
 int epq_materialize(const epq_store* store, void* w, int64_t ldw, int32_t out_dtype,
                     void* stream);
+
+/* Rows of the dequantised table for a packed embedding: out[i, :] (row stride
+ * ldo >= k, out_dtype) = W[ids[i], :] with materialize's rounding, for n_ids
+ * device-resident int64 ids; only those rows are decoded.  Replaces
+ * PackedEmbedding.forward (runtime.py:129-160: gather cb[idx] for the ids'
+ * rows, cast, multiply by the rows' scales).  Any store format.  An id outside
+ * [0, n) gives a zero row and sets bit 3 of epq_device_error. */
+int epq_embedding(const epq_store* store, const int64_t* ids, int64_t n_ids, void* out, int64_t ldo,
+                  int32_t out_dtype, void* stream);
 
 #ifdef __cplusplus
 }
