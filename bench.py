@@ -32,6 +32,8 @@ Other workloads (not the headline; each prints its own metric):
   --mode model: greedy decode of the whole model (epure.model.PackedDecoder:
       packed linears through libepq.so, attention / norms / lm_head in torch, one
       CUDA graph per token after a 128-token prompt), metric tok/s;
+  --mode embedding [--tokens N]: packed embedding rows for N ids (epq_embedding), with
+      the reference's torch formulation timed beside it;
   --mode per-linear --batch B: a B-token decode step through the per-linear launches
       (the tensor-core GEMV up to 16 rows, the tcgen05 GEMM above), metric tok/s;
   --model qwen3-1.7b|llama3-8b|llama3-70b picks the decoder shapes;
@@ -402,6 +404,70 @@ def time_fallback_finetune(stack, x, steps):
             "steps": steps}
 
 
+def run_embedding(args, rank, world, local_rank):
+    """Packed embedding rows (PackedEmbedding.forward -> epq_embedding) for a batch of
+    `--tokens` ids from a vector-codebook table of the model's vocab x hidden."""
+    import torch
+    from epure import synthetic
+    from epure.runtime import PackedEmbedding
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    shapes = synthetic.SHAPES[args.model]
+    st = synthetic.make_store(shapes.vocab, shapes.hidden, device=dev, seed=1000 * rank)
+    emb = PackedEmbedding(st, dtype=torch.bfloat16)
+    n = args.tokens
+    g = torch.Generator(device=dev).manual_seed(rank)
+    # rotate over 64 id batches so the gathered rows do not stay in L2
+    batches = [torch.randint(0, shapes.vocab, (n,), generator=g, device=dev) for _ in range(64)]
+
+    def reference(ids):                    # the reference's torch formulation (runtime.py:129-160)
+        flat = ids.reshape(-1)
+        idx = st.index_rows(flat).to(torch.long)
+        w = st.cb.reshape(st.levels, 4)[idx].reshape(flat.numel(), st.in_features).to(torch.bfloat16)
+        sc = st.scale[flat].to(torch.bfloat16)
+        for gi, start in enumerate(range(0, st.in_features, st.group)):
+            w[:, start:start + st.group] *= sc[:, gi:gi + 1]
+        return w
+
+    def timed(fn, steps):
+        for i in range(max(args.warmup, 3)):
+            fn(batches[i % 64])
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(steps):
+            fn(batches[i % 64])
+        e1.record()
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / steps
+
+    with ClockSampler(local_rank) as clocks:
+        ms = timed(emb, args.steps)
+    ms_ref = timed(reference, max(3, min(args.steps, 20)))
+    # bytes a batch must move: each id's index row (k / 4) and scales, the codebook, the output
+    k = shapes.hidden
+    step_bytes = n * (k // 4 + (k // st.group) * 2 + k * 2) + st.cb.numel() * 2
+    hbm_peak, peak_kind = _peaks()
+    achieved = step_bytes / (ms * 1e-3) / 1e9
+    if rank == 0:
+        print(json.dumps({
+            "metric": f"packed embedding rows/s @{args.model} ({n} ids per batch)",
+            "value": round(n * 1000.0 / ms, 1), "unit": "rows/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"{shapes.vocab} x {k} vector-codebook embedding, {n} random ids",
+                       "mode": "embedding", "l2": "64 rotating id batches over a 0.3+ GB table",
+                       "bytes_per_step": step_bytes},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind,
+                         "kernel": "embedding_kernel", "traffic": None},
+            "reference_torch_ms": round(ms_ref, 5),
+            "gpu_launches": args.steps,
+            "clocks": clocks.summary(),
+        }), flush=True)
+
+
 def run_model(args, rank, world, local_rank):
     """Greedy decode of the whole model (epure.model.PackedDecoder): packed linears
     through libepq.so, attention / norms / RoPE / SwiGLU / lm_head in torch, one
@@ -691,7 +757,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--mode", choices=["chain", "per-linear", "prefill", "finetune", "model"],
+    ap.add_argument("--mode", choices=["chain", "per-linear", "prefill", "finetune", "model", "embedding"],
                     default="chain")
     ap.add_argument("--model", choices=["qwen3-1.7b", "llama3-8b", "llama3-70b"], default=None)
     ap.add_argument("--layers", type=int, default=None)
@@ -736,6 +802,8 @@ def main():
             return run_finetune(args, rank, world, local_rank)
         if args.mode == "model":
             return run_model(args, rank, world, local_rank)
+        if args.mode == "embedding":
+            return run_embedding(args, rank, world, local_rank)
         return run_ours(args, rank, world, local_rank)
     finally:
         if world > 1:
