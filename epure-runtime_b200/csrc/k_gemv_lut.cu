@@ -264,12 +264,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_lut_kernel(const __grid_cons
             const int slot_i = atomicAdd(n_finish, 1);
             if (slot_i < kListCap) {
                 finish[slot_i] = (si << 24) | rb;
-            } else {  // list full: reduce this row block here (rare, correct)
+            } else {  // list full: reduce this row block here (rare)
+                // Same order as the list path below (even groups, odd groups, then
+                // their sum), so the result does not depend on which path ran.
                 for (int r = 0; r < 16; ++r) {
                     const int row = rb * 16 + r;
-                    float sum = 0.f;
-                    for (int gg = 0; gg < S.ng; ++gg) sum += __ldcg(S.partials + (int64_t)gg * S.rb * 16 + row);
-                    if (row < S.n) store_f(S.out, P.out_dtype, row, sum);
+                    float even = 0.f, odd = 0.f;
+                    for (int gg = 0; gg < S.ng; gg += 2) even += __ldcg(S.partials + (int64_t)gg * S.rb * 16 + row);
+                    for (int gg = 1; gg < S.ng; gg += 2) odd += __ldcg(S.partials + (int64_t)gg * S.rb * 16 + row);
+                    if (row < S.n) store_f(S.out, P.out_dtype, row, even + odd);
                 }
                 S.counters[rb] = 0u;
             }
