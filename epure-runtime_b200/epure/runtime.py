@@ -10,6 +10,9 @@ Same public names, signatures and return types as the reference
     resolve(path, filename)                                      runtime.py:308-320
     load(path, device=None) -> (model, tokenizer)                runtime.py:373-415
 
+plus ``read_stores(path, device, tp)`` (the container's stores by name,
+optionally cut into this rank's tensor-parallel shards at load).
+
 Differences, all on the GPU path:
 
 * ``PackedLinear.forward`` on a CUDA activation always runs the sm_100a kernels
@@ -27,6 +30,7 @@ Differences, all on the GPU path:
   rounding bit for bit (cb and scale cast to ``dtype`` first, product rounded
   to ``dtype``).
 """
+import contextlib
 import os
 
 import numpy as np
@@ -286,200 +290,266 @@ class PackedEmbedding(nn.Module):
         return self.store.materialize(self.dtype)
 
 
-class _ExpertHolder:
-    """Keeps a stacked expert slab packed except while its module runs (runtime.py:163-186)."""
-
-    def __init__(self, mod, attr, store, dtype=torch.float16):
-        self.mod, self.attr, self.store = mod, attr, store
-        self.dtype = dtype
-        if attr in mod._parameters:
-            del mod._parameters[attr]
-        mod.register_forward_pre_hook(self._attach)
-        mod.register_forward_hook(self._release)
-        setattr(mod, attr, None)
-
-    def _attach(self, mod, _a):
-        setattr(mod, self.attr, self.store.materialize(self.dtype))
-
-    def _release(self, mod, _a, _o):
-        setattr(mod, self.attr, None)
+# ---------------------------------------------------------------------------
+# loading a container into a module tree
+# ---------------------------------------------------------------------------
+_MISSING = object()
 
 
-def _get(root, dotted):
-    cur = root
-    for p in dotted.split("."):
-        if not hasattr(cur, p):
+def _walk(root, dotted):
+    """The object at attribute path ``dotted`` below ``root`` (None if a step is missing)."""
+    obj = root
+    for step in dotted.split("."):
+        obj = getattr(obj, step, _MISSING)
+        if obj is _MISSING:
             return None
-        cur = getattr(cur, p)
-    return cur
+    return obj
 
 
-def _set(root, dotted, mod):
-    parts = dotted.split(".")
-    parent = root
-    for p in parts[:-1]:
-        parent = getattr(parent, p)
-    setattr(parent, parts[-1], mod)
+def _owner(root, dotted):
+    """(module holding the last step of ``dotted``, that step's name)."""
+    head, _, leaf = dotted.rpartition(".")
+    return (root.get_submodule(head) if head else root), leaf
 
 
-def _assign(root, dotted, tensor):
-    parts = dotted.split(".")
-    parent = root
-    for p in parts[:-1]:
-        parent = getattr(parent, p)
-    setattr(parent, parts[-1], nn.Parameter(tensor, requires_grad=False))
+def _replace_module(root, dotted, module):
+    parent, leaf = _owner(root, dotted)
+    setattr(parent, leaf, module)
 
 
-def attach_store(model, name, store, dtype, holders, embed_holder):
-    """Swap the module that owns tensor ``name`` for its packed form.
+def _install_dense(root, dotted, tensor):
+    """A frozen dense parameter at ``dotted`` (replacing what was there)."""
+    parent, leaf = _owner(root, dotted)
+    setattr(parent, leaf, nn.Parameter(tensor, requires_grad=False))
 
-    The module-type rules of the reference's ``apply_to`` (runtime.py:251-287):
-    embeddings -> PackedEmbedding, linears -> PackedLinear, convolutions and
-    unrecognised owners -> dense, rank-3 expert slabs -> _ExpertHolder.
-    Returns "packed" or "dense".
+
+class PackedParameter:
+    """A stacked expert slab (rank-3 parameter of a module that does its own
+    batched matmul) kept packed: the owner gets the dense tensor from a forward
+    pre-hook and drops it in a forward hook, so only the module currently
+    running holds a dense copy (the reference's _ExpertHolder,
+    runtime.py:163-186)."""
+
+    def __init__(self, owner, attr, store, dtype=torch.float16):
+        self.owner, self.attr, self.store, self.dtype = owner, attr, store, dtype
+        owner._parameters.pop(attr, None)
+        setattr(owner, attr, None)
+        self.handles = (owner.register_forward_pre_hook(self._expand),
+                        owner.register_forward_hook(self._drop))
+
+    def _expand(self, module, args):
+        setattr(module, self.attr, self.store.materialize(self.dtype))
+
+    def _drop(self, module, args, output):
+        setattr(module, self.attr, None)
+
+
+def placement(model, name, rank):
+    """Where a compressed tensor ``name`` of the given rank goes in ``model``.
+
+    Returns (kind, path): "embedding" / "linear" (path = the module to swap for
+    PackedEmbedding / PackedLinear), "experts" (path = the parameter kept
+    packed by a PackedParameter) or "dense" (path = the parameter to overwrite
+    with the decoded tensor).  The rules are the reference's
+    (runtime.py:251-287):
+
+    * an ``nn.Embedding`` (exactly that type; subclasses have their own forward
+      signatures) or any tensor named ``*embed_tokens*``  -> embedding;
+    * an ``nn.Linear`` (or subclass)                      -> linear, bias kept;
+    * a convolution (rank 3/4 weight, not an expert slab)  -> dense;
+    * another rank-3 tensor whose owner has that attribute -> experts;
+    * anything else (routers, odd modules)                 -> dense.
     """
-    mod_name = name[:-7] if name.endswith(".weight") else name
-    target = _get(model, mod_name)
+    module_path = name[:-len(".weight")] if name.endswith(".weight") else name
+    target = _walk(model, module_path)
     if type(target) is nn.Embedding or "embed_tokens" in name:
-        embed_holder.append(store)
-        _set(model, mod_name, PackedEmbedding(store, dtype))
-        return "packed"
+        return "embedding", module_path
     if isinstance(target, nn.Linear):
-        _set(model, mod_name, PackedLinear(store, getattr(target, "bias", None)))
-        return "packed"
+        return "linear", module_path
     if isinstance(target, (nn.Conv1d, nn.Conv2d, nn.Conv3d)):
-        _assign(model, name, store.materialize(dtype))
-        return "dense"
-    if len(store.shape) == 3:
-        owner_path, _, attr = mod_name.rpartition(".")
-        owner = _get(model, owner_path) if owner_path else model
-        if owner is not None and (attr in getattr(owner, "_parameters", {})
-                                  or hasattr(owner, attr)):
-            holders.append(_ExpertHolder(owner, attr, store, dtype))
-            return "packed"
-    _assign(model, name, store.materialize(dtype))
-    return "dense"
+        return "dense", name
+    if rank == 3:
+        holder_path, _, attr = module_path.rpartition(".")
+        holder = _walk(model, holder_path) if holder_path else model
+        if holder is not None and (attr in getattr(holder, "_parameters", {}) or hasattr(holder, attr)):
+            return "experts", module_path
+    return "dense", name
 
 
-def tie_lm_head(model, cfg, embed_store, verbose=True):
-    """Tied lm_head -> PackedLinear over the embedding store (runtime.py:289-300)."""
-    if cfg is not None and getattr(cfg, "tie_word_embeddings", False) and embed_store:
-        _set(model, "lm_head", PackedLinear(embed_store))
+def _read_store(ebin, rec, levels, group, vec):
+    """The PackedWeight (CPU, row layout) of one compressed header entry."""
+    cb = np.frombuffer(ebin.blob(rec["cb"]), np.float32).copy()
+    if vec > 1:
+        cb = cb.reshape(-1, vec)
+    scale = np.frombuffer(ebin.blob(rec["scale"]), np.float16).reshape(rec["scale_shape"]).copy()
+    codes = container.rans_decode(ebin.blob(rec["idx"]), rec["chunks"], rec["counts"])
+    packed = codes if vec > 1 else _pack4(codes, levels)
+    return PackedWeight(rec["shape"], packed, scale, cb, group, levels, vec=vec)
+
+
+def _raw_tensor(ebin, rec):
+    return torch.from_numpy(np.frombuffer(ebin.blob(rec["data"]), np.float16).reshape(rec["shape"]).copy())
+
+
+def apply_to(model, path, device="cpu", cfg=None, verbose=True, dtype=None):
+    """Put the weights of container ``path`` into ``model``, in place (runtime.py:214-305).
+
+    Raw tensors become frozen dense parameters in ``dtype`` (default: the
+    model's current floating dtype, since ``load`` chose it).  Compressed ones
+    become PackedWeight stores on ``device`` -- vector-codebook stores are laid
+    out for the GPU kernels as they land there -- placed by ``placement``.  A
+    config with ``tie_word_embeddings`` gets an lm_head over the embedding's
+    store, and the flag is cleared so a later ``tie_weights()`` does not look
+    for a dense embedding parameter.  Returns ``model``.
+    """
+    if dtype is None:
+        dtype = next((p.dtype for p in model.parameters() if p.is_floating_point()), torch.float16)
+    counts = {"packed": 0, "dense": 0}
+    embed_store = None
+    holders = []
+    with container.Ebin(path) as ebin:
+        levels, group, vec = ebin.header["levels"], ebin.header["group"], ebin.vec
+        for rec in ebin.tensors():
+            name = rec["name"]
+            if rec["kind"] == "raw":
+                _install_dense(model, name, _raw_tensor(ebin, rec).to(device=device, dtype=dtype))
+                counts["dense"] += 1
+                continue
+            store = _read_store(ebin, rec, levels, group, vec).to(device)
+            kind, where = placement(model, name, len(rec["shape"]))
+            if kind == "embedding":
+                embed_store = store
+                _replace_module(model, where, PackedEmbedding(store, dtype))
+            elif kind == "linear":
+                _replace_module(model, where, PackedLinear(store, getattr(_walk(model, where), "bias", None)))
+            elif kind == "experts":
+                holders.append(PackedParameter(*_owner(model, where), store, dtype))
+            else:
+                _install_dense(model, where, store.materialize(dtype).to(device))
+            counts["dense" if kind == "dense" else "packed"] += 1
+
+    if cfg is not None and getattr(cfg, "tie_word_embeddings", False) and embed_store is not None:
+        _replace_module(model, "lm_head", PackedLinear(embed_store))
         cfg.tie_word_embeddings = False
         if hasattr(model, "config"):
             model.config.tie_word_embeddings = False
         if verbose:
             print("  tied lm_head -> embedding store")
-
-
-def apply_to(model, path, device="cpu", cfg=None, verbose=True, dtype=None):
-    """Replace a module tree's weights with packed stores, in place (runtime.py:214-305).
-
-    Reads the ``.ebin`` container; each compressed tensor becomes a
-    PackedWeight on ``device`` (vector-codebook stores are laid out for the
-    GPU kernels as they land there).
-    """
-    if dtype is None:
-        dtype = next((p.dtype for p in model.parameters()
-                      if p.is_floating_point()), torch.float16)
-    header = container.read_header(path)
-    group, levels = header["group"], header["levels"]
-    vec = int(header.get("vec", 1))
-    n_packed = n_dense = 0
-    embed = []
-    holders = []
-
-    with open(path, "rb") as f:
-        for t in header["tensors"]:
-            name = t["name"]
-            if t["kind"] == "raw":
-                arr = np.frombuffer(container.read_blob(f, t["data"]),
-                                    np.float16).reshape(t["shape"])
-                _assign(model, name,
-                        torch.from_numpy(arr.copy()).to(device=device, dtype=dtype))
-                n_dense += 1
-                continue
-            cb = np.frombuffer(container.read_blob(f, t["cb"]), np.float32).copy()
-            if vec == 4:
-                cb = cb.reshape(-1, 4)
-            scale = np.frombuffer(container.read_blob(f, t["scale"]), np.float16
-                                  ).reshape(t["scale_shape"]).copy()
-            idx = container.rans_decode(container.read_blob(f, t["idx"]),
-                                        t["chunks"], t["counts"])
-            packed = idx if vec == 4 else _pack4(idx, levels)
-            store = PackedWeight(t["shape"], packed, scale, cb, group, levels,
-                                 vec=vec).to(device)
-            kind = attach_store(model, name, store, dtype, holders, embed)
-            if kind == "packed":
-                n_packed += 1
-            else:
-                n_dense += 1
-
-    tie_lm_head(model, cfg, embed[0] if embed else None, verbose)
     if holders:
         model._epure_holders = holders
     if verbose:
-        print(f"  {n_packed} packed + {n_dense} dense tensors from {path}")
+        print(f"  {counts['packed']} packed + {counts['dense']} dense tensors from {path}")
     return model
 
 
+def read_stores(path, device="cpu", tp=None):
+    """Every compressed tensor of container ``path`` as a PackedWeight, by name.
+
+    For callers that run their own decoder on the stores (epure.model,
+    epure.tp) instead of a module tree.  ``tp=(rank, world)`` keeps only this
+    rank's tensor-parallel shard of each decoder projection, cut on the host
+    before the shard is moved to ``device``: rows of ``*q_proj`` / ``k_proj`` /
+    ``v_proj`` / ``gate_proj`` / ``up_proj`` (column-parallel) and group-aligned
+    columns of ``*o_proj`` / ``down_proj`` (row-parallel); other tensors are
+    returned whole."""
+    from . import tp as tp_mod
+    out = {}
+    with container.Ebin(path) as ebin:
+        levels, group, vec = ebin.header["levels"], ebin.header["group"], ebin.vec
+        for rec in ebin.tensors():
+            if rec["kind"] == "raw":
+                continue
+            store = _read_store(ebin, rec, levels, group, vec)
+            stem = rec["name"][:-len(".weight")] if rec["name"].endswith(".weight") else rec["name"]
+            leaf = stem.rpartition(".")[2]
+            if tp is not None and tp[1] > 1 and leaf in tp_mod.COLUMN + tp_mod.ROW:
+                dim = "rows" if leaf in tp_mod.COLUMN else "cols"
+                store = tp_mod.shard_store(store, tp[0], tp[1], dim)
+            out[rec["name"]] = store.to(device)
+    return out
+
+
 def resolve(path, filename="model.ebin"):
-    """Accept either a local ``.ebin`` or a Hugging Face repo id (runtime.py:308-320)."""
+    """A local ``.ebin`` path as given, or a Hugging Face repo id ("org/name")
+    fetched into the hub cache (runtime.py:308-320)."""
     if os.path.exists(path):
         return path
-    if "/" not in path or os.path.isabs(path):
+    if os.path.isabs(path) or "/" not in path:
         raise FileNotFoundError(path)
     from huggingface_hub import hf_hub_download
     return hf_hub_download(repo_id=path, filename=filename)
 
 
+def _declared_dtype(cfg):
+    """The training dtype a transformers config declares (``torch_dtype`` before
+    ``dtype``: transformers fills ``dtype`` with a default of its own)."""
+    for key in ("torch_dtype", "dtype"):
+        value = getattr(cfg, key, None)
+        if value is not None:
+            return getattr(torch, value, None) if isinstance(value, str) else value
+    return None
+
+
 def _runtime_dtype(cfg, device):
-    """Run in the checkpoint's training precision, never narrowing bf16 to fp16 (runtime.py:323-370)."""
-    if device == "cpu":
+    """The dtype a model runs in (runtime.py:323-370): float32 on the CPU; on a GPU
+    bfloat16 when the checkpoint was trained in it (float32 where bf16 is not
+    supported -- never float16, whose range overflows bf16-trained
+    activations), float16 otherwise.  The choice is printed."""
+    if str(device) == "cpu":
         return torch.float32
-    want = getattr(cfg, "torch_dtype", None)
-    if want is None:
-        want = getattr(cfg, "dtype", None)
-    if isinstance(want, str):
-        want = getattr(torch, want, None)
+    want = _declared_dtype(cfg)
     if want is torch.bfloat16:
-        if torch.cuda.is_available() and torch.cuda.is_bf16_supported():
-            chosen = torch.bfloat16
-        else:
-            chosen = torch.float32
+        bf16_ok = torch.cuda.is_available() and torch.cuda.is_bf16_supported()
+        chosen = torch.bfloat16 if bf16_ok else torch.float32
     else:
         chosen = torch.float16
     print(f"  epure: config declares {want}, running in {chosen}", flush=True)
     return chosen
 
 
-def load(path, device=None):
-    """Load a ``.ebin`` as a model, from a local path or a HF repo id (runtime.py:373-415).
+@contextlib.contextmanager
+def _parameters_on_meta():
+    """Build modules with their parameters on the meta device and their buffers
+    real: every parameter is overwritten from the container, while buffers
+    computed at construction (rotary tables) are not stored in it."""
+    register = nn.Module.register_parameter
 
-    Returns (model, tokenizer).
-    """
+    def to_meta(module, name, param):
+        if param is not None and param.device.type != "meta":
+            param = nn.Parameter(param.detach().to("meta"), requires_grad=param.requires_grad)
+        register(module, name, param)
+
+    nn.Module.register_parameter = to_meta
+    try:
+        yield
+    finally:
+        nn.Module.register_parameter = register
+
+
+def load(path, device=None):
+    """(model, tokenizer) from a ``.ebin`` path or Hugging Face repo id (runtime.py:373-415).
+
+    The config and tokenizer files bundled in the container are written next
+    to it (``<path>.meta/``); the model class is the config's declared
+    architecture (AutoModelForCausalLM when transformers has no such class),
+    built with parameters on the meta device and filled by ``apply_to``."""
     import transformers
-    from transformers import AutoConfig, AutoModelForCausalLM, AutoTokenizer
 
     path = resolve(path)
     device = device or ("cuda" if torch.cuda.is_available() else "cpu")
-    tmp = path + ".meta"
-    os.makedirs(tmp, exist_ok=True)
-    for name, data in container.extras(path).items():
-        with open(os.path.join(tmp, name), "wb") as f:
+    meta_dir = path + ".meta"
+    os.makedirs(meta_dir, exist_ok=True)
+    for fname, data in container.extras(path).items():
+        with open(os.path.join(meta_dir, fname), "wb") as f:
             f.write(data)
-
-    cfg = AutoConfig.from_pretrained(tmp)
+    cfg = transformers.AutoConfig.from_pretrained(meta_dir)
     cfg.use_cache = True
-    tok = AutoTokenizer.from_pretrained(tmp)
+    tok = transformers.AutoTokenizer.from_pretrained(meta_dir)
     arch = (getattr(cfg, "architectures", None) or [None])[0]
-    factory = getattr(transformers, arch, None) if arch else None
-    if factory is None:
-        factory = AutoModelForCausalLM
-    with torch.device("meta"):
-        model = (factory.from_config(cfg) if factory is AutoModelForCausalLM
-                 else factory(cfg))
-    chosen_dtype = _runtime_dtype(cfg, device)
-    model = model.to_empty(device=device).to(dtype=chosen_dtype)
-    apply_to(model, path, device=device, cfg=cfg, dtype=chosen_dtype)
+    cls = getattr(transformers, arch, None) if arch else None
+    with _parameters_on_meta():
+        model = cls(cfg) if cls is not None else transformers.AutoModelForCausalLM.from_config(cfg)
+    dtype = _runtime_dtype(cfg, device)
+    model = model.to(dtype=dtype)
+    apply_to(model, path, device=device, cfg=cfg, dtype=dtype)
     return model.eval(), tok
