@@ -5,7 +5,8 @@
 Compiles every csrc/*.cu with nvcc into epure/libepq.so next to the Python
 package, so the library travels with the source tree.  Object files go to
 csrc/_build/.  A source is recompiled only when it or a header is newer than
-its object.
+its object.  The CPU kernel (csrc_cpu/epq_cpu.cpp, include/epq_cpu.h) is built
+with g++/OpenMP into epure/libepq_cpu.so.
 """
 import argparse
 import glob
@@ -18,6 +19,8 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 OBJ = os.path.join(CSRC, "_build")
 OUT = os.path.join(HERE, "epure", "libepq.so")
+CPU_SRC = os.path.join(HERE, "csrc_cpu", "epq_cpu.cpp")
+CPU_OUT = os.path.join(HERE, "epure", "libepq_cpu.so")
 INCLUDE = os.path.join(ROOT, "include")
 
 NVCC_FLAGS = [
@@ -58,7 +61,31 @@ def build(verbose_ptxas=False, force=False, quiet=False):
         cmd = [_nvcc(), "-shared", "-gencode", "arch=compute_100a,code=sm_100a",
                *objs, "-o", OUT, "-lcudart_static", "-lrt", "-ldl", "-lpthread"]
         subprocess.check_call(cmd)
+    build_cpu(force=force, quiet=quiet)
     return OUT
+
+
+def _cxx():
+    """A g++ with OpenMP: EPURE_CXX, else the system g++ (a toolchain named by CXX
+    may lack libgomp)."""
+    for cand in (os.environ.get("EPURE_CXX"), "/usr/bin/g++", "g++"):
+        if cand and (not os.path.isabs(cand) or os.path.exists(cand)):
+            return cand
+    return "g++"
+
+
+def build_cpu(force=False, quiet=False):
+    """libepq_cpu.so: -ffp-contract=off keeps the reference's unfused multiply-then-add."""
+    header = os.path.join(INCLUDE, "epq_cpu.h")
+    newest = max(os.path.getmtime(CPU_SRC), os.path.getmtime(header))
+    if not force and os.path.exists(CPU_OUT) and os.path.getmtime(CPU_OUT) >= newest:
+        return CPU_OUT
+    cmd = [_cxx(), "-O3", "-std=c++17", "-fPIC", "-shared", "-fopenmp",
+           "-ffp-contract=off", "-I", INCLUDE, CPU_SRC, "-o", CPU_OUT]
+    if not quiet:
+        print(" ".join(os.path.relpath(c, ROOT) if c.startswith(ROOT) else c for c in cmd), flush=True)
+    subprocess.check_call(cmd)
+    return CPU_OUT
 
 
 if __name__ == "__main__":

@@ -245,7 +245,9 @@ class PackedLinear(nn.Module):
             if x.is_cuda:
                 # Every batch size runs the packed kernels; errors raise.
                 out = cuda_kernel.linear(x, s)
-            elif s.levels <= 16:
+            else:
+                # f32 CPU activations run the fused C++ kernel (it declines
+                # otherwise, and when autograd needs this call's gradients)
                 out = cpu_kernel.linear(x, s, _BUFFER_CACHE)
             if out is not None:
                 return out + self.bias if self.bias is not None else out
