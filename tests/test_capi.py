@@ -9,10 +9,13 @@ import pytest
 from conftest import ROOT
 
 
-def _declared():
+CPU_HEADER = "epq_cpu.h"      # declared by libepq_cpu.so (the CPU kernel), not libepq.so
+
+
+def _declared(cpu=False):
     names = set()
     for h in sorted(os.listdir(os.path.join(ROOT, "include"))):
-        if h.endswith(".h"):
+        if h.endswith(".h") and (h == CPU_HEADER) == cpu:
             src = open(os.path.join(ROOT, "include", h)).read()
             src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
             names |= set(re.findall(r"\b(epq_[a-z0-9_]+)\s*\(", src))
@@ -35,6 +38,16 @@ def test_every_declared_symbol_is_exported(lib):
 def test_python_binding_covers_header():
     from epure import _native
     assert set(_declared()) <= set(_native.EXPORTS)
+
+
+def test_cpu_library_exports_its_header():
+    from epure.kernels import cpu
+    lib = cpu._load()
+    assert lib is not None
+    names = _declared(cpu=True)
+    assert "epq_cpu_linear" in names
+    for name in names:
+        assert hasattr(lib, name), name
 
 
 def test_abi_version(lib):
