@@ -1,6 +1,7 @@
 """The drop-in host API (epure.runtime / epure.finetune) on the CPU, against the
-reference's recorded outputs.  No GPU is needed: on the CPU a PackedLinear
-materializes, exactly as the reference does without its Rust extension."""
+reference's recorded outputs.  No GPU is needed: on the CPU a PackedLinear runs
+the fused CPU kernel for f32 activations and materializes for 16-bit ones (and
+whenever gradients are needed), as the reference does with its Rust extension."""
 import numpy as np
 import pytest
 import torch
