@@ -4,9 +4,43 @@
 #include <stdarg.h>
 #include <stdio.h>
 
+#include <mutex>
+#include <set>
+#include <tuple>
+
 #include "epq_common.cuh"
 
 namespace epq {
+
+namespace {
+std::mutex g_attr_mutex;
+std::set<std::tuple<const void*, int, int>> g_attr_done;   // (kernel, device, bytes)
+int g_dev_sms[64] = {0};
+}  // namespace
+
+int set_smem_limit(const void* fn, int bytes, const char* who) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return check_launch(who);
+    std::lock_guard<std::mutex> lock(g_attr_mutex);
+    const auto key = std::make_tuple(fn, dev, bytes);
+    if (g_attr_done.count(key)) return EPQ_OK;
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+        return check_launch(who);
+    g_attr_done.insert(key);
+    return EPQ_OK;
+}
+
+int device_sms() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    std::lock_guard<std::mutex> lock(g_attr_mutex);
+    if (g_dev_sms[dev] == 0) {
+        int v = 0;
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+        g_dev_sms[dev] = v;
+    }
+    return g_dev_sms[dev];
+}
 
 static thread_local char g_err[512] = "";
 
@@ -78,6 +112,7 @@ int make_store(const epq_store* in, StoreD* s, const char* who) {
 int lut_read_device_error(int* flag);
 int mma_read_device_error(int* flag);
 int chain_read_device_error(int* flag);
+int glue_read_device_error(int* flag);
 
 static bool x_ok(const void* x, int64_t m, int64_t k, int64_t ldx) {
     return (m == 0 || k == 0) || (x != nullptr && ldx >= k);
@@ -113,11 +148,14 @@ int epq_device_error(int* flag) {
     int emb = 0;
     rc = embed_read_device_error(&emb);
     if (rc) return rc;
+    int glue = 0;
+    rc = glue_read_device_error(&glue);
+    if (rc) return rc;
     // bit 0: LUT placement check; bit 1: a bounded wait gave up (GEMV, GEMM, backward or chain);
     // bit 2: the chain kernel's placement or grid check failed; bit 3: an embedding id was
-    // outside the store's rows
+    // outside the store's rows; bit 4: a decode position was at or past the KV cache's capacity
     *flag = (lut ? 1 : 0) | ((mma || tc || bwd || chain == 1) ? 2 : 0) | (chain == 2 ? 4 : 0) |
-            (emb ? 8 : 0);
+            (emb ? 8 : 0) | (glue ? 16 : 0);
     return EPQ_OK;
 }
 

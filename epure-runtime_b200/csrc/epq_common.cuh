@@ -88,6 +88,11 @@ __device__ __forceinline__ float scale_at(const StoreD& s, int64_t r, int64_t g)
 // host-side helpers
 // ---------------------------------------------------------------------------
 int set_error(int code, const char* fmt, ...);
+// Raises kernel `fn`'s dynamic shared-memory limit to `bytes` on the current
+// device, once per (kernel, device, bytes); thread-safe (epq_capi.cu).
+int set_smem_limit(const void* fn, int bytes, const char* who);
+// The current device's SM count, cached per device; thread-safe.
+int device_sms();
 int check_launch(const char* what);
 int make_store(const epq_store* in, StoreD* out, const char* who);
 

@@ -231,5 +231,8 @@ __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
 // fill outside the matrix (k_gemm_tc.cu).
 int make_tmap_2d(CUtensorMap* map, const void* base, int dtype, int64_t inner, int64_t outer,
                  int64_t ld, int box_inner, int box_outer, const char* who);
+// The same without swizzle, for 2- or 4-byte elements (k_gemm_tc.cu).
+int make_tmap_2d_plain(CUtensorMap* map, const void* base, int elem_bytes, int64_t inner, int64_t outer,
+                       int64_t ld, int box_inner, int box_outer, const char* who);
 
 }  // namespace epq

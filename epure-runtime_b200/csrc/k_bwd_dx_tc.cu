@@ -303,18 +303,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-bool g_dx_attr[3][2][2][64];
 
 template <bool kBf16, int kLayout, int BN>
 int launch_dx(const CUtensorMap& ymap, const DxParams& P, int bi, cudaStream_t st, int dev) {
     using C = Cfg<BN>;
     auto kern = bwd_dx_tc_kernel<kBf16, kLayout, BN>;
-    bool& done = g_dx_attr[bi][kBf16 ? 1 : 0][kLayout == EPQ_LAYOUT_MMA16 ? 1 : 0][dev];
-    if (!done) {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) != cudaSuccess)
-            return check_launch("cudaFuncSetAttribute(bwd_dx_tc_kernel)");
-        done = true;
-    }
+    (void)bi;
+    (void)dev;
+    const int arc = set_smem_limit(reinterpret_cast<const void*>(kern), C::kSmem, "cudaFuncSetAttribute(bwd_dx_tc_kernel)");
+    if (arc != EPQ_OK) return arc;
     const dim3 grid((unsigned)P.ng, (unsigned)cdiv(P.m, BN));
     kern<<<grid, kThreads, C::kSmem, st>>>(ymap, P);
     return check_launch("bwd_dx_tc_kernel");

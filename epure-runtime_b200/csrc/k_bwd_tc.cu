@@ -236,7 +236,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-bool g_bwd_attr[2][64];
 
 }  // namespace
 
@@ -290,11 +289,8 @@ int launch_bwd_dw_tc(const StoreD& s, const void* x, int64_t ldx, const void* dy
     P.m = (int)m;
     const bool bf = act_dtype == EPQ_BF16;
     auto kern = bf ? bwd_dw_tc_kernel<true> : bwd_dw_tc_kernel<false>;
-    if (!g_bwd_attr[bf ? 1 : 0][dev]) {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess)
-            return check_launch("cudaFuncSetAttribute(bwd_dw_tc_kernel)");
-        g_bwd_attr[bf ? 1 : 0][dev] = true;
-    }
+    const int arc = set_smem_limit(reinterpret_cast<const void*>(kern), kSmem, "cudaFuncSetAttribute(bwd_dw_tc_kernel)");
+    if (arc != EPQ_OK) return arc;
     const dim3 grid((unsigned)cdiv(s.n, kBT), (unsigned)s.ng);
     kern<<<grid, kThreads, kSmem, st>>>(ymap, xmap, P);
     return check_launch("bwd_dw_tc_kernel");

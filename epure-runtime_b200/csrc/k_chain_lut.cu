@@ -48,6 +48,8 @@
 #include <cstring>
 #include <vector>
 
+#include <mutex>
+
 #include "epq_common.cuh"
 
 namespace epq {
@@ -916,18 +918,22 @@ int chain_grid(int* grid) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
         return set_error(EPQ_EUNSUPPORTED, "chain: no usable current device");
-    if (!g_chain_attr[dev]) {
-        if (cudaFuncSetAttribute(chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmem) !=
-            cudaSuccess)
-            return check_launch("cudaFuncSetAttribute(chain_kernel)");
-        int per_sm = 0, sms = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, chain_kernel, kThreads, kDynSmem) !=
-                cudaSuccess ||
-            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-            return check_launch("chain occupancy");
-        if (per_sm < 1) return set_error(EPQ_EUNSUPPORTED, "chain: kernel does not fit on an SM");
-        g_chain_sms[dev] = sms;
-        g_chain_attr[dev] = true;
+    {
+        static std::mutex mu;
+        std::lock_guard<std::mutex> lock(mu);
+        if (!g_chain_attr[dev]) {
+            if (cudaFuncSetAttribute(chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmem) !=
+                cudaSuccess)
+                return check_launch("cudaFuncSetAttribute(chain_kernel)");
+            int per_sm = 0, sms = 0;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, chain_kernel, kThreads, kDynSmem) !=
+                    cudaSuccess ||
+                cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+                return check_launch("chain occupancy");
+            if (per_sm < 1) return set_error(EPQ_EUNSUPPORTED, "chain: kernel does not fit on an SM");
+            g_chain_sms[dev] = sms;
+            g_chain_attr[dev] = true;
+        }
     }
     *grid = g_chain_sms[dev];
     return EPQ_OK;

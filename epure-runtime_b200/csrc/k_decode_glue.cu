@@ -23,6 +23,10 @@
 namespace epq {
 namespace {
 
+// Set when a decode position is at or past the KV cache's capacity (max_len):
+// the kernel then writes nothing to the cache and zeros to its output.
+__device__ int g_glue_position_error = 0;
+
 // Programmatic dependent launch: every glue kernel is launched allowed to start
 // while the previous kernel in the stream is still running; it lets its own
 // dependents launch at once and waits for the previous grid's completion (and
@@ -95,7 +99,7 @@ __global__ void __launch_bounds__(128) rope_kv_kernel(
     void* __restrict__ q, const void* __restrict__ k, const void* __restrict__ v,
     const int64_t* __restrict__ pos, int H, int KV, int hd, const float* __restrict__ cos_t,
     const float* __restrict__ sin_t, void* __restrict__ k_cache, void* __restrict__ v_cache,
-    int qk_norm, float eps, int dtype) {
+    int qk_norm, float eps, int dtype, int64_t max_len) {
     pdl_enter();
     __shared__ float red[32];
     const int64_t row = blockIdx.x;
@@ -104,6 +108,10 @@ __global__ void __launch_bounds__(128) rope_kv_kernel(
     const bool is_q = head < H;
     const int kh = head - H;
     const int64_t p = pos[row];
+    if (p < 0 || p >= max_len) {   // uniform per CTA: nothing is written
+        if (i == 0) atomicExch(&g_glue_position_error, 1);
+        return;
+    }
     const void* src = is_q ? static_cast<const void*>(q) : k;
     const int64_t base = is_q ? (row * H + head) * hd : (row * KV + kh) * hd;
     float x1 = load_f(src, dtype, base + i), x2 = load_f(src, dtype, base + i + half);
@@ -186,7 +194,7 @@ template <int kDims, int kGroup>
 __global__ void __launch_bounds__(kAttnWarps * 32) attn_split_kernel(
     const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k_cache,
     const __nv_bfloat16* __restrict__ v_cache, const int64_t* __restrict__ pos, int KV, float scale,
-    __nv_bfloat16* __restrict__ out, float* __restrict__ ws, unsigned* __restrict__ counters) {
+    __nv_bfloat16* __restrict__ out, float* __restrict__ ws, unsigned* __restrict__ counters, int64_t max_len) {
     pdl_enter();
     constexpr int hd = kDims * 32;
     constexpr int kRec = hd + 2;                       // acc[hd], max, sum
@@ -195,6 +203,14 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_split_kernel(
     __shared__ bool last;
     const int kvh = blockIdx.x, split = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (pos[0] < 0 || pos[0] >= max_len) {   // every CTA sees the same position: all return here
+        if (split == 0) {
+            for (int e = threadIdx.x; e < kGroup * hd; e += kAttnWarps * 32)
+                out[(int64_t)kvh * kGroup * hd + e] = __float2bfloat16_rn(0.f);
+            if (threadIdx.x == 0) atomicExch(&g_glue_position_error, 1);
+        }
+        return;
+    }
     const int64_t n = pos[0] + 1;
     const int64_t chunk = (n + kAttnSplits - 1) / kAttnSplits;
     const int64_t t0 = split * chunk, t1 = min(n, t0 + chunk);
@@ -324,7 +340,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_rope_split_kernel(
     const __nv_bfloat16* __restrict__ v_in, __nv_bfloat16* __restrict__ k_cache,
     __nv_bfloat16* __restrict__ v_cache, const int64_t* __restrict__ pos, int KV,
     const float* __restrict__ cos_t, const float* __restrict__ sin_t, int qk_norm, float eps, float scale,
-    __nv_bfloat16* __restrict__ out, float* __restrict__ ws, unsigned* __restrict__ counters) {
+    __nv_bfloat16* __restrict__ out, float* __restrict__ ws, unsigned* __restrict__ counters, int64_t max_len) {
     pdl_enter();
     constexpr int hd = kDims * 32;
     constexpr int kRec = hd + 2;
@@ -334,6 +350,14 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_rope_split_kernel(
     const int kvh = blockIdx.x, split = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t P = pos[0];
+    if (P < 0 || P >= max_len) {   // every CTA sees the same position: all return here
+        if (split == 0) {
+            for (int e = threadIdx.x; e < kGroup * hd; e += kAttnWarps * 32)
+                out[(int64_t)kvh * kGroup * hd + e] = __float2bfloat16_rn(0.f);
+            if (threadIdx.x == 0) atomicExch(&g_glue_position_error, 1);
+        }
+        return;
+    }
     const int64_t n = P + 1;
     const int64_t chunk = (n + kAttnSplits - 1) / kAttnSplits;
     const int64_t t0 = split * chunk, t1 = min(n, t0 + chunk);
@@ -510,7 +534,8 @@ __global__ void __launch_bounds__(256) argmax_kernel(const float* __restrict__ x
 template <int kDims>
 __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(
     const void* __restrict__ q, const void* __restrict__ k_cache, const void* __restrict__ v_cache,
-    const int64_t* __restrict__ pos, int H, int KV, float scale, void* __restrict__ out, int dtype) {
+    const int64_t* __restrict__ pos, int H, int KV, float scale, void* __restrict__ out, int dtype,
+    int64_t max_len) {
     pdl_enter();
     constexpr int hd = kDims * 32;
     __shared__ float wm[kAttnWarps], wl[kAttnWarps];
@@ -518,6 +543,11 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(
     const int head = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int kvh = head / (H / KV);
     const int64_t P = pos[0];
+    if (P < 0 || P >= max_len) {
+        for (int e = threadIdx.x; e < hd; e += kAttnWarps * 32) store_f(out, dtype, (int64_t)head * hd + e, 0.f);
+        if (threadIdx.x == 0) atomicExch(&g_glue_position_error, 1);
+        return;
+    }
     float qv[kDims];
 #pragma unroll
     for (int d = 0; d < kDims; ++d) qv[d] = load_f(q, dtype, (int64_t)head * hd + lane * kDims + d);
@@ -572,6 +602,13 @@ __global__ void silu_mul_kernel(const void* __restrict__ g, const void* __restri
 bool glue_dtype_ok(int d) { return d == EPQ_F32 || d == EPQ_F16 || d == EPQ_BF16; }
 
 }  // namespace
+
+int glue_read_device_error(int* flag) {
+    if (cudaMemcpyFromSymbol(flag, g_glue_position_error, sizeof(int)) != cudaSuccess)
+        return check_launch("read decode glue error flag");
+    return EPQ_OK;
+}
+
 }  // namespace epq
 
 using namespace epq;
@@ -598,8 +635,9 @@ int epq_add_rmsnorm(const void* x, const void* add, void* h_out, void* y, int64_
 
 int epq_rope_kv(void* q, const void* k, const void* v, const int64_t* pos, int64_t m, int32_t heads,
                 int32_t kv_heads, int32_t head_dim, const float* cos_tab, const float* sin_tab,
-                void* k_cache, void* v_cache, int32_t qk_norm, float eps, int32_t dtype, void* stream) {
-    if (!q || !k || !v || !pos || !cos_tab || !sin_tab || !k_cache || !v_cache || m < 0)
+                void* k_cache, void* v_cache, int64_t max_len, int32_t qk_norm, float eps, int32_t dtype,
+                void* stream) {
+    if (!q || !k || !v || !pos || !cos_tab || !sin_tab || !k_cache || !v_cache || m < 0 || max_len <= 0)
         return set_error(EPQ_EINVAL, "epq_rope_kv: bad arguments");
     if (!glue_dtype_ok(dtype)) return set_error(EPQ_EDTYPE, "epq_rope_kv: dtype %d", dtype);
     if ((head_dim != 64 && head_dim != 128 && head_dim != 256) || heads <= 0 || kv_heads <= 0 ||
@@ -610,7 +648,7 @@ int epq_rope_kv(void* q, const void* k, const void* v, const int64_t* pos, int64
     return launch_pdl(rope_kv_kernel, dim3((unsigned)m, heads + kv_heads), dim3(head_dim / 2), 0,
                       static_cast<cudaStream_t>(stream), "epq_rope_kv", q, k, v, pos, (int)heads,
                       (int)kv_heads, (int)head_dim, cos_tab, sin_tab, k_cache, v_cache, (int)qk_norm, eps,
-                      (int)dtype);
+                      (int)dtype, max_len);
 }
 
 int64_t epq_attn_decode_workspace_bytes(int32_t heads, int32_t kv_heads, int32_t head_dim) {
@@ -619,9 +657,10 @@ int64_t epq_attn_decode_workspace_bytes(int32_t heads, int32_t kv_heads, int32_t
 }
 
 int epq_attn_decode(const void* q, const void* k_cache, const void* v_cache, const int64_t* pos,
-                    int32_t heads, int32_t kv_heads, int32_t head_dim, float scale, void* out,
+                    int64_t max_len, int32_t heads, int32_t kv_heads, int32_t head_dim, float scale, void* out,
                     int32_t dtype, void* workspace, int64_t workspace_bytes, void* stream) {
-    if (!q || !k_cache || !v_cache || !pos || !out || heads <= 0 || kv_heads <= 0 || heads % kv_heads)
+    if (!q || !k_cache || !v_cache || !pos || !out || heads <= 0 || kv_heads <= 0 || heads % kv_heads ||
+        max_len <= 0)
         return set_error(EPQ_EINVAL, "epq_attn_decode: bad arguments");
     if (!glue_dtype_ok(dtype)) return set_error(EPQ_EDTYPE, "epq_attn_decode: dtype %d", dtype);
     if (head_dim != 64 && head_dim != 128)
@@ -645,7 +684,7 @@ int epq_attn_decode(const void* q, const void* k_cache, const void* v_cache, con
         auto* ob = static_cast<__nv_bfloat16*>(out);
         const dim3 grid(kv_heads, kAttnSplits);
 #define EPQ_ATTN_SPLIT(D, G) return launch_pdl(attn_split_kernel<D, G>, grid, dim3(kAttnWarps * 32), 0, st, \
-                                             "epq_attn_decode", qb, kb, vb, pos, (int)kv_heads, scale, ob, ws, ctr)
+                                             "epq_attn_decode", qb, kb, vb, pos, (int)kv_heads, scale, ob, ws, ctr, max_len)
         if (head_dim == 128) {
             if (group == 1) EPQ_ATTN_SPLIT(4, 1);
             else if (group == 2) EPQ_ATTN_SPLIT(4, 2);
@@ -660,20 +699,20 @@ int epq_attn_decode(const void* q, const void* k_cache, const void* v_cache, con
 #undef EPQ_ATTN_SPLIT
     } else if (head_dim == 128) {
         return launch_pdl(attn_decode_kernel<4>, dim3(heads), dim3(kAttnWarps * 32), 0, st, "epq_attn_decode",
-                          q, k_cache, v_cache, pos, (int)heads, (int)kv_heads, scale, out, (int)dtype);
+                          q, k_cache, v_cache, pos, (int)heads, (int)kv_heads, scale, out, (int)dtype, max_len);
     } else {
         return launch_pdl(attn_decode_kernel<2>, dim3(heads), dim3(kAttnWarps * 32), 0, st, "epq_attn_decode",
-                          q, k_cache, v_cache, pos, (int)heads, (int)kv_heads, scale, out, (int)dtype);
+                          q, k_cache, v_cache, pos, (int)heads, (int)kv_heads, scale, out, (int)dtype, max_len);
     }
     return check_launch("epq_attn_decode");
 }
 
 int epq_attn_rope_decode(const void* q, const void* k, const void* v, const int64_t* pos, int32_t heads,
                          int32_t kv_heads, int32_t head_dim, const float* cos_tab, const float* sin_tab,
-                         void* k_cache, void* v_cache, int32_t qk_norm, float eps, float scale, void* out,
-                         int32_t dtype, void* workspace, int64_t workspace_bytes, void* stream) {
+                         void* k_cache, void* v_cache, int64_t max_len, int32_t qk_norm, float eps, float scale,
+                         void* out, int32_t dtype, void* workspace, int64_t workspace_bytes, void* stream) {
     if (!q || !k || !v || !pos || !cos_tab || !sin_tab || !k_cache || !v_cache || !out || !workspace ||
-        heads <= 0 || kv_heads <= 0 || heads % kv_heads)
+        heads <= 0 || kv_heads <= 0 || heads % kv_heads || max_len <= 0)
         return set_error(EPQ_EINVAL, "epq_attn_rope_decode: bad arguments");
     const int group = heads / kv_heads;
     if (dtype != EPQ_BF16 || (head_dim != 64 && head_dim != 128) ||
@@ -696,7 +735,8 @@ int epq_attn_rope_decode(const void* q, const void* k, const void* v, const int6
     const dim3 grid(kv_heads, kAttnSplits);
 #define EPQ_ATTN_ROPE(D, G)                                                                                 \
     return launch_pdl(attn_rope_split_kernel<D, G>, grid, dim3(kAttnWarps * 32), 0, st, "epq_attn_rope_decode", \
-                      qb, kb, vb, kcb, vcb, pos, (int)kv_heads, cos_tab, sin_tab, (int)qk_norm, eps, scale, ob, ws, ctr)
+                      qb, kb, vb, kcb, vcb, pos, (int)kv_heads, cos_tab, sin_tab, (int)qk_norm, eps, scale, ob, ws, ctr, \
+                      max_len)
     if (head_dim == 128) {
         if (group == 1) EPQ_ATTN_ROPE(4, 1);
         if (group == 2) EPQ_ATTN_ROPE(4, 2);

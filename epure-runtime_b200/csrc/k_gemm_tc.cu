@@ -410,22 +410,37 @@ int make_tmap_2d(CUtensorMap* map, const void* base, int dtype, int64_t inner, i
     return EPQ_OK;
 }
 
+// 2-D tensor map without swizzle over `outer` rows of `inner` elements of
+// `elem_bytes` (2 or 4) with a row stride of `ld` elements; box {box_inner,
+// box_outer}; out-of-range boxes are zero-filled.
+int make_tmap_2d_plain(CUtensorMap* map, const void* base, int elem_bytes, int64_t inner, int64_t outer,
+                       int64_t ld, int box_inner, int box_outer, const char* who) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc = encode_fn();
+    if (!enc) return set_error(EPQ_EUNSUPPORTED, "%s: cuTensorMapEncodeTiled unavailable", who);
+    const cuuint64_t gdim[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+    const cuuint64_t gstride[1] = {(cuuint64_t)(ld * elem_bytes)};
+    const cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer};
+    const cuuint32_t estride[2] = {1, 1};
+    const CUresult cr = enc(map, elem_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16,
+                            2, const_cast<void*>(base), gdim, gstride, box, estride,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                            CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (cr != CUDA_SUCCESS) return set_error(EPQ_EINVAL, "%s: tensor map (error %d)", who, (int)cr);
+    return EPQ_OK;
+}
+
 namespace {
 
-bool g_attr[3][2][2][64];
 
 template <bool kBf16, int kLayout, int BN>
 int launch_tc(const CUtensorMap& xmap, const TcParams& P, int tiles, int bi, cudaStream_t st,
               int dev) {
     using C = Cfg<BN>;
     auto kern = gemm_tc_kernel<kBf16, kLayout, BN>;
-    bool& done = g_attr[bi][kBf16 ? 1 : 0][kLayout == EPQ_LAYOUT_MMA16 ? 1 : 0][dev];
-    if (!done) {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) !=
-            cudaSuccess)
-            return check_launch("cudaFuncSetAttribute(gemm_tc_kernel)");
-        done = true;
-    }
+    (void)bi;
+    (void)dev;
+    const int arc = set_smem_limit(reinterpret_cast<const void*>(kern), C::kSmem, "cudaFuncSetAttribute(gemm_tc_kernel)");
+    if (arc != EPQ_OK) return arc;
     const dim3 grid(tiles, (unsigned)cdiv(P.m, BN));
     kern<<<grid, kThreads, C::kSmem, st>>>(xmap, P);
     return check_launch("gemm_tc_kernel");

@@ -293,22 +293,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_lut_kernel(const __grid_cons
     }
 }
 
-int g_num_sms[64] = {0};
-
-int num_sms() {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64) return 148;
-    if (g_num_sms[dev] == 0) {
-        int v = 0;
-        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0)
-            v = 148;
-        g_num_sms[dev] = v;
-    }
-    return g_num_sms[dev];
-}
-
-bool g_attr_set[64] = {false};
+int num_sms() { return device_sms(); }
 
 }  // namespace
 
@@ -345,11 +330,10 @@ int launch_linear_lut(const StoreD* s, int count, const void* x, int x_dtype, vo
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return set_error(EPQ_EUNSUPPORTED, "device ordinal %d", dev);
-    if (!g_attr_set[dev]) {
-        if (cudaFuncSetAttribute(gemv_lut_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 kDynSmem) != cudaSuccess)
-            return check_launch("cudaFuncSetAttribute(gemv_lut_kernel)");
-        g_attr_set[dev] = true;
+    {
+        const int arc = set_smem_limit(reinterpret_cast<const void*>(gemv_lut_kernel), kDynSmem,
+                                       "cudaFuncSetAttribute(gemv_lut_kernel)");
+        if (arc != EPQ_OK) return arc;
     }
     LutParams P{};
     P.count = count;
@@ -457,9 +441,13 @@ int launch_linear_lut_static(const StoreD* s, int count, const void* x, int x_dt
         ptr = g_static_ptr[dev];
     }
     // The completion counters must start at zero; clear the ones this call uses
-    // (partial sums are written before they are read).
+    // (partial sums are written before they are read).  Stores with more row
+    // blocks than the counter region holds are refused before anything is cleared.
     int64_t n_counters = 0;
     for (int i = 0; i < count; ++i) n_counters += s[i].rb;
+    if (!lut_counters_fit(s, count))
+        return set_error(EPQ_EUNSUPPORTED, "linear_noalloc: %lld row blocks exceed the %lld counters of the "
+                         "batch-1 kernel", (long long)n_counters, (long long)(kCounterRegionBytes / 4));
     if (cudaMemsetAsync(ptr, 0, n_counters * 4, st) != cudaSuccess)
         return check_launch("linear_noalloc: clear counters");
     return launch_linear_lut(s, count, x, x_dtype, outs, out_dtype, ptr, kStaticScratchBytes, st);

@@ -3,43 +3,64 @@
 // W[r, 4j+p] = cb[idx[r, j], p] * scale[r, g(j)].
 //
 // Reference op: epure/kernels/_triton.py:56-107 (_dequant_matmul, table mode):
-// gather cb[idx] per weight, multiply by the group scale, tl.dot with x.
+// gather cb[idx] per weight, multiply by the group scale, tl.dot with x.  The
+// weight it contracts is the reference's own, rounded as the bf16 / fp16 path
+// rounds it (epure/runtime.py:78-89, PackedWeight.materialize):
+//     W = dtype( dtype(cb[idx]) * dtype(scale) )
+// i.e. the codebook and the scale are each rounded to the activation type and
+// their product is rounded once more.  This kernel forms exactly that value
+// for every weight (a bf16x2 / f16x2 multiply of the gathered codebook pair by
+// the row's rounded scale), so its only difference from the reference's
+// F.linear(x, materialize(dtype)) is the fp32 summation order.
 //
 // Design (B200, sm_100a).  The op is HBM-bound (1 index byte per 4 weights),
-// so everything is built around a cheap gather per index byte and a low
-// instruction count per byte:
-// * mma.m16n8k16 with A = 16 dequantised weight rows x 16 k and B = the
+// and at batch 1 the binding on-chip resource is the shared-memory gather of
+// the codebook (8 bytes per index byte), so everything is built around one
+// conflict-free 64-bit gather per index and a short instruction stream:
+// * mma.m16n8k16 with A = 16 decoded weight rows x 16 k and B = the
 //   activations (8 columns = 8 activation rows; two MMAs when M > 8).  The k
 //   axis is permuted so that the four k slots a thread holds for one A row
 //   ({2q, 2q+1, 2q+8, 2q+9}) are the four weights of ONE codebook vector: a
-//   thread's A fragment for a row is exactly one 8-byte codebook entry, one
-//   64-bit shared load.  B is permuted the same way, so a thread's B fragment
-//   is 4 consecutive activations (one 64-bit load).
-// * The codebook is replicated 16 times in shared memory (copy c in bank pair
-//   c) and lane l reads copy l % 16, so the random gathers of a half-warp never
-//   share a bank.  Codebook values are converted to the activation type
-//   (cb.to(dtype), as the reference's bf16 path does); the group scale
-//   multiplies the fp32 accumulator, once per row per group.
+//   thread's A fragment for a row is one 8-byte codebook entry (one 64-bit
+//   shared load) times the row's scale (two packed multiplies).
+// * The codebook is replicated 32 times in shared memory (entry e, copy c at
+//   byte e * 256 + c * 8) and lane l reads copy l: one byte permute forms the
+//   gather address, and the 32 lanes' random gathers fill every bank pair
+//   exactly twice (the 2-wavefront minimum of a 256-byte request).
+// * Activations are staged in shared memory in the B-fragment order of two
+//   consecutive k-steps per 16-byte word: one 128-bit load feeds two MMAs, and
+//   the four lanes of a row read one contiguous 64-byte run (no conflicts).
 // * Index layout EPQ_LAYOUT_MMA16: per (16-row block, group) a 512-byte tile;
 //   lane 4*r + q holds the indices of rows r and r + 8 at positions q + 4s,
-//   s = 0..7.  Tiles run group-fastest, so the 32 groups of one 16-row block
-//   ("chunk") are one contiguous 16 KB run.
-// * A producer warp streams chunks with TMA bulk copies (cp.async.bulk, into this
-//   CTA's shared memory only) into a 4-stage shared-memory ring guarded by mbarriers: one
-//   16 KB copy for the indices and one 32/64-byte copy per group for the
-//   scales (stored group-major, rows padded to 16).  16 consumer warps each
-//   take two tiles of a chunk; per tile a lane does 16 gathers (PRMT + IMAD +
-//   LDS.64), 8 MMAs and 8 activation loads from shared memory.
-// * Full rows per CTA, no split over k between CTAs: one CTA per SM owns a
-//   contiguous range of 16-row blocks; per block the consumer warps' sums are
-//   added in warp order through shared memory (deterministic).  No workspace,
-//   no atomics.  With programmatic dependent launch the producer starts
-//   streaming weights before the previous kernel (which produces x) finishes.
+//   s = 0..7.  Tiles run group-fastest, so the groups of one 16-row block are
+//   one contiguous run.
+// * A producer warp streams 32-group chunks through a 4-stage shared-memory
+//   ring guarded by mbarriers, two copies per chunk into this CTA's shared
+//   memory only: the index tiles (cp.async.bulk, one contiguous run) and the
+//   chunk's 16 x 32 scales (one 2-D cp.async.bulk.tensor box over the
+//   group-major scales).  16 consumer warps each take two tiles of a chunk,
+//   interleaved so their gathers and MMAs overlap.
+// * Full rows per CTA (no split over k between CTAs): one CTA per SM owns a
+//   contiguous range of 16-row blocks ("units").  At the end of a unit every
+//   warp drops its partial sums into one of kSlots shared-memory slots and
+//   counts itself in with a shared-memory atomic; the last warp to arrive adds
+//   the 16 warps' sums in warp order (deterministic) and runs the epilogue.
+//   No CTA-wide barrier per unit, so warps run ahead by up to the ring depth.
+// * Fused decode glue (epq_decode_linear): the prologue can replace x by
+//   RMSNorm(x) (weight 1) while staging it, the epilogue can add the result
+//   into a residual stream in place (h = h + dtype(out)), and a paired launch
+//   of two stores (gate, up) can emit dtype(silu(dtype(g)) * dtype(u)) -- the
+//   Llama / Qwen3 block's rounding points, so a decode token needs five
+//   launches per layer.
+// * With programmatic dependent launch the producer starts streaming weights
+//   before the previous kernel (which produces x) finishes.
 // * Every mbarrier wait is bounded; a wait that gives up sets a device error
 //   flag (read by epq_device_error) and the kernel runs to completion.
 #include <climits>
 
 #include "epq_common.cuh"
+#include "epq_decode.h"
+#include "epq_sm100.cuh"
 
 namespace epq {
 namespace {
@@ -48,20 +69,20 @@ constexpr int kConsumerWarps = 16;
 constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kThreads = kConsumers + 32;       // + one producer warp
 constexpr int kStages = 4;
+constexpr int kSlots = kStages + 1;             // unit reduction slots (see the ring argument below)
 constexpr int kChunkGroups = 32;                // groups per chunk
 constexpr int kStageIdx = kChunkGroups * 512;   // 16 KB of index tiles
 constexpr int kStageBytes = kStageIdx + kChunkGroups * 64;
-constexpr int kReplicaBytes = 256 * 16 * 8;     // 256 entries x 16 copies x 8 B
-constexpr int kRedFloats = kConsumerWarps * 16 * 16;   // [warp][16 rows][16 m]
-constexpr int kBarOffset = kReplicaBytes + 2 * kRedFloats * 4;
-constexpr int kStageOffset = kBarOffset + 128;
-constexpr int kFixedSmem = kStageOffset + kStages * kStageBytes;
+constexpr int kReplicaBytes = 256 * 32 * 8;     // 256 entries x 32 copies x 8 B
+constexpr int kBarBytes = 256;                  // mbarriers + slot counters
 constexpr int kMaxXSmem = 64 * 1024;            // activations staged in shared memory up to this
+constexpr int kMaxSmem = 227 * 1024;
 constexpr uint32_t kWaitLimit = 1u << 22;       // bounded mbarrier waits
 
 __device__ int g_mma_wait_timeout = 0;
 
 struct MmaStore {
+    CUtensorMap smap;     // the scales as a [groups][rows] tensor, box {16 rows, 32 groups}
     const uint8_t* idx;   // EPQ_LAYOUT_MMA16
     const void* scale;    // group-major: scale(r, g) at g * s_g + r; s_g % 16 == 0
     int64_t s_g;
@@ -79,6 +100,11 @@ struct MmaParams {
     int64_t ldx;
     int count, m, k, kpad, out_dtype;
     int total_units, chunks_per_unit;
+    int parts;            // 2: each unit is the same block of stores 0 and 1 (SiLU pair), else 1
+    int prologue, epilogue;
+    float eps;
+    int slot_floats;      // floats of one reduction slot: parts * warps * 16 rows * m
+    int x_off;            // byte offset of the staged activations
 };
 
 template <bool kBf16>
@@ -90,6 +116,15 @@ __device__ __forceinline__ uint32_t cvt_pair(float a, float b) {
         __half2 v = __floats2half2_rn(a, b);
         return *reinterpret_cast<uint32_t*>(&v);
     }
+}
+
+// Packed multiply with one rounding of the exact product (torch's bf16 / fp16 mul).
+template <bool kBf16>
+__device__ __forceinline__ uint32_t mul2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    if constexpr (kBf16) asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    else asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
 }
 
 template <bool kBf16>
@@ -131,6 +166,18 @@ __device__ __forceinline__ float lds_scale(uint32_t addr) {
         asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h) : "r"(addr));
         return __half2float(__ushort_as_half(h));
     }
+}
+
+// Activation type helpers on 16-bit raw values.
+template <bool kBf16>
+__device__ __forceinline__ float act_to_f(uint32_t raw16) {
+    if constexpr (kBf16) return __uint_as_float(raw16 << 16);
+    else return __half2float(__ushort_as_half((unsigned short)raw16));
+}
+template <bool kBf16>
+__device__ __forceinline__ uint32_t f_to_act(float v) {
+    if constexpr (kBf16) return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v));
+    else return (uint32_t)__half_as_ushort(__float2half_rn(v));
 }
 
 // --- mbarrier / bulk copy -----------------------------------------------------
@@ -175,18 +222,100 @@ __device__ __forceinline__ void pdl_trigger() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
-// Codebook of store S -> 16 interleaved copies in the activation type (consumer threads).
+// Codebook of store S -> 32 interleaved copies in the activation type: entry e,
+// copy c at byte e * 256 + c * 8.  Consumer thread t converts entry t / 2 once
+// and writes 16 of its copies.
 template <bool kBf16>
 __device__ void build_replica(const MmaStore& S, uint2* rep) {
-    for (int slot = threadIdx.x; slot < 256 * 16; slot += kConsumers) {
-        const int e = slot >> 4;
-        uint2 v = make_uint2(0u, 0u);
-        if (e < S.levels) {
-            const int64_t b = (int64_t)e * 4;
-            v.x = cvt_pair<kBf16>(load_f(S.cb, S.cb_dtype, b), load_f(S.cb, S.cb_dtype, b + 1));
-            v.y = cvt_pair<kBf16>(load_f(S.cb, S.cb_dtype, b + 2), load_f(S.cb, S.cb_dtype, b + 3));
+    static_assert(kConsumers == 2 * 256, "two consumer threads per codebook entry");
+    const int e = threadIdx.x >> 1, c0 = (threadIdx.x & 1) * 16;
+    uint2 v = make_uint2(0u, 0u);
+    if (e < S.levels) {
+        const int64_t b = (int64_t)e * 4;
+        v.x = cvt_pair<kBf16>(load_f(S.cb, S.cb_dtype, b), load_f(S.cb, S.cb_dtype, b + 1));
+        v.y = cvt_pair<kBf16>(load_f(S.cb, S.cb_dtype, b + 2), load_f(S.cb, S.cb_dtype, b + 3));
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) rep[e * 32 + c0 + i] = v;
+}
+
+// kT (1 or 2) tiles of one chunk, interleaved so their gathers and MMAs overlap:
+// tile t is group gl0 + 16 t of the chunk (one 16-row block x 128 weights), its
+// products go to accumulator chain t.  Lanes whose activation row is past m
+// load no activations (their B columns are never stored).
+template <bool kBf16, int kNT, bool kScaleF32, bool kXSmem, int kT>
+__device__ __forceinline__ void mma_tiles(float (&acc)[2][kNT][4], const uint32_t sdst, const int gl0, const int g0,
+                                          const uint32_t rep_l, const uint32_t xs0, const uint32_t xs1,
+                                          const uint16_t* xg0, const uint16_t* xg1, const int k_lane,
+                                          const bool xon0, const bool xon1, const int lane) {
+    constexpr int kScaleBytes = kScaleF32 ? 4 : 2;
+    const int gq = lane >> 2;
+    uint32_t wlo[kT][2], whi[kT][2], sc0[kT], sc1[kT];
+#pragma unroll
+    for (int t = 0; t < kT; ++t) {
+        const int gl = gl0 + 16 * t;
+        const uint4 w = lds128(sdst + gl * 512 + lane * 16);
+        wlo[t][0] = w.x;
+        wlo[t][1] = w.y;
+        whi[t][0] = w.z;
+        whi[t][1] = w.w;
+        // The rows' scales rounded to the activation type, twice per register.
+        const float s0 = lds_scale<kScaleF32>(sdst + kStageIdx + (gl * 16 + gq) * kScaleBytes);
+        const float s1 = lds_scale<kScaleF32>(sdst + kStageIdx + (gl * 16 + gq + 8) * kScaleBytes);
+        sc0[t] = cvt_pair<kBf16>(s0, s0);
+        sc1[t] = cvt_pair<kBf16>(s1, s1);
+    }
+    const uint32_t lanebase = (uint32_t)lane << 3;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+        uint4 bx[kT], by[kT];
+#pragma unroll
+        for (int t = 0; t < kT; ++t) {
+            const int gidx = g0 + gl0 + 16 * t;
+            bx[t] = by[t] = make_uint4(0u, 0u, 0u, 0u);
+            if constexpr (kXSmem) {
+                if (xon0) bx[t] = lds128(xs0 + (gidx * 4 + p) * 64);
+                if constexpr (kNT == 2)
+                    if (xon1) by[t] = lds128(xs1 + (gidx * 4 + p) * 64);
+            } else {
+                const int col = gidx * 128 + 32 * p;
+                if (xon0) {
+                    const uint2 z = make_uint2(0u, 0u);
+                    const uint2 b0 = col < k_lane ? __ldg(reinterpret_cast<const uint2*>(xg0 + col)) : z;
+                    const uint2 b1 = col + 16 < k_lane ? __ldg(reinterpret_cast<const uint2*>(xg0 + col + 16)) : z;
+                    bx[t] = make_uint4(b0.x, b0.y, b1.x, b1.y);
+                }
+                if constexpr (kNT == 2) {
+                    if (xon1) {
+                        const uint2 z = make_uint2(0u, 0u);
+                        const uint2 c0 = col < k_lane ? __ldg(reinterpret_cast<const uint2*>(xg1 + col)) : z;
+                        const uint2 c1 =
+                            col + 16 < k_lane ? __ldg(reinterpret_cast<const uint2*>(xg1 + col + 16)) : z;
+                        by[t] = make_uint4(c0.x, c0.y, c1.x, c1.y);
+                    }
+                }
+            }
         }
-        rep[slot] = v;
+#pragma unroll
+        for (int hs = 0; hs < 2; ++hs) {
+            const int s = 2 * p + hs;
+            // result byte 0 = lane * 8, byte 1 = index byte s % 4, bytes 2-3 = 0
+            const uint32_t sel = 0x5504u | ((uint32_t)(s & 3) << 4);
+            uint2 alo[kT], ahi[kT];
+#pragma unroll
+            for (int t = 0; t < kT; ++t) {
+                alo[t] = lds64(rep_l + __byte_perm(wlo[t][s >> 2], lanebase, sel));
+                ahi[t] = lds64(rep_l + __byte_perm(whi[t][s >> 2], lanebase, sel));
+            }
+#pragma unroll
+            for (int t = 0; t < kT; ++t) {
+                const uint32_t a0 = mul2<kBf16>(alo[t].x, sc0[t]), a2 = mul2<kBf16>(alo[t].y, sc0[t]);
+                const uint32_t a1 = mul2<kBf16>(ahi[t].x, sc1[t]), a3 = mul2<kBf16>(ahi[t].y, sc1[t]);
+                mma16816<kBf16>(acc[t][0], a0, a1, a2, a3, hs ? bx[t].z : bx[t].x, hs ? bx[t].w : bx[t].y);
+                if constexpr (kNT == 2)
+                    mma16816<kBf16>(acc[t][1], a0, a1, a2, a3, hs ? by[t].z : by[t].x, hs ? by[t].w : by[t].y);
+            }
+        }
     }
 }
 
@@ -196,16 +325,26 @@ __device__ __forceinline__ int store_of(const MmaParams& P, int u) {
     return si;
 }
 
+// Element offset of activation (row, col) in the staged B-fragment order: per
+// group, per pair of k-steps p (s = 2p, 2p+1), per lane column q, 8 values
+// {x[c0 .. c0+3], x[c0+16 .. c0+19]} with c0 = 128 g + 32 p + 4 q.
+__device__ __forceinline__ int xperm(int row, int kpad, int col) {
+    const int g = col >> 7, s = (col >> 4) & 7, q = (col >> 2) & 3, j = col & 3;
+    return row * kpad + (((g * 4 + (s >> 1)) * 4 + q) << 3) + ((s & 1) << 2) + j;
+}
+
 template <bool kBf16, int kNT, bool kScaleF32, bool kXSmem>
 __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const __grid_constant__ MmaParams P) {
     extern __shared__ __align__(128) uint8_t smem[];
+    const int rep_bytes = P.parts * kReplicaBytes;
     uint2* rep = reinterpret_cast<uint2*>(smem);
-    float* red = reinterpret_cast<float*>(smem + kReplicaBytes);   // [2][warp][16 rows][16 m]
     const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
-    const uint32_t bar_full = sbase + kBarOffset;          // kStages x 8 B
+    const uint32_t bar_full = sbase + rep_bytes;           // kStages x 8 B
     const uint32_t bar_empty = bar_full + 8 * kStages;     // kStages x 8 B
-    const uint32_t stage0 = sbase + kStageOffset;
-    uint16_t* xs = reinterpret_cast<uint16_t*>(smem + kFixedSmem);   // [m][kpad] when kXSmem
+    int* cnt = reinterpret_cast<int*>(smem + rep_bytes + 16 * kStages);   // kSlots arrival counters
+    const uint32_t stage0 = sbase + rep_bytes + kBarBytes;
+    float* slots = reinterpret_cast<float*>(smem + rep_bytes + kBarBytes + kStages * kStageBytes);
+    uint16_t* xs = reinterpret_cast<uint16_t*>(smem + P.x_off);   // [m][kpad] when kXSmem
     constexpr int kScaleBytes = kScaleF32 ? 4 : 2;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -215,7 +354,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const __grid_cons
     const int u_begin = (int)((int64_t)U * blockIdx.x / G);
     const int u_end = (int)((int64_t)U * (blockIdx.x + 1) / G);
     const int cpu = P.chunks_per_unit;
-    const int n_chunks = (u_end - u_begin) * cpu;
+    const int n_chunks = (u_end - u_begin) * cpu * P.parts;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -224,38 +363,47 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const __grid_cons
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
+    if (threadIdx.x < kSlots) cnt[threadIdx.x] = 0;
     __syncthreads();
 
     if (warp == kConsumerWarps) {
         // ---------------- producer: stream chunks into the ring ----------------
-        int si = store_of(P, u_begin);
-        int s_next = si + 1 < P.count ? P.st[si + 1].unit0 : INT_MAX;
-        int u = u_begin, c = 0;
+        int si = P.parts == 2 ? 0 : store_of(P, u_begin);
+        int s_next = (P.parts == 1 && si + 1 < P.count) ? P.st[si + 1].unit0 : INT_MAX;
+        int u = u_begin, part = 0, c = 0;
         for (int i = 0; i < n_chunks; ++i) {
             const int stage = i % kStages;
             if (i >= kStages) mbar_wait(bar_empty + 8 * stage, ((i / kStages) - 1) & 1);
-            if (u >= s_next) {
-                si = store_of(P, u);
-                s_next = si + 1 < P.count ? P.st[si + 1].unit0 : INT_MAX;
+            int rb;
+            if (P.parts == 2) {
+                si = part;
+                rb = u;
+            } else {
+                if (u >= s_next) {
+                    si = store_of(P, u);
+                    s_next = si + 1 < P.count ? P.st[si + 1].unit0 : INT_MAX;
+                }
+                rb = u - P.st[si].unit0;
             }
             const MmaStore& S = P.st[si];
-            const int rb = u - S.unit0;
             const int g0 = c * kChunkGroups;
             const int ngc = min(kChunkGroups, S.ng - g0);
             const uint32_t dst = stage0 + stage * kStageBytes;
-            const uint32_t sb = 16 * kScaleBytes;   // one group's 16 scales
-            if (lane == 0) mbar_expect_tx(bar_full + 8 * stage, ngc * (512 + sb));
-            __syncwarp();
-            if (lane == 0)
+            // Two copies per chunk: the index tiles (one contiguous run) and the
+            // scales of its 16 rows x 32 groups (one 2-D tensor box; groups past
+            // the store's last are zero-filled, and the full box is counted).
+            if (lane == 0) {
+                mbar_expect_tx(bar_full + 8 * stage, ngc * 512 + kChunkGroups * 16 * kScaleBytes);
                 bulk_g2s(dst, S.idx + ((int64_t)rb * S.ng + g0) * 512, ngc * 512, bar_full + 8 * stage);
-            if (lane < ngc) {
-                const char* src = static_cast<const char*>(S.scale) +
-                                  ((int64_t)(g0 + lane) * S.s_g + (int64_t)rb * 16) * kScaleBytes;
-                bulk_g2s(dst + kStageIdx + lane * 64, src, sb, bar_full + 8 * stage);
+                sm100::tma_load_2d(dst + kStageIdx, &S.smap, bar_full + 8 * stage, rb * 16, g0);
             }
+            __syncwarp();
             if (++c == cpu) {
                 c = 0;
-                ++u;
+                if (++part == P.parts) {
+                    part = 0;
+                    ++u;
+                }
             }
         }
         pdl_trigger();
@@ -264,11 +412,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const __grid_cons
 
     // ---------------- consumers ----------------
     const int gq = lane >> 2, q = lane & 3;
-    int cur = store_of(P, u_begin);
-    int c_next = cur + 1 < P.count ? P.st[cur + 1].unit0 : INT_MAX;
+    int cur = P.parts == 2 ? 0 : store_of(P, u_begin);
+    int c_next = (P.parts == 1 && cur + 1 < P.count) ? P.st[cur + 1].unit0 : INT_MAX;
     if (u_begin < u_end) {
-        if constexpr (kBf16) build_replica<true>(P.st[cur], rep);
-        else build_replica<false>(P.st[cur], rep);
+        for (int r = 0; r < P.parts; ++r) {
+            if constexpr (kBf16) build_replica<true>(P.st[P.parts == 2 ? r : cur], rep + r * (256 * 32));
+            else build_replica<false>(P.st[P.parts == 2 ? r : cur], rep + r * (256 * 32));
+        }
     }
     pdl_trigger();
     pdl_wait();   // x (and the output buffers) belong to the previous kernel until here
@@ -281,32 +431,68 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const __grid_cons
     const uint16_t* xg1 = static_cast<const uint16_t*>(P.x) + (int64_t)xr1 * P.ldx + 4 * q;
     uint32_t xs0 = 0, xs1 = 0;
     if constexpr (kXSmem) {
+        // Stage x (or RMSNorm(x)) in the permuted B-fragment order.
         const int per_row = P.kpad >> 2;
-        const int chunks = P.m * per_row;
-        for (int i = threadIdx.x; i < chunks; i += kConsumers) {
-            const int row = i / per_row, c4 = (i - row * per_row) * 4;
-            uint2 v = make_uint2(0u, 0u);
-            if (c4 < P.k)
-                v = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(P.x) + (int64_t)row * P.ldx + c4);
-            *reinterpret_cast<uint2*>(xs + row * P.kpad + c4) = v;
+        const bool norm = P.prologue == EPQ_PRO_RMSNORM;
+        for (int row = 0; row < P.m; ++row) {
+            float ss = 0.f;
+            for (int i = threadIdx.x; i < per_row; i += kConsumers) {
+                const int c4 = i * 4;
+                uint2 v = make_uint2(0u, 0u);
+                if (c4 < P.k)
+                    v = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(P.x) +
+                                                        (int64_t)row * P.ldx + c4);
+                if (norm) {
+                    const float a = act_to_f<kBf16>(v.x & 0xffffu), b = act_to_f<kBf16>(v.x >> 16);
+                    const float c = act_to_f<kBf16>(v.y & 0xffffu), d = act_to_f<kBf16>(v.y >> 16);
+                    ss += a * a + b * b + c * c + d * d;
+                }
+                *reinterpret_cast<uint2*>(xs + xperm(row, P.kpad, c4)) = v;
+            }
+            if (norm) {
+                for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+                if (lane == 0) slots[row * kConsumerWarps + warp] = ss;   // slots are free until the first unit ends
+            }
+        }
+        if (norm) {
+            consumers_sync();
+            for (int row = 0; row < P.m; ++row) {
+                float ss = 0.f;
+#pragma unroll
+                for (int w = 0; w < kConsumerWarps; ++w) ss += slots[row * kConsumerWarps + w];
+                const float r = rsqrtf(ss / (float)P.k + P.eps);
+                for (int i = threadIdx.x; i < per_row; i += kConsumers) {
+                    uint2* p = reinterpret_cast<uint2*>(xs + xperm(row, P.kpad, i * 4));
+                    const uint2 v = *p;
+                    uint2 y;
+                    y.x = f_to_act<kBf16>(act_to_f<kBf16>(v.x & 0xffffu) * r) |
+                          (f_to_act<kBf16>(act_to_f<kBf16>(v.x >> 16) * r) << 16);
+                    y.y = f_to_act<kBf16>(act_to_f<kBf16>(v.y & 0xffffu) * r) |
+                          (f_to_act<kBf16>(act_to_f<kBf16>(v.y >> 16) * r) << 16);
+                    *p = y;
+                }
+            }
         }
         const uint32_t xsb = static_cast<uint32_t>(__cvta_generic_to_shared(xs));
-        xs0 = xsb + (xr0 * P.kpad + 4 * q) * 2;
-        xs1 = xsb + (xr1 * P.kpad + 4 * q) * 2;
+        xs0 = xsb + (xr0 * P.kpad + 8 * q) * 2;
+        xs1 = xsb + (xr1 * P.kpad + 8 * q) * 2;
     }
     consumers_sync();
 
-    const uint32_t rep_lane = sbase + (lane & 15) * 8;
     const int k_lane = P.k - 4 * q;   // global-load path: column c is in range iff c < k_lane
-    float acc[kNT][4];
+    const bool xon0 = gq < P.m, xon1 = gq + 8 < P.m;
+    // Two accumulator chains (the two tiles a warp takes per chunk) keep dependent MMAs apart.
+    float acc[2][kNT][4];
 #pragma unroll
-    for (int h = 0; h < kNT; ++h) acc[h][0] = acc[h][1] = acc[h][2] = acc[h][3] = 0.f;
-    int parity = 0;
-    int u = u_begin, c = 0;
+    for (int e = 0; e < 2; ++e)
+#pragma unroll
+        for (int h = 0; h < kNT; ++h) acc[e][h][0] = acc[e][h][1] = acc[e][h][2] = acc[e][h][3] = 0.f;
+    int u = u_begin, part = 0, c = 0, uslot = 0;
     for (int i = 0; i < n_chunks; ++i) {
         const int stage = i % kStages;
-        if (c == 0 && u >= c_next) {
-            // New store (CTA-uniform): rebuild the codebook replica.
+        if (P.parts == 1 && c == 0 && u >= c_next) {
+            // New store (CTA-uniform): rebuild the codebook replica once every warp
+            // is past the previous store's gathers.
             consumers_sync();
             cur = store_of(P, u);
             c_next = cur + 1 < P.count ? P.st[cur + 1].unit0 : INT_MAX;
@@ -314,99 +500,93 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const __grid_cons
             else build_replica<false>(P.st[cur], rep);
             consumers_sync();
         }
-        const int ng = P.st[cur].ng;
+        const int sidx = P.parts == 2 ? part : cur;
+        const int ng = P.st[sidx].ng;
+        const uint32_t rep_l = sbase + (P.parts == 2 ? part * kReplicaBytes : 0);
         const int g0 = c * kChunkGroups;
         const int ngc = min(kChunkGroups, ng - g0);
         mbar_wait(bar_full + 8 * stage, (i / kStages) & 1);
         const uint32_t sdst = stage0 + stage * kStageBytes;
-#pragma unroll
-        for (int t = 0; t < 2; ++t) {
-            const int gl = warp + kConsumerWarps * t;   // group within the chunk
-            if (gl < ngc) {
-                const uint4 w = lds128(sdst + gl * 512 + lane * 16);
-                const float s0 = lds_scale<kScaleF32>(sdst + kStageIdx + gl * 64 + gq * kScaleBytes);
-                const float s1 = lds_scale<kScaleF32>(sdst + kStageIdx + gl * 64 + (gq + 8) * kScaleBytes);
-                float d[2][kNT][4];
-#pragma unroll
-                for (int e = 0; e < 2; ++e)
-#pragma unroll
-                    for (int h = 0; h < kNT; ++h) d[e][h][0] = d[e][h][1] = d[e][h][2] = d[e][h][3] = 0.f;
-                const int cbase = (g0 + gl) * 128;
-                const uint32_t wlo[2] = {w.x, w.y}, whi[2] = {w.z, w.w};
-#pragma unroll
-                for (int s = 0; s < 8; ++s) {
-                    const int col = cbase + 16 * s;
-                    const uint32_t sel = 0x4440u | (s & 3);
-                    const uint32_t elo = __byte_perm(wlo[s >> 2], 0u, sel);
-                    const uint32_t ehi = __byte_perm(whi[s >> 2], 0u, sel);
-                    const uint2 alo = lds64(rep_lane + elo * 128u);
-                    const uint2 ahi = lds64(rep_lane + ehi * 128u);
-                    uint2 bx, by;
-                    if constexpr (kXSmem) {
-                        bx = lds64(xs0 + col * 2);
-                        if constexpr (kNT == 2) by = lds64(xs1 + col * 2);
-                    } else {
-                        bx = col < k_lane ? __ldg(reinterpret_cast<const uint2*>(xg0 + col)) : make_uint2(0u, 0u);
-                        if constexpr (kNT == 2)
-                            by = col < k_lane ? __ldg(reinterpret_cast<const uint2*>(xg1 + col)) : make_uint2(0u, 0u);
-                    }
-                    mma16816<kBf16>(d[s & 1][0], alo.x, ahi.x, alo.y, ahi.y, bx.x, bx.y);
-                    if constexpr (kNT == 2) mma16816<kBf16>(d[s & 1][1], alo.x, ahi.x, alo.y, ahi.y, by.x, by.y);
-                }
-#pragma unroll
-                for (int h = 0; h < kNT; ++h) {
-                    acc[h][0] = fmaf(d[0][h][0] + d[1][h][0], s0, acc[h][0]);
-                    acc[h][1] = fmaf(d[0][h][1] + d[1][h][1], s0, acc[h][1]);
-                    acc[h][2] = fmaf(d[0][h][2] + d[1][h][2], s1, acc[h][2]);
-                    acc[h][3] = fmaf(d[0][h][3] + d[1][h][3], s1, acc[h][3]);
-                }
-            }
-        }
+        if (warp + kConsumerWarps < ngc)
+            mma_tiles<kBf16, kNT, kScaleF32, kXSmem, 2>(acc, sdst, warp, g0, rep_l, xs0, xs1, xg0, xg1, k_lane,
+                                                        xon0, xon1, lane);
+        else if (warp < ngc)
+            mma_tiles<kBf16, kNT, kScaleF32, kXSmem, 1>(acc, sdst, warp, g0, rep_l, xs0, xs1, xg0, xg1, k_lane,
+                                                        xon0, xon1, lane);
         __syncwarp();
         if (lane == 0) mbar_arrive(bar_empty + 8 * stage);   // this warp is done with the stage
-        if (++c == cpu) {
-            // End of a 16-row block: add the warps' sums in warp order, write 16 rows.
-            const MmaStore& S = P.st[cur];
-            float* rb_buf = red + parity * kRedFloats;
-            float* mine = rb_buf + warp * 256;     // [16 rows][16 m]
+        if (++c < cpu) continue;
+        c = 0;
+        // End of one part of a unit: this warp's partial sums into the unit's slot,
+        // laid out [part][warp][m][16 rows].
+        {
+            float* mine = slots + uslot * P.slot_floats + (part * kConsumerWarps + warp) * 16 * P.m;
 #pragma unroll
             for (int h = 0; h < kNT; ++h) {
                 const int m0 = 8 * h + 2 * q;
-                mine[gq * 16 + m0] = acc[h][0];
-                mine[gq * 16 + m0 + 1] = acc[h][1];
-                mine[(gq + 8) * 16 + m0] = acc[h][2];
-                mine[(gq + 8) * 16 + m0 + 1] = acc[h][3];
-                acc[h][0] = acc[h][1] = acc[h][2] = acc[h][3] = 0.f;
-            }
-            consumers_sync();
-            if (threadIdx.x < 256) {
-                const int mm = threadIdx.x >> 4, rr = threadIdx.x & 15;   // 16 x 16
-                const int row = (u - S.unit0) * 16 + rr;
-                if (mm < P.m && row < S.n) {
-                    float sum = 0.f;
+                if (m0 < P.m) {
+                    mine[m0 * 16 + gq] = acc[0][h][0] + acc[1][h][0];
+                    mine[m0 * 16 + gq + 8] = acc[0][h][2] + acc[1][h][2];
+                }
+                if (m0 + 1 < P.m) {
+                    mine[(m0 + 1) * 16 + gq] = acc[0][h][1] + acc[1][h][1];
+                    mine[(m0 + 1) * 16 + gq + 8] = acc[0][h][3] + acc[1][h][3];
+                }
 #pragma unroll
-                    for (int ww = 0; ww < kConsumerWarps; ++ww) sum += rb_buf[ww * 256 + rr * 16 + mm];
-                    store_f(S.out, P.out_dtype, mm * S.ldo + row, sum);
+                for (int e = 0; e < 2; ++e) acc[e][h][0] = acc[e][h][1] = acc[e][h][2] = acc[e][h][3] = 0.f;
+            }
+        }
+        if (++part < P.parts) continue;
+        part = 0;
+        // Count this warp in; the 16th warp to arrive reduces the unit.  A slot is
+        // reused kSlots units later: by then its reducer is done, because a warp
+        // can run at most kStages chunks (>= units) ahead of the slowest warp and
+        // kSlots = kStages + 1.
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) {
+            __threadfence_block();
+            last = atomicAdd(&cnt[uslot], 1) == kConsumerWarps - 1;
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+            __syncwarp();
+            __threadfence_block();
+            const int sidx0 = P.parts == 2 ? 0 : cur;
+            const MmaStore& S = P.st[sidx0];
+            const int rowbase = (P.parts == 2 ? u : u - S.unit0) * 16;
+            const float* base = slots + uslot * P.slot_floats;
+            const int per = 16 * P.m;   // floats per warp per part
+            for (int e = lane; e < per; e += 32) {
+                const int rr = e & 15, mm = e >> 4;
+                const int row = rowbase + rr;
+                float v0 = 0.f, v1 = 0.f;
+#pragma unroll
+                for (int ww = 0; ww < kConsumerWarps; ++ww) v0 += base[ww * per + e];
+                if (P.parts == 2) {
+#pragma unroll
+                    for (int ww = 0; ww < kConsumerWarps; ++ww) v1 += base[(kConsumerWarps + ww) * per + e];
+                }
+                if (row < S.n) {
+                    const int64_t o = (int64_t)mm * S.ldo + row;
+                    if (P.epilogue == EPQ_EPI_RESIDUAL) {
+                        const int dt = kBf16 ? EPQ_BF16 : EPQ_F16;
+                        store_f(S.out, dt, o, load_f(S.out, dt, o) + round_to(v0, dt));
+                    } else if (P.epilogue == EPQ_EPI_SILU_MUL) {
+                        const int dt = kBf16 ? EPQ_BF16 : EPQ_F16;
+                        const float gv = round_to(v0, dt), uv = round_to(v1, dt);
+                        store_f(S.out, dt, o, gv / (1.f + expf(-gv)) * uv);
+                    } else {
+                        store_f(S.out, P.out_dtype, o, v0);
+                    }
                 }
             }
-            parity ^= 1;
-            c = 0;
-            ++u;
+            __syncwarp();
+            if (lane == 0) cnt[uslot] = 0;
         }
+        ++u;
+        if (++uslot == kSlots) uslot = 0;
     }
-}
-
-int g_sms[64] = {0};
-bool g_attr[16][64] = {{false}};
-
-int sm_count(int dev) {
-    if (g_sms[dev] == 0) {
-        int v = 0;
-        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0)
-            v = 148;
-        g_sms[dev] = v;
-    }
-    return g_sms[dev];
 }
 
 }  // namespace
@@ -428,23 +608,35 @@ bool mma_eligible(const StoreD& s, int64_t m, int x_dtype) {
            s.k > 0 && s.k < (1 << 30);
 }
 
-int launch_linear_mma(const StoreD* s, int count, const void* x, int x_dtype, int64_t m, int64_t ldx,
-                      void* const* outs, const int64_t* ldo, int out_dtype, cudaStream_t st) {
+int launch_linear_mma_fused(const StoreD* s, int count, const void* x, int x_dtype, int64_t m, int64_t ldx,
+                            void* const* outs, const int64_t* ldo, int out_dtype, int prologue, int epilogue,
+                            float eps, cudaStream_t st) {
     if ((reinterpret_cast<uintptr_t>(x) & 7) || (ldx & 3))
         return set_error(EPQ_EALIGN, "linear: x must be 8-byte aligned with ldx a multiple of 4");
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64) return set_error(EPQ_EUNSUPPORTED, "device ordinal %d", dev);
     const bool bf = x_dtype == EPQ_BF16;
     const int nt = m > 8 ? 2 : 1;
     const bool sf32 = s[0].scale_dtype == EPQ_F32;
     for (int i = 1; i < count; ++i)
         if ((s[i].scale_dtype == EPQ_F32) != sf32)
             return set_error(EPQ_EDTYPE, "linear: fused stores need one scale dtype");
+    const int parts = epilogue == EPQ_EPI_SILU_MUL ? 2 : 1;
+    if (parts == 2 && (count != 2 || s[0].n != s[1].n))
+        return set_error(EPQ_ESHAPE, "decode linear: the SiLU epilogue takes two stores of equal rows");
+    if (epilogue == EPQ_EPI_RESIDUAL && count != 1)
+        return set_error(EPQ_ESHAPE, "decode linear: the residual epilogue takes one store");
+    if (epilogue != EPQ_EPI_STORE && out_dtype != x_dtype)
+        return set_error(EPQ_EDTYPE, "decode linear: fused epilogues write the activation dtype");
     const int64_t kpad = s[0].ng * 128;
     const int64_t xbytes = m * kpad * 2;
-    const bool xsm = xbytes <= kMaxXSmem;
-    const int smem = kFixedSmem + (xsm ? (int)xbytes : 0);
+    const int slot_floats = parts * kConsumerWarps * 16 * (int)m;
+    const int fixed = parts * kReplicaBytes + kBarBytes + kStages * kStageBytes + kSlots * slot_floats * 4;
+    const bool xsm = xbytes <= kMaxXSmem && fixed + xbytes <= kMaxSmem;
+    if (prologue == EPQ_PRO_RMSNORM && !xsm)
+        return set_error(EPQ_EUNSUPPORTED, "decode linear: RMSNorm prologue needs m*k*2 <= %d bytes", kMaxXSmem);
+    if (fixed > kMaxSmem)
+        return set_error(EPQ_EUNSUPPORTED, "decode linear: m=%lld needs %d bytes of shared memory", (long long)m,
+                         fixed);
+    const int smem = fixed + (xsm ? (int)xbytes : 0);
     const int variant = (bf ? 1 : 0) + (nt == 2 ? 2 : 0) + (sf32 ? 4 : 0) + (xsm ? 8 : 0);
     using KernT = void (*)(MmaParams);
     static const KernT kernels[16] = {
@@ -457,11 +649,10 @@ int launch_linear_mma(const StoreD* s, int count, const void* x, int x_dtype, in
         gemv_mma_kernel<false, 1, true, true>,   gemv_mma_kernel<true, 1, true, true>,
         gemv_mma_kernel<false, 2, true, true>,   gemv_mma_kernel<true, 2, true, true>};
     const KernT kern = kernels[variant];
-    if (!g_attr[variant][dev]) {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 kFixedSmem + kMaxXSmem) != cudaSuccess)
-            return check_launch("cudaFuncSetAttribute(gemv_mma_kernel)");
-        g_attr[variant][dev] = true;
+    {
+        const int arc = set_smem_limit(reinterpret_cast<const void*>(kern), kMaxSmem,
+                                       "cudaFuncSetAttribute(gemv_mma_kernel)");
+        if (arc != EPQ_OK) return arc;
     }
     MmaParams P{};
     P.count = count;
@@ -472,9 +663,19 @@ int launch_linear_mma(const StoreD* s, int count, const void* x, int x_dtype, in
     P.kpad = (int)kpad;
     P.out_dtype = out_dtype;
     P.chunks_per_unit = (int)cdiv(s[0].ng, kChunkGroups);
+    P.parts = parts;
+    P.prologue = prologue;
+    P.epilogue = epilogue;
+    P.eps = eps;
+    P.slot_floats = slot_floats;
+    P.x_off = fixed;
     int64_t units = 0;
     for (int i = 0; i < count; ++i) {
         MmaStore& S = P.st[i];
+        const int esz = s[i].scale_dtype == EPQ_F32 ? 4 : 2;
+        const int trc = make_tmap_2d_plain(&S.smap, s[i].scale, esz, s[i].rb * 16, s[i].ng, s[i].s_g, 16,
+                                           kChunkGroups, "linear");
+        if (trc != EPQ_OK) return trc;
         S.idx = s[i].idx;
         S.scale = s[i].scale;
         S.s_g = s[i].s_g;
@@ -486,12 +687,13 @@ int launch_linear_mma(const StoreD* s, int count, const void* x, int x_dtype, in
         S.n = (int)s[i].n;
         S.ng = (int)s[i].ng;
         S.rb = (int)s[i].rb;
-        S.unit0 = (int)units;
+        S.unit0 = parts == 2 ? 0 : (int)units;
         units += S.rb;
     }
+    if (parts == 2) units = s[0].rb;
     if (units >= (int64_t(1) << 30)) return set_error(EPQ_EUNSUPPORTED, "linear: too many rows");
     P.total_units = (int)units;
-    int grid = sm_count(dev);
+    int grid = device_sms();
     if (grid > units) grid = (int)units;
 
     cudaLaunchConfig_t cfg = {};
@@ -508,4 +710,41 @@ int launch_linear_mma(const StoreD* s, int count, const void* x, int x_dtype, in
     return check_launch("gemv_mma_kernel");
 }
 
+int launch_linear_mma(const StoreD* s, int count, const void* x, int x_dtype, int64_t m, int64_t ldx,
+                      void* const* outs, const int64_t* ldo, int out_dtype, cudaStream_t st) {
+    return launch_linear_mma_fused(s, count, x, x_dtype, m, ldx, outs, ldo, out_dtype, EPQ_PRO_NONE,
+                                   EPQ_EPI_STORE, 0.f, st);
+}
+
 }  // namespace epq
+
+using namespace epq;
+
+extern "C" int epq_decode_linear(const epq_store* stores, int32_t count, const void* x, int32_t x_dtype,
+                                 int64_t m, int64_t ldx, int32_t prologue, float eps, void* const* outs,
+                                 const int64_t* ldo, int32_t epilogue, void* stream) {
+    if (!stores || !x || !outs || count < 1 || count > kLutMaxStores || m < 1 || m > 16)
+        return set_error(EPQ_EINVAL, "epq_decode_linear: bad arguments");
+    if (prologue != EPQ_PRO_NONE && prologue != EPQ_PRO_RMSNORM)
+        return set_error(EPQ_EINVAL, "epq_decode_linear: prologue=%d", prologue);
+    if (epilogue != EPQ_EPI_STORE && epilogue != EPQ_EPI_RESIDUAL && epilogue != EPQ_EPI_SILU_MUL)
+        return set_error(EPQ_EINVAL, "epq_decode_linear: epilogue=%d", epilogue);
+    if (x_dtype != EPQ_BF16 && x_dtype != EPQ_F16)
+        return set_error(EPQ_EDTYPE, "epq_decode_linear: activations must be bf16 or f16");
+    StoreD s[kLutMaxStores];
+    for (int i = 0; i < count; ++i) {
+        const int rc = make_store(&stores[i], &s[i], "epq_decode_linear");
+        if (rc != EPQ_OK) return rc;
+        if (!mma_eligible(s[i], m, x_dtype))
+            return set_error(EPQ_ELAYOUT,
+                             "epq_decode_linear: store %d is not an EPQ_LAYOUT_MMA16 vec-4 group-128 store "
+                             "with group-major f16/f32 scales",
+                             i);
+        if (s[i].k != s[0].k) return set_error(EPQ_ESHAPE, "epq_decode_linear: stores differ in k");
+        if (!outs[i]) return set_error(EPQ_EINVAL, "epq_decode_linear: output %d is NULL", i);
+        if (ldo && ldo[i] < s[i].n) return set_error(EPQ_ESHAPE, "epq_decode_linear: ldo[%d] < n", i);
+    }
+    if (ldx < s[0].k) return set_error(EPQ_ESHAPE, "epq_decode_linear: ldx < k");
+    return launch_linear_mma_fused(s, count, x, x_dtype, m, ldx, outs, ldo, x_dtype, prologue, epilogue, eps,
+                                   static_cast<cudaStream_t>(stream));
+}

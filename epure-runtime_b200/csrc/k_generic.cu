@@ -212,7 +212,8 @@ __global__ void embedding_kernel(StoreD s, const int64_t* __restrict__ ids, int6
     for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
          t += (int64_t)gridDim.x * blockDim.x) {
         const int64_t i = t / s.k, c = t - i * s.k;
-        const int64_t r = ids[i];
+        int64_t r = ids[i];
+        if (r < 0) r += s.n;          // negative ids count from the end, as torch indexing does
         if (r < 0 || r >= s.n) {
             if (c == 0) atomicExch(&g_embed_bad, 1);
             store_f(out, out_dtype, i * ldo + c, 0.f);

@@ -22,6 +22,11 @@ LAYOUT_CODES = {"rows": LAYOUT_ROWS, "tiled": LAYOUT_TILED, "mma16": LAYOUT_MMA1
 
 _DT = {torch.float32: EPQ_F32, torch.float16: EPQ_F16, torch.bfloat16: EPQ_BF16}
 
+# EPURE_CHECK_IDS=1: range-check embedding ids on the host before the kernel
+# (one device-to-host read per call; out-of-range ids then raise IndexError as
+# torch indexing does, instead of giving zero rows and a device error flag).
+CHECK_IDS = os.environ.get("EPURE_CHECK_IDS", "0") not in ("", "0")
+
 
 class EpqStore(ctypes.Structure):
     _fields_ = [
@@ -54,7 +59,7 @@ EXPORTS = (
     "epq_chain_workspace_bytes", "epq_chain_prepare", "epq_chain_run", "epq_chain_set_tp",
     "epq_add_rmsnorm", "epq_rope_kv", "epq_attn_decode", "epq_attn_decode_workspace_bytes",
     "epq_silu_mul", "epq_argmax", "epq_argmax_workspace_bytes", "epq_attn_rope_decode",
-    "epq_embedding",
+    "epq_embedding", "epq_decode_linear",
 )
 
 _lib = None
@@ -97,16 +102,17 @@ def load_library(path=None):
         lib.epq_embedding.argtypes = [SP, P, I64, P, I64, I32, P]
         F32 = ctypes.c_float
         lib.epq_add_rmsnorm.argtypes = [P, P, P, P, I64, I64, F32, I32, P]
-        lib.epq_rope_kv.argtypes = [P, P, P, P, I64, I32, I32, I32, P, P, P, P, I32, F32, I32, P]
-        lib.epq_attn_decode.argtypes = [P, P, P, P, I32, I32, I32, F32, P, I32, P, I64, P]
+        lib.epq_rope_kv.argtypes = [P, P, P, P, I64, I32, I32, I32, P, P, P, P, I64, I32, F32, I32, P]
+        lib.epq_attn_decode.argtypes = [P, P, P, P, I64, I32, I32, I32, F32, P, I32, P, I64, P]
         lib.epq_attn_decode_workspace_bytes.restype = I64
         lib.epq_attn_decode_workspace_bytes.argtypes = [I32, I32, I32]
         lib.epq_argmax.argtypes = [P, I64, P, P, I64, P]
-        lib.epq_attn_rope_decode.argtypes = [P, P, P, P, I32, I32, I32, P, P, P, P, I32, F32, F32, P, I32, P,
-                                             I64, P]
+        lib.epq_attn_rope_decode.argtypes = [P, P, P, P, I32, I32, I32, P, P, P, P, I64, I32, F32, F32, P, I32,
+                                             P, I64, P]
         lib.epq_argmax_workspace_bytes.restype = I64
         lib.epq_argmax_workspace_bytes.argtypes = []
         lib.epq_silu_mul.argtypes = [P, P, P, I64, I32, P]
+        lib.epq_decode_linear.argtypes = [SP, I32, P, I32, I64, I64, I32, F32, P, P, I32, P]
         for name in EXPORTS:
             getattr(lib, name)          # every declared entry point must be exported
         if lib.epq_abi_version() != 1:
@@ -277,10 +283,16 @@ def embedding(store, ids, dtype):
     materialize's rounding in ``dtype``: a tensor ``[*ids.shape, in_features]``."""
     lib = load_library()
     d = describe_store(store)
-    flat = ids.reshape(-1).to(torch.int64).contiguous()
-    out = torch.empty((flat.numel(), store.in_features), dtype=dtype, device=store.packed.device)
-    _check(lib.epq_embedding(ctypes.byref(d), flat.data_ptr(), flat.numel(), out.data_ptr(), out.stride(0),
-                             dtype_code(dtype), _stream_ptr(out.device)), "epq_embedding")
+    dev = store.packed.device
+    flat = ids.reshape(-1).to(dev, torch.int64).contiguous()      # ids from another device are copied over
+    if CHECK_IDS and flat.numel():
+        n = store.out_features
+        if bool(((flat < -n) | (flat >= n)).any()):
+            raise IndexError(f"epure: embedding id out of range for {n} rows")
+    out = torch.empty((flat.numel(), store.in_features), dtype=dtype, device=dev)
+    with torch.cuda.device(dev):
+        _check(lib.epq_embedding(ctypes.byref(d), flat.data_ptr(), flat.numel(), out.data_ptr(), out.stride(0),
+                                 dtype_code(dtype), _stream_ptr(dev)), "epq_embedding")
     return out.view(*ids.shape, store.in_features)
 
 
@@ -372,7 +384,7 @@ def rope_kv(q, k, v, pos, cos, sin, k_cache, v_cache, qk_norm, eps=1e-6):
     m, H, hd = q.shape
     _check(lib.epq_rope_kv(q.data_ptr(), k.data_ptr(), v.data_ptr(), pos.data_ptr(), m, H,
                            k.shape[1], hd, cos.data_ptr(), sin.data_ptr(), k_cache.data_ptr(),
-                           v_cache.data_ptr(), int(qk_norm), eps, dtype_code(q.dtype),
+                           v_cache.data_ptr(), k_cache.shape[0], int(qk_norm), eps, dtype_code(q.dtype),
                            _stream_ptr(q.device)), "epq_rope_kv")
 
 
@@ -388,7 +400,7 @@ def attn_decode(q, k_cache, v_cache, pos, scale, ws=None):
     H, hd = q.shape[-2], q.shape[-1]
     out = torch.empty((H, hd), dtype=q.dtype, device=q.device)
     _check(lib.epq_attn_decode(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), pos.data_ptr(),
-                               H, k_cache.shape[-2], hd, scale, out.data_ptr(), dtype_code(q.dtype),
+                               k_cache.shape[0], H, k_cache.shape[-2], hd, scale, out.data_ptr(), dtype_code(q.dtype),
                                _ptr(ws), ws.numel() if ws is not None else 0,
                                _stream_ptr(q.device)), "epq_attn_decode")
     return out
@@ -401,7 +413,7 @@ def attn_rope_decode(q, k, v, pos, cos, sin, k_cache, v_cache, qk_norm, eps, sca
     out = torch.empty((H, hd), dtype=q.dtype, device=q.device)
     _check(lib.epq_attn_rope_decode(q.data_ptr(), k.data_ptr(), v.data_ptr(), pos.data_ptr(), H,
                                     k.shape[-2], hd, cos.data_ptr(), sin.data_ptr(), k_cache.data_ptr(),
-                                    v_cache.data_ptr(), int(qk_norm), eps, scale, out.data_ptr(),
+                                    v_cache.data_ptr(), k_cache.shape[0], int(qk_norm), eps, scale, out.data_ptr(),
                                     dtype_code(q.dtype), ws.data_ptr(), ws.numel(), _stream_ptr(q.device)),
            "epq_attn_rope_decode")
     return out
@@ -425,3 +437,44 @@ def silu_mul(g, u):
     _check(lib.epq_silu_mul(g.data_ptr(), u.data_ptr(), out.data_ptr(), g.numel(), dtype_code(g.dtype),
                             _stream_ptr(g.device)), "epq_silu_mul")
     return out
+
+
+PRO_NONE, PRO_RMSNORM = 0, 1
+EPI_STORE, EPI_RESIDUAL, EPI_SILU_MUL = 0, 1, 2
+
+
+def decode_linear(x, stores, prologue=PRO_NONE, epilogue=EPI_STORE, outs=None, eps=1e-6):
+    """A decode-step packed linear with the block glue fused in (epq_decode_linear).
+
+    ``x`` [m, k] bf16/f16 (m <= 16).  ``prologue=PRO_RMSNORM`` normalises x first;
+    ``epilogue=EPI_RESIDUAL`` adds the result into ``outs[0]`` (a residual stream,
+    updated in place); ``EPI_SILU_MUL`` (stores = [gate, up]) returns
+    silu(gate(x)) * up(x).  Returns the list of written outputs."""
+    lib = load_library()
+    if not x.is_cuda:
+        raise RuntimeError("epure: decode_linear needs a CUDA activation")
+    k = stores[0].in_features
+    x2 = x.reshape(-1, x.shape[-1])
+    if x2.shape[-1] != k:
+        raise RuntimeError(f"epure: activation has {x2.shape[-1]} features, store expects {k}")
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    m = x2.shape[0]
+    count = len(stores)
+    if outs is None:
+        if epilogue == EPI_RESIDUAL:
+            raise RuntimeError("epure: the residual epilogue needs the residual stream as outs[0]")
+        n_out = 1 if epilogue == EPI_SILU_MUL else count
+        outs = [torch.empty((m, s.out_features), dtype=x.dtype, device=x.device) for s in stores[:n_out]]
+    for o in outs:
+        if o.dtype != x.dtype or o.device != x.device or o.stride(-1) != 1:
+            raise RuntimeError("epure: decode_linear outputs must be contiguous rows of x's dtype and device")
+    wr = outs if len(outs) == count else outs + [outs[0]] * (count - len(outs))
+    descs = (EpqStore * count)(*[describe_store(s) for s in stores])
+    out_ptrs = (ctypes.c_void_p * count)(*[o.data_ptr() for o in wr])
+    ldo = (ctypes.c_int64 * count)(*[o.stride(0) if o.dim() == 2 else s.out_features
+                                     for o, s in zip(wr, stores)])
+    _check(lib.epq_decode_linear(descs, count, x2.data_ptr(), dtype_code(x2.dtype), m, x2.stride(0),
+                                 int(prologue), float(eps), out_ptrs, ldo, int(epilogue),
+                                 _stream_ptr(x.device)), "epq_decode_linear")
+    return outs

@@ -82,6 +82,7 @@ class PackedDecoder:
         if self.fused_glue:
             self.attn_ws = _native.attn_decode_workspace(shapes.heads, shapes.kv_heads, hd, self.device)
             self.arg_ws = _native.argmax_workspace(self.device)
+        self._fusable = all(st.layout == "mma16" for b in self.stack.blocks for st in b.values())
 
     def share_weights(self, linear_mode):
         """The same model (stores, embedding, lm_head) with another linear mode."""
@@ -117,9 +118,40 @@ class PackedDecoder:
         return (hl.float() @ self.lm_head_f32.T)[0]
 
     def _decode_fused(self, ids, pos):
-        """One token with libepq.so's decode glue (include/epq_decode.h): per layer the
-        packed q/k/v launch, RoPE + KV write + attention (one launch), o, residual add
-        fused with the next RMSNorm, gate/up, SiLU * up, down -- 7 launches."""
+        """One token with libepq.so's fused decode kernels.  With the tensor-core
+        layout (``gpu_layout="mma16"``) a layer is five launches of
+        epq_decode_linear / epq_attn_rope_decode (include/epq_decode.h):
+
+        * q/k/v with the input RMSNorm as its prologue;
+        * RoPE + KV write + attention;
+        * o, added into the residual stream in its epilogue;
+        * gate/up with the RMSNorm prologue and a SiLU(gate) * up epilogue;
+        * down, added into the residual stream.
+
+        The rounding points are the reference block's: every linear output,
+        the residual after each add, the normed input and SiLU * up are rounded
+        to bf16.  Other layouts use the unfused launches (linear_multi + glue)."""
+        sh = self.shapes
+        H, hd = sh.heads, sh.head_dim
+        if not self._fusable:
+            return self._decode_unfused(ids, pos)
+        h = self.embed[ids].contiguous()                               # residual stream [1, hidden]
+        for li, b in enumerate(self.stack.blocks):
+            q, k, v = _native.decode_linear(h, [b["q_proj"], b["k_proj"], b["v_proj"]],
+                                            prologue=_native.PRO_RMSNORM, eps=self.eps)
+            att = _native.attn_rope_decode(q.view(H, hd), k.view(-1, hd), v.view(-1, hd), pos, self.cos,
+                                           self.sin, self.k_cache[li], self.v_cache[li], self.qk_norm,
+                                           self.eps, 1.0 / math.sqrt(hd), self.attn_ws)
+            _native.decode_linear(att.view(1, H * hd), [b["o_proj"]], epilogue=_native.EPI_RESIDUAL,
+                                  outs=[h])
+            (a,) = _native.decode_linear(h, [b["gate_proj"], b["up_proj"]], prologue=_native.PRO_RMSNORM,
+                                         epilogue=_native.EPI_SILU_MUL, eps=self.eps)
+            _native.decode_linear(a, [b["down_proj"]], epilogue=_native.EPI_RESIDUAL, outs=[h])
+        return self._logits(_native.add_rmsnorm(h, eps=self.eps))
+
+    def _decode_unfused(self, ids, pos):
+        """One token with the per-linear launches and the separate glue kernels
+        (residual add + RMSNorm, RoPE + KV write + attention, SiLU * up)."""
         sh = self.shapes
         H, hd = sh.heads, sh.head_dim
         x = self.embed[ids]                                            # [1, hidden]
@@ -169,8 +201,14 @@ class PackedDecoder:
         return self._logits(self._rms(x[-1:]))
 
     # -- decoding ------------------------------------------------------------------
+    def _check_capacity(self, positions, what):
+        if positions > self.max_len:
+            raise ValueError(f"epure: {what} needs {positions} KV-cache positions; this decoder holds "
+                             f"max_len={self.max_len}")
+
     def prefill(self, prompt):
         """Runs the prompt (long tensor [T]); returns the logits after its last token."""
+        self._check_capacity(prompt.shape[0], "the prompt")
         pos = torch.arange(prompt.shape[0], device=self.device)
         return self.forward(prompt.to(self.device), pos)
 
@@ -206,7 +244,11 @@ class PackedDecoder:
         self.pos.add_(1)
 
     def generate(self, prompt, n_new, graph=True):
-        """Greedy decode: ``n_new`` tokens after ``prompt`` (returns a long tensor)."""
+        """Greedy decode: ``n_new`` tokens after ``prompt`` (returns a long tensor).
+
+        The prompt and the new tokens must fit the KV cache (``max_len``); the
+        graphed step also checks its device-side position on every replay."""
+        self._check_capacity(prompt.shape[0] + n_new, f"a {prompt.shape[0]}-token prompt + {n_new} new tokens")
         first = int(torch.argmax(self.prefill(prompt)))
         out = [first]
         if graph:
@@ -231,6 +273,7 @@ class PackedDecoder:
         """Float32 logits [len(tokens), vocab] after the prompt and after each of
         ``tokens[:-1]`` fed in order: the prediction for every position of ``tokens``
         given the true prefix."""
+        self._check_capacity(prompt.shape[0] + tokens.shape[0], "teacher forcing")
         out = torch.empty(tokens.shape[0], self.shapes.vocab, device=self.device)
         out[0] = self.prefill(prompt)
         T0 = prompt.shape[0]

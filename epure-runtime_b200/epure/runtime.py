@@ -251,6 +251,11 @@ class PackedLinear(nn.Module):
                 out = cpu_kernel.linear(x, s, _BUFFER_CACHE)
             if out is not None:
                 return out + self.bias if self.bias is not None else out
+        elif x.is_cuda:
+            # A stacked (rank > 2) store is not one linear: the reference's
+            # fallback would hand F.linear a 3-D weight.  Say so instead.
+            raise RuntimeError(f"epure: PackedLinear needs a 2-D store, got shape {tuple(s.shape)}; "
+                               "stacked expert slabs are served by PackedParameter")
 
         w = s.materialize(x.dtype)
         out = F.linear(x, w, self.bias)

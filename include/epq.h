@@ -124,7 +124,9 @@ const char* epq_last_error(void);
  * memory placement violated and wrote nothing; bit 1 -- a bounded
  * device-side wait gave up (that call's output is invalid); bit 2 -- the
  * chain kernel's placement or grid check failed; bit 3 -- epq_embedding was
- * given an id outside the store's rows (that row of its output is zero).
+ * given an id outside the store's rows (that row of its output is zero); bit
+ * 4 -- a decode-glue call (include/epq_decode.h) got a position outside its
+ * KV cache (nothing was written to the cache).
  * *flag = 0 means no kernel has reported a failure. */
 int epq_device_error(int* flag);
 
@@ -259,8 +261,10 @@ int epq_materialize(const epq_store* store, void* w, int64_t ldw, int32_t out_dt
  * ldo >= k, out_dtype) = W[ids[i], :] with materialize's rounding, for n_ids
  * device-resident int64 ids; only those rows are decoded.  Replaces
  * PackedEmbedding.forward (runtime.py:129-160: gather cb[idx] for the ids'
- * rows, cast, multiply by the rows' scales).  Any store format.  An id outside
- * [0, n) gives a zero row and sets bit 3 of epq_device_error. */
+ * rows, cast, multiply by the rows' scales).  Any store format.  A negative
+ * id counts from the end (id + n), as torch indexing does; an id outside
+ * [-n, n) gives a zero row and sets bit 3 of epq_device_error (the reference's
+ * indexing raises there -- set EPURE_CHECK_IDS=1 for the same on the host). */
 int epq_embedding(const epq_store* store, const int64_t* ids, int64_t n_ids, void* out, int64_t ldo,
                   int32_t out_dtype, void* stream);
 

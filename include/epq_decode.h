@@ -26,6 +26,11 @@ extern "C" {
 int epq_add_rmsnorm(const void* x, const void* add, void* h_out, void* y, int64_t m, int64_t n,
                     float eps, int32_t dtype, void* stream);
 
+/* Positions are read on the device, so every call below that takes a KV cache
+ * also takes its capacity max_len: a position outside [0, max_len) writes
+ * nothing to the cache (and zeros to an attention output) and sets bit 4 of
+ * epq_device_error, instead of writing past the cache. */
+
 /* For m rows at positions pos[m] (device): q [m, heads, head_dim] is rotated in
  * place; k, v [m, kv_heads, head_dim] are written to k_cache / v_cache
  * [max_len, kv_heads, head_dim] at those positions, k rotated.  qk_norm != 0
@@ -34,7 +39,8 @@ int epq_add_rmsnorm(const void* x, const void* add, void* h_out, void* y, int64_
  * head_dim 64, 128 or 256. */
 int epq_rope_kv(void* q, const void* k, const void* v, const int64_t* pos, int64_t m, int32_t heads,
                 int32_t kv_heads, int32_t head_dim, const float* cos_tab, const float* sin_tab,
-                void* k_cache, void* v_cache, int32_t qk_norm, float eps, int32_t dtype, void* stream);
+                void* k_cache, void* v_cache, int64_t max_len, int32_t qk_norm, float eps, int32_t dtype,
+                void* stream);
 
 /* One query token: out[h] = softmax(scale * q[h] . K[0..pos[0]]) V for every head h
  * (grouped-query: head h reads kv head h / (heads / kv_heads)); q, out [heads, head_dim],
@@ -45,7 +51,7 @@ int epq_rope_kv(void* q, const void* k, const void* v, const int64_t* pos, int64
  * first use and is left ready for the next call.  Without one, one CTA per head. */
 int64_t epq_attn_decode_workspace_bytes(int32_t heads, int32_t kv_heads, int32_t head_dim);
 int epq_attn_decode(const void* q, const void* k_cache, const void* v_cache, const int64_t* pos,
-                    int32_t heads, int32_t kv_heads, int32_t head_dim, float scale, void* out,
+                    int64_t max_len, int32_t heads, int32_t kv_heads, int32_t head_dim, float scale, void* out,
                     int32_t dtype, void* workspace, int64_t workspace_bytes, void* stream);
 
 /* epq_rope_kv + epq_attn_decode in one launch (bf16, head_dim 64 or 128, heads /
@@ -55,8 +61,8 @@ int epq_attn_decode(const void* q, const void* k_cache, const void* v_cache, con
  * over positions 0..pos[0].  Workspace as for epq_attn_decode (required). */
 int epq_attn_rope_decode(const void* q, const void* k, const void* v, const int64_t* pos, int32_t heads,
                          int32_t kv_heads, int32_t head_dim, const float* cos_tab, const float* sin_tab,
-                         void* k_cache, void* v_cache, int32_t qk_norm, float eps, float scale, void* out,
-                         int32_t dtype, void* workspace, int64_t workspace_bytes, void* stream);
+                         void* k_cache, void* v_cache, int64_t max_len, int32_t qk_norm, float eps, float scale,
+                         void* out, int32_t dtype, void* workspace, int64_t workspace_bytes, void* stream);
 
 /* *out = the first index of the maximum of x[0..n) (torch.argmax), on the device.
  * workspace: epq_argmax_workspace_bytes(), 256-byte aligned, zeroed once before first
@@ -67,6 +73,30 @@ int epq_argmax(const float* x, int64_t n, int64_t* out, void* workspace, int64_t
 
 /* out = silu(g) * u over n values. */
 int epq_silu_mul(const void* g, const void* u, void* out, int64_t n, int32_t dtype, void* stream);
+
+/* Prologue / epilogue options of epq_decode_linear. */
+enum epq_prologue { EPQ_PRO_NONE = 0, EPQ_PRO_RMSNORM = 1 };
+enum epq_epilogue { EPQ_EPI_STORE = 0, EPQ_EPI_RESIDUAL = 1, EPQ_EPI_SILU_MUL = 2 };
+
+/* A decode-step packed linear with the block glue around it fused in: the
+ * tensor-core GEMV of epq_linear_multi (1 <= m <= 16 rows of bf16 / f16
+ * activations, EPQ_LAYOUT_MMA16 vector stores sharing k; each weight decoded
+ * as dtype(dtype(cb[idx]) * dtype(scale)), the reference's materialize rounding)
+ * with
+ *   prologue EPQ_PRO_RMSNORM: x is replaced by RMSNorm(x) (weight 1, eps) per
+ *            row while it is staged (m * k * 2 <= 64 KiB);
+ *   epilogue EPQ_EPI_STORE:    outs[i] = x @ W_i^T (rounded to x_dtype);
+ *            EPQ_EPI_RESIDUAL: one store; outs[0] is a residual stream updated
+ *                              in place: h = h + dtype(x @ W^T);
+ *            EPQ_EPI_SILU_MUL: two stores of equal rows (gate, up);
+ *                              outs[0] = dtype(silu(dtype(x @ Wg^T)) * dtype(x @ Wu^T))
+ *                              (outs[1] is not written).
+ * The reference's block (epure/runtime.py:98-126 PackedLinear inside a Llama /
+ * Qwen3 decoder layer) rounds at exactly these points.  No workspace; the launch
+ * may overlap the previous kernel on the stream (programmatic dependent launch). */
+int epq_decode_linear(const epq_store* stores, int32_t count, const void* x, int32_t x_dtype, int64_t m,
+                      int64_t ldx, int32_t prologue, float eps, void* const* outs, const int64_t* ldo,
+                      int32_t epilogue, void* stream);
 
 #ifdef __cplusplus
 }

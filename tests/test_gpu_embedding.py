@@ -52,3 +52,27 @@ def test_embedding_empty_batch():
     st = synthetic.make_store(64, 256, device=DEV, seed=2)
     out = PackedEmbedding(st, dtype=torch.bfloat16)(torch.zeros(0, dtype=torch.long, device=DEV))
     assert out.shape == (0, 256)
+
+
+def test_negative_ids_count_from_the_end():
+    """As torch indexing does: id -1 is the last row."""
+    from epure import synthetic
+    from epure.runtime import PackedEmbedding
+    st = synthetic.make_store(100, 256, device=DEV, seed=4)
+    ids = torch.tensor([[-1, 0, -100, 5]], device=DEV)
+    got = PackedEmbedding(st, dtype=torch.bfloat16)(ids)
+    w = st.materialize(torch.bfloat16)
+    assert torch.equal(got[0], w[torch.tensor([99, 0, 0, 5], device=DEV)])
+
+
+def test_ids_on_the_host_are_moved_to_the_store(monkeypatch):
+    from epure import _native, synthetic
+    from epure.runtime import PackedEmbedding
+    st = synthetic.make_store(64, 256, device=DEV, seed=5)
+    ids = torch.tensor([3, 63, 0])
+    got = _native.embedding(st, ids, torch.bfloat16)
+    assert got.device == st.packed.device
+    assert torch.equal(got, st.materialize(torch.bfloat16)[ids.to(DEV)])
+    monkeypatch.setattr(_native, "CHECK_IDS", True)
+    with pytest.raises(IndexError):
+        PackedEmbedding(st, dtype=torch.bfloat16)(torch.tensor([64], device=DEV))

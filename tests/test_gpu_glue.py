@@ -133,3 +133,56 @@ def test_attn_rope_matches_two_kernels(heads, kv, hd, qk):
     assert _rel(got, want) <= 1e-2
     assert _rel(kc[P], kc2[P]) <= 1e-2 and torch.equal(vc[P], vc2[P])
     assert torch.equal(kc[:P], kc2[:P])
+
+
+_PAST_CACHE_CHILD = r"""
+import math, sys, torch
+sys.path.insert(0, sys.argv[1])
+from epure import _native
+dev = "cuda:0"
+heads, kv, hd, L = 16, 8, 128, 32
+g = torch.Generator(device=dev).manual_seed(0)
+q = torch.randn(heads, hd, generator=g, device=dev).to(torch.bfloat16)
+k = torch.randn(kv, hd, generator=g, device=dev).to(torch.bfloat16)
+v = torch.randn(kv, hd, generator=g, device=dev).to(torch.bfloat16)
+kc = torch.randn(L, kv, hd, generator=g, device=dev).to(torch.bfloat16)
+vc = kc.clone()
+cos = torch.ones(L, hd // 2, device=dev)
+sin = torch.zeros(L, hd // 2, device=dev)
+ws = _native.attn_decode_workspace(heads, kv, hd, dev)
+k0, v0 = kc.clone(), vc.clone()
+assert _native.device_error() == 0
+out = _native.attn_rope_decode(q, k, v, torch.tensor([L], device=dev), cos, sin, kc, vc, False, 1e-6,
+                               1.0 / math.sqrt(hd), ws)
+torch.cuda.synchronize()
+assert torch.equal(kc, k0) and torch.equal(vc, v0), "cache written past its capacity"
+assert not out.any(), "attention output not zeroed"
+flag = _native.device_error()
+# the same workspace still serves an in-range call afterwards
+_native.attn_rope_decode(q, k, v, torch.tensor([L - 1], device=dev), cos, sin, kc, vc, False, 1e-6,
+                         1.0 / math.sqrt(hd), ws)
+torch.cuda.synchronize()
+print("FLAG", flag)
+"""
+
+
+def test_position_past_cache_is_refused():
+    """A device-side position at the KV cache's capacity writes nothing to the cache,
+    zeroes the attention output and sets bit 4 of epq_device_error.  Run in a child
+    process, because the flag stays set for the rest of that process."""
+    import subprocess
+    import sys
+    from conftest import PKG
+    r = subprocess.run([sys.executable, "-c", _PAST_CACHE_CHILD, PKG], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert "FLAG 16" in r.stdout, r.stdout
+
+
+def test_decoder_refuses_more_tokens_than_its_cache():
+    from epure.model import PackedDecoder
+    from epure.synthetic import DecoderShapes
+    dec = PackedDecoder(DecoderShapes("tiny", 1, 256, 512, 4, 2, 64, 100), device=DEV, seed=1, max_len=16)
+    with pytest.raises(ValueError, match="max_len"):
+        dec.generate(torch.arange(10), 7, graph=False)
+    with pytest.raises(ValueError, match="max_len"):
+        dec.prefill(torch.arange(17))

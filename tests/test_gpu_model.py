@@ -2,19 +2,24 @@
 
 * The decoder with libepq.so's kernels ("ours") gives the same logits as the
   same model in float32 (weights cb * scale exactly) within bf16 tolerance.
+* The fused decode launches (RMSNorm prologue, residual / SiLU epilogues) give
+  the logits of the same block written with torch glue.
 * The CUDA-graphed greedy loop emits exactly the tokens of the eager loop.
-* Greedy top-1 agreement over 256 decode steps of the Qwen3-1.7B-shaped model
-  (28 layers, 128-token prompt of uniform random ids), teacher-forced on the
-  reference's own greedy sequence: ours against the float32 model is at least
-  as close as the reference's bf16 path (``F.linear(x, materialize(bf16))``,
-  runtime.py:123-124) is, ours against the reference is >= 0.9, ours' logits are
-  no further from float32 than the reference's (max relative error over all steps
-  after 28 bf16 layers: ~4-5e-2 for both), and every step where ours
-  picks another token than float32 is a near-tie: the float32 gap between the
-  two tokens is within twice ours' logit error on them.  With random weights the
-  logits are nearly flat (top-1 margins of a few hundredths), so the bf16 weight
-  rounding of the reference path itself flips ~9 % of the argmaxes relative to
-  float32; the agreement bounds are relative for that reason.
+* Greedy top-1 agreement over 256 decode steps (128-token prompt of uniform
+  random ids) on the Qwen3-1.7B and Llama-3-8B shapes, teacher-forced on the
+  reference's own greedy sequence (``F.linear(x, materialize(bf16))``,
+  runtime.py:123-124, with the block in torch ops).  Ours decodes the
+  reference's bf16 weight bit for bit, so the two differ only in the fp32
+  summation order of each linear.  With random weights the logits are nearly
+  flat, and any change of summation order flips some argmaxes: the same
+  reference block with every linear computed exactly (float64, then rounded
+  to bf16 -- the "exact control") agrees with the reference on ~95 % of the
+  steps, not 99 %.  The test therefore asserts that ours agrees with the
+  reference about as well as the exact control does (flip counts are small
+  and noisy: within 8 of 256 steps), that every step where ours and the
+  reference differ is a near-tie of the reference's own logits (their gap
+  is within twice ours' logit deviation there), and that ours is no further
+  from the float32 model than the reference is.
 """
 import pytest
 import torch
@@ -87,39 +92,55 @@ def test_graph_matches_eager():
     assert torch.equal(got.cpu(), want.cpu())
 
 
-def _flip_stats(lg, l32):
-    """Top-1 flips of logits ``lg`` against ``l32`` and whether each is a near-tie: the
-    float32 gap between the two tokens is within twice ``lg``'s error on them."""
-    a, a32 = lg.argmax(-1), l32.argmax(-1)
-    flips = (a != a32).nonzero().flatten()
-    rows = torch.arange(lg.shape[0], device=lg.device)
-    gap = l32[rows, a32] - l32[rows, a]
-    err = torch.maximum((lg[rows, a] - l32[rows, a]).abs(), (lg[rows, a32] - l32[rows, a32]).abs())
-    explained = bool((gap[flips] <= 2 * err[flips] + 1e-6).all())
-    rel = float(((lg - l32).abs().amax(-1) / l32.abs().amax(-1)).max())
-    return a.cpu(), len(flips), explained, rel, float(gap[flips].max()) if len(flips) else 0.0
+def _exact_control(dec):
+    """The reference block with each linear computed exactly (float64) and rounded
+    to bf16: a valid implementation of the reference's arithmetic that differs
+    from it only in summation order."""
+    import types
+    ctl = dec.share_weights("reference")
+
+    def lin(self, x, stores):
+        return [(x.double() @ st.materialize(x.dtype).double().T).to(x.dtype) for st in stores]
+
+    ctl._lin = types.MethodType(lin, ctl)
+    return ctl
 
 
-def test_qwen3_greedy_agreement_256():
+@pytest.mark.parametrize("model", ["qwen3-1.7b", "llama3-8b"])
+def test_greedy_agreement_256(model):
     from epure import synthetic
     from epure.model import PackedDecoder
-    ours = PackedDecoder(synthetic.QWEN3_1_7B, device=DEV, seed=11, max_len=128 + 256)
+    shapes = synthetic.SHAPES[model]
+    ours = PackedDecoder(shapes, device=DEV, seed=11, max_len=128 + 256)
     ref = ours.share_weights("reference")
     f32 = ours.share_weights("fp32")
     g = torch.Generator().manual_seed(2)
-    prompt = torch.randint(0, synthetic.QWEN3_1_7B.vocab, (128,), generator=g)
+    prompt = torch.randint(0, shapes.vocab, (128,), generator=g)
     seq = ref.generate(prompt, 256, graph=False).cpu()
+    l_ref = ref.teacher_forced_logits(prompt, seq)
+    l_ours = ours.teacher_forced_logits(prompt, seq)
+    p_ref, p_ours = l_ref.argmax(-1).cpu(), l_ours.argmax(-1).cpu()
+    p_ctl = _exact_control(ours).teacher_forced_argmax(prompt, seq)
     l32 = f32.teacher_forced_logits(prompt, seq)
-    p_ours, n_ours, expl_ours, rel_ours, gap_ours = _flip_stats(ours.teacher_forced_logits(prompt, seq), l32)
-    p_ref, n_ref, expl_ref, rel_ref, gap_ref = _flip_stats(ref.teacher_forced_logits(prompt, seq), l32)
     p_f32 = l32.argmax(-1).cpu()
     assert torch.equal(p_ref, seq)                    # the reference reproduces itself
     agree = lambda a, b: float((a == b).float().mean())          # noqa: E731
-    ours_f32, ref_f32, ours_ref = agree(p_ours, p_f32), agree(p_ref, p_f32), agree(p_ours, p_ref)
-    print(f"top-1 agreement over 256 steps: ours~fp32 {ours_f32:.4f}  reference~fp32 {ref_f32:.4f}  "
-          f"ours~reference {ours_ref:.4f}; logit max rel err vs fp32: ours {rel_ours:.2e} "
-          f"reference {rel_ref:.2e}; largest flipped fp32 gap: ours {gap_ours:.4f} reference {gap_ref:.4f}")
-    assert rel_ours <= min(6e-2, max(1.1 * rel_ref, 1e-2))   # no further from fp32 than the reference
-    assert expl_ours                                   # every flip of ours is a near-tie
+    ours_ref, ctl_ref = agree(p_ours, p_ref), agree(p_ctl, p_ref)
+    ours_f32, ref_f32 = agree(p_ours, p_f32), agree(p_ref, p_f32)
+    # steps where ours differs from the reference: the reference's own logit gap
+    # between the two tokens against the size of ours' logit deviation there
+    rows = (p_ours != p_ref).nonzero().flatten()
+    gap = (l_ref[rows, p_ref[rows]] - l_ref[rows, p_ours[rows]]).abs()
+    dev = (l_ours[rows] - l_ref[rows]).abs().amax(-1)
+    rel_ours = float(((l_ours - l32).abs().amax(-1) / l32.abs().amax(-1)).max())
+    rel_ref = float(((l_ref - l32).abs().amax(-1) / l32.abs().amax(-1)).max())
+    print(f"{model}: top-1 agreement over 256 steps: ours~reference {ours_ref:.4f}  "
+          f"exact-control~reference {ctl_ref:.4f}  ours~fp32 {ours_f32:.4f}  reference~fp32 {ref_f32:.4f}; "
+          f"flips {len(rows)}, largest reference gap at a flip {float(gap.max()) if len(rows) else 0:.4f}; "
+          f"logit max rel err vs fp32: ours {rel_ours:.2e} reference {rel_ref:.2e}")
+    # the flip counts of two implementations that differ only in summation order are
+    # small (~5-15 of 256) and noisy: allow ours 8 more flips than the exact control
+    assert ours_ref >= min(0.99, ctl_ref - 8 / 256)
+    assert bool((gap <= 2 * dev + 1e-6).all())          # every flip is a near-tie of the reference
     assert ours_f32 >= ref_f32 - 0.01
-    assert ours_ref >= 0.9
+    assert rel_ours <= max(1.1 * rel_ref, 1e-2)

@@ -90,3 +90,32 @@ def test_noalloc_rejects_oversized_and_unsupported(lib):
     o = torch.empty(1, 64, device=DEV)
     rc = lib.epq_linear_noalloc(d, 1, xs.data_ptr(), 0, (ctypes.c_void_p * 1)(o.data_ptr()), 0, None)
     assert rc == -8
+
+
+def test_noalloc_rejects_too_many_row_blocks(lib):
+    """More 16-row blocks than the static scratch has completion counters (16384):
+    refused before launch, although the partial sums themselves would fit."""
+    from epure import _native
+    stores = _tiled_stores([(70000, 128)] * 4, seed=40)          # 4 x 4375 row blocks
+    x = torch.randn(1, 128, device=DEV).to(torch.bfloat16)
+    d = (_native.EpqStore * 4)(*[_native.describe_store(s) for s in stores])
+    outs = [torch.empty(1, 70000, dtype=torch.bfloat16, device=DEV) for _ in stores]
+    ptrs = (ctypes.c_void_p * 4)(*[o.data_ptr() for o in outs])
+    rc = lib.epq_linear_noalloc(d, 4, x.data_ptr(), 2, ptrs, 2, None)
+    assert rc == -8 and b"row blocks" in lib.epq_last_error()
+
+
+def test_noalloc_large_then_small_then_large(lib):
+    """Calls of different sizes in a row reuse the one static scratch: the counters a
+    large call used must not leak into the next, smaller one (or back)."""
+    from epure import _native
+    big = _tiled_stores([(6144, 2048), (1024, 2048)], seed=60)
+    small = _tiled_stores([(37, 200)], seed=70)
+    for stores in (big, small, big, small):
+        x = torch.randn(1, stores[0].in_features, device=DEV).to(torch.bfloat16)
+        got = _noalloc(lib, stores, x)
+        want = _native.linear_multi(x, stores)
+        torch.cuda.synchronize()
+        for g, w in zip(got, want):
+            assert float((g.float() - w.float()).abs().max() / w.float().abs().max()) <= 1e-5
+    assert _native.device_error() == 0
