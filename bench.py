@@ -1,61 +1,58 @@
-"""Benchmark: batch-1 decode through every packed linear of a Llama-3-8B-shaped model.
+"""Benchmark: batch-1 greedy decode of a Llama-3-8B-shaped codebook-quantized model.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-One step is one decode token: all 32 x 7 codebook-quantized linears of the
-Llama-3-8B shapes (indices u8 per 4-weight vector, 256x4 fp16 codebook, fp16
-scale per row per 128 weights; 1.85 GB of indices), visited in layer order
-with each launch reading the previous one's output.  The packed weights
-(1.9 GB) are far larger than the 126 MB L2, so every step streams them from
-HBM; no L2 flush is needed.  Attention, norms and the bf16 lm_head are not
-part of the packed-linear path and are not in the step.
+N = 1 (the headline).  One step is one whole decode
+token of ``epure.model.PackedDecoder`` on Llama-3-8B shapes with random weights
+in the benchmark's format (u8 index per 4-weight vector, 256x4 fp16 codebook,
+fp16 scale per row per 128 weights; bf16 embedding and lm_head): the embedding
+row, then per layer five launches of libepq.so -- q/k/v with the input RMSNorm
+fused in, RoPE + KV-cache write + attention, o added into the residual, gate/up
+with the RMSNorm and SiLU(gate)*up fused in, down added into the residual --
+then the final RMSNorm, the bf16 lm_head (cuBLAS), argmax and the position
+update, all replayed from one CUDA graph after a 128-token prompt.  Every
+packed weight is decoded exactly as the reference's bf16 path decodes it.  The
+2.9 GB the step streams are far larger than the 126 MB L2, so no flush is
+needed.
+  value      tokens/s over K graph replays (the token stays on the device);
+  e2e        the same through the public step with the token copied in from
+             pinned host memory and the next token read back every step;
+  roofline   the dominant kernel, gemv_mma_kernel: the token's 128 packed
+             launches replayed alone (epure.decode.GraphedLinearStack over the
+             same stores), algorithmic bytes / their CUDA-event time;
+  token_roofline  the whole token's bytes (packed + lm_head + embedding row +
+             KV read) / token time -- the north-star basis (2,904.6 MB/token);
+  cpu_baseline    the reference's CPU path on whole tokens (below), rank 0.
 
-Our arm runs the step as ONE persistent launch of libepq.so's chain kernel
-(epq_chain_run: every packed linear of the token, weights streamed through a
-TMA ring per SM, each linear's input polled from the tagged split-k partial sums
-of the previous one, no grid barrier), replayed from a CUDA
-graph (value), and separately through the public runner with host buffers
-(e2e: pinned H2D copy of the token input, replay, D2H copy of the output, every
-step).  `--mode per-linear` instead replays 128 launches of the single-linear
-tensor-core GEMV (one per fused q/k/v, o, gate/up, down).  At N > 1
-each rank runs an independent replica on its own GPU (weak scaling; the 8B
-model fits one GPU, so there is no collective on the data path); the time is
-the max over ranks.
+N > 1.  Llama-3-70B shapes (config 4) tensor-parallel over the N GPUs: every
+packed linear of a token on each rank's shards in ONE persistent launch of the
+chain kernel per rank, the all-reduce after o and down done inside the kernel
+over NVLink (peer loads; no NCCL launch on the data path); strong scaling.
+Before timing, rank 0 checks the TP chain against the single-GPU chain on a
+2-layer slice of the same model (full width) and prints the error as
+``tp_check``; past 1e-4 every rank exits non-zero.  ``--replicas`` runs N
+independent copies of the N = 1 workload instead (weak scaling).
 
-Other workloads (not the headline; each prints its own metric):
-  --mode finetune [--tokens 16384]: one compressed-state fine-tuning step (the
-      config-3 batch of 8 x 2048 tokens, Qwen3-1.7B shapes by default) through
-      every packed linear: forward, dX, dscale/dcb (epure.train.PackedTrainStep);
-  --mode prefill [--tokens 2048]: a prompt of `tokens` rows through every packed
-      linear (the tensor-core dequant-GEMM, one launch per fused group), metric
-      prefill tok/s, roofline against the sustained bf16 tensor peak;
-  --mode model: greedy decode of the whole model (epure.model.PackedDecoder:
-      packed linears through libepq.so, attention / norms / lm_head in torch, one
-      CUDA graph per token after a 128-token prompt), metric tok/s;
-  --mode embedding [--tokens N]: packed embedding rows for N ids (epq_embedding), with
-      the reference's torch formulation timed beside it;
-  --mode per-linear --batch B: a B-token decode step through the per-linear launches
-      (the tensor-core GEMV up to 16 rows, the tcgen05 GEMM above), metric tok/s;
-  --model qwen3-1.7b|llama3-8b|llama3-70b picks the decoder shapes;
-  --layers L keeps the first L layers (small cases for profiling);
-  --tp (with N > 1): one model tensor-parallel over the N GPUs (column-parallel
-      q/k/v and gate/up, row-parallel o and down), one token stream, strong
-      scaling; in the default chain mode the all-reduce of o and down happens
-      inside the persistent kernel over NVLink, with --mode per-linear it is an
-      NCCL all-reduce after each row-parallel launch;
-  --fallback also times the reference's bf16 fallback path on the GPU
-      (F.linear(x, materialize(bf16)) store by store, torch ops) on the same step.
+Reference arm (--impl reference; rank 0 alone, the other ranks exit 0): the
+reference's CPU implementation of the path on every host thread -- each packed
+linear through the C restatement of its fused Rust kernel (kernel/src/lib.rs,
+oracle/epq_oracle.c; f32 activations, as lib.rs takes), the rest of the block
+(RMSNorm, RoPE, attention over the KV cache, SiLU, lm_head) in numpy float32.
+N = 1: one whole 8B token per step.  N > 1: the 70B shapes' packed linears of
+8 of the 80 layers per step (tok/s = 1 / (10 x step)); the sample is named in
+``cpu_baseline.sample``.  It imports nothing from the epure package.
 
-The reference arm (--impl reference) runs the reference's fused CPU kernel
-(kernel/src/lib.rs, restated in C under oracle/) on the host cores: each step
-is one layer's 7 linears with f32 activations, and tokens/s is scaled by the
-32 layers.  Rank 0 alone runs it.
+Other workloads (each prints its own metric): --mode chain (the packed linears
+only, as one persistent chain launch per token, fp32 between layers), --mode
+per-linear [--batch B] (the per-linear GEMV / GEMM launches), --mode prefill
+[--tokens 2048], --mode finetune [--tokens 16384], --mode embedding;
+--model / --layers pick the shapes; --fallback also times the reference's bf16
+GPU fallback (materialize + F.linear, torch ops) on the same step.
 """
 import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import time
 
@@ -65,24 +62,49 @@ sys.path.insert(0, ROOT)
 
 METRIC = "decode tok/s bs1 @8B; dequant-GEMV HBM GB/s as % of B200 peak"
 UNIT = "tok/s"
-WORKLOAD = "llama3-8b packed linears, batch-1 decode token (224 linears)"
+PROMPT = 128
 
-# DRAM traffic / algorithmic bytes per mode, from one ncu capture each.  Traffic
-# grows with the bytes streamed, so a step's traffic is reported as the ratio
-# times the step's algorithmic bytes.
-#   per-linear: gemv_mma_kernel on a Llama-3-8B gate+up launch
-#     (profiles/gemv_mma_kernel_llama3-8b_gateup_b1.md): 31,236,096 B of
-#     dram__bytes_read.sum + dram__bytes_write.sum against 31,264,768 B.
-#   chain: chain_kernel on a 4-layer Llama-3-8B chain
-#     (profiles/chain_kernel_llama3-8b_decode_b1.md): 232,937,728 B read +
-#     24,145,664 B written against 232,349,696 algorithmic bytes.
-NCU_TRAFFIC_RATIO = {"per-linear": 31236096 / 31264768,
+# The decoder shapes (name, layers, hidden, intermediate, heads, kv heads, head dim,
+# vocab) -- copied here so the reference arm needs nothing from the epure package.
+SHAPES = {
+    "qwen3-1.7b": ("qwen3-1.7b", 28, 2048, 6144, 16, 8, 128, 151936),
+    "llama3-8b": ("llama3-8b", 32, 4096, 14336, 32, 8, 128, 128256),
+    "llama3-70b": ("llama3-70b", 80, 8192, 28672, 64, 8, 128, 128256),
+}
+ROPE_THETA = {"qwen3-1.7b": 1.0e6, "llama3-8b": 5.0e5, "llama3-70b": 5.0e5}
+RMS_EPS = {"qwen3-1.7b": 1e-6, "llama3-8b": 1e-5, "llama3-70b": 1e-5}
+
+# DRAM traffic / algorithmic bytes of the dominant kernel, from one ncu capture
+# (profiles/): per-linear = gemv_mma_kernel on a Llama-3-8B gate+up launch
+# (dram__bytes_read.sum + dram__bytes_write.sum over the launch's algorithmic
+# bytes); chain = chain_kernel on a 4-layer chain.
+NCU_TRAFFIC_RATIO = {"per-linear": 31249152 / 31264768,
                      "chain": (232937728 + 24145664) / 232349696}
-TRAFFIC_NOTE = {"per-linear": "per step, scaled from one ncu capture of the gate+up launch "
-                              "(traffic/algorithmic = 0.999)",
-                "chain": "per step, scaled from one ncu capture of a 4-layer chain "
-                         "(traffic/algorithmic = 1.106; the extra bytes are the tagged split-k "
-                         "partial sums written back to DRAM)"}
+
+
+def linears(shape):
+    """(name, out_features, in_features) of one layer's packed linears."""
+    _, _, h, i, heads, kv, hd, _ = shape
+    return [("q_proj", heads * hd, h), ("k_proj", kv * hd, h), ("v_proj", kv * hd, h),
+            ("o_proj", h, heads * hd), ("gate_proj", i, h), ("up_proj", i, h), ("down_proj", h, i)]
+
+
+def workload(args, world):
+    """(workload name, config dict) shared by both arms, so the two lines compare."""
+    shape = SHAPES[args.model]
+    layers = args.layers or shape[1]
+    part = f" (first {layers} of {shape[1]} layers)" if layers != shape[1] else ""
+    if args.mode == "model":
+        name = f"{args.model} whole-model greedy decode token, batch 1, after a {PROMPT}-token prompt{part}"
+        par = f"replicas x{world}" if world > 1 else "single GPU"
+    else:   # tp chain
+        name = f"{args.model} packed linears of one batch-1 decode token, tensor-parallel{part}"
+        par = f"tp{world}"
+    cfg = {"workload": name, "mode": args.mode if not args.tp else "tp-chain", "model": args.model,
+           "layers": layers, "global_batch": world if (args.mode == "model" and world > 1) else 1,
+           "seq_len": PROMPT + args.warmup + args.steps + 2 if args.mode == "model" else 1,
+           "parallelism": par, "l2": "inputs larger than L2 (no flush needed)"}
+    return name, cfg
 
 
 def _peaks():
@@ -105,126 +127,242 @@ def _tensor_peak():
 
 
 class ClockSampler:
-    """nvidia-smi clock/throttle samples for one GPU during the timed region."""
+    """SM clock, power and clock-event reasons of one GPU, polled from NVML every
+    few milliseconds while the timed region runs (nvidia-smi's 200 ms loop sees
+    too few samples of a tens-of-milliseconds region)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, gpu_index):
-        self.gpu = gpu_index
-        self.proc = None
+    def __init__(self, device_index, interval_s=0.004):
+        self.device_index, self.interval = device_index, interval_s
+        self.samples, self.max_mhz, self._thread, self._stop = [], None, None, False
+
+    def _handle(self, nv):
+        import torch
+        try:
+            p = torch.cuda.get_device_properties(self.device_index)
+            bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+            return nv.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return nv.nvmlDeviceGetHandleByIndex(self.device_index)
+
+    def _run(self, nv, h):
+        while not self._stop:
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                power = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+                self.samples.append((sm, reasons, power))
+            except Exception:
+                pass
+            time.sleep(self.interval)
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            import threading
+            import pynvml as nv
+            nv.nvmlInit()
+            h = self._handle(nv)
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            self._thread = threading.Thread(target=self._run, args=(nv, h), daemon=True)
+            self._thread.start()
         except Exception:
-            self.proc = None
+            self._thread = None
         return self
 
     def __exit__(self, *a):
-        self.lines = []
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                out, _ = self.proc.communicate(timeout=5)
-            except Exception:
-                self.proc.kill()
-                out = ""
-            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+        self._stop = True
+        if self._thread is not None:
+            self._thread.join(timeout=2)
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in getattr(self, "lines", []):
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for nm, val in zip(names, parts[5:9]):
-                if val.lower().startswith("active"):
-                    reasons.add(nm)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": ["no samples"]}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["no samples"]}
+        reasons = set()
+        for _, bits, _ in self.samples:
+            reasons |= {name for bit, name in self.REASONS.items() if bits & bit}
+        return {"sm_mhz": statistics.median(s for s, _, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(self.samples),
+                "power_w_max": round(max(p for _, _, p in self.samples), 1), "source": "nvml"}
 
 
 # ---------------------------------------------------------------------------
-# CPU reference arm / CPU baseline
+# the reference's CPU path (reference arm and cpu_baseline)
 # ---------------------------------------------------------------------------
-def cpu_reference_sample(seconds=10.0, threads=0, steps=None, warmup=1, model="llama3-8b"):
-    """Time the lib.rs restatement on one layer of `model`; returns (tok/s, info)."""
-    import numpy as np
-    from oracle import oracle as O
-    from epure import synthetic
+def host_threads():
+    """Every host thread this process may run on (torchrun sets OMP_NUM_THREADS=1
+    for its ranks; the reference's rayon pool ignores that and uses all cores)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
 
-    shapes = synthetic.SHAPES[model]
-    O.build_c_oracle()
-    rng = np.random.default_rng(0)
-    layer = []
-    for name, n, k in shapes.linears():
-        idx = rng.integers(0, 256, (n, k // 4), dtype=np.uint8)
-        cb = rng.standard_normal((256, 4)).astype(np.float16).astype(np.float32)
-        sc = np.abs(rng.normal(0, 0.02, (n, k // 128))).astype(np.float16).astype(np.float32)
-        x = rng.standard_normal((1, k)).astype(np.float32)
-        layer.append((x, idx, sc, cb, n, k))
 
-    def one_layer():
-        for x, idx, sc, cb, n, k in layer:
-            O.c_dequant_matmul(x, idx, sc, cb, n, k, 4, 128, 256, threads=threads)
+class CpuReferenceDecoder:
+    """One batch-1 decode token the way the reference runs it on the CPU.
 
+    Every packed linear is the reference's fused CPU kernel (kernel/src/lib.rs:
+    96-151, restated in C in oracle/epq_oracle.c: per output row and group a
+    table of cb * scale, an f32 sum over the group, group sums in order), with
+    f32 activations as that kernel takes them; the rest of the Llama / Qwen3
+    block (RMSNorm, RoPE, grouped-query attention over a KV cache, SiLU * up,
+    residuals, final norm, lm_head, argmax) is numpy float32, standing in for
+    the Hugging Face modules around the reference's PackedLinear.  Weights are
+    seeded random in the benchmark's format.  ``linears_only`` keeps just the
+    packed linears chained output to input (the tensor-parallel workload)."""
+
+    def __init__(self, shape, layers, threads, max_len=PROMPT + 64, seed=0, linears_only=False):
+        import numpy as np
+        from oracle import oracle as O
+        self.np, self.O = np, O
+        O.build_c_oracle()
+        self.shape, self.layers, self.threads = shape, layers, threads
+        self.linears_only = linears_only
+        name, _, h, inter, heads, kv, hd, vocab = shape
+        rng = np.random.default_rng(seed)
+        self.blocks = []
+        for _ in range(layers):
+            blk = {}
+            for lname, n, k in linears(shape):
+                idx = rng.integers(0, 256, (n, k // 4), dtype=np.uint8)
+                cb = rng.standard_normal((256, 4), dtype=np.float32).astype(np.float16).astype(np.float32)
+                sc = np.abs(rng.normal(0, 0.02, (n, k // 128))).astype(np.float16).astype(np.float32)
+                blk[lname] = (idx, sc, cb, n, k)
+            self.blocks.append(blk)
+        self.h, self.heads, self.kv, self.hd = h, heads, kv, hd
+        self.eps, self.qk_norm = RMS_EPS.get(name, 1e-6), name.startswith("qwen3")
+        if not linears_only:
+            self.embed = (rng.standard_normal((vocab, h), dtype=np.float32) * 0.02).astype(np.float32)
+            self.lm_head = self.embed if name.startswith("qwen3") else \
+                (rng.standard_normal((vocab, h), dtype=np.float32) * 0.02).astype(np.float32)
+            inv = 1.0 / (ROPE_THETA.get(name, 1e6) ** (np.arange(0, hd, 2, dtype=np.float64) / hd))
+            ang = np.arange(max_len, dtype=np.float64)[:, None] * inv[None, :]
+            self.cos, self.sin = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+            self.kc = np.zeros((layers, max_len, kv, hd), np.float32)
+            self.vc = np.zeros((layers, max_len, kv, hd), np.float32)
+            # a filled prompt: random K/V rows stand in for the 128 prefill positions
+            self.kc[:, :PROMPT] = rng.standard_normal((layers, PROMPT, kv, hd), dtype=np.float32)
+            self.vc[:, :PROMPT] = rng.standard_normal((layers, PROMPT, kv, hd), dtype=np.float32)
+            self.pos = PROMPT
+
+    def _lin(self, x, st):
+        idx, sc, cb, n, k = st
+        return self.O.c_dequant_matmul(x, idx, sc, cb, n, k, 4, 128, 256, threads=self.threads)
+
+    def _rms(self, x):
+        np = self.np
+        return x / np.sqrt(np.mean(x * x, axis=-1, keepdims=True) + self.eps)
+
+    def _rope(self, x, p):
+        np = self.np
+        half = self.hd // 2
+        c, s = self.cos[p], self.sin[p]
+        x1, x2 = x[..., :half], x[..., half:]
+        return np.concatenate([x1 * c - x2 * s, x2 * c + x1 * s], axis=-1)
+
+    def step_linears(self, x):
+        for b in self.blocks:
+            q = self._lin(x, b["q_proj"])
+            self._lin(x, b["k_proj"])
+            self._lin(x, b["v_proj"])
+            o = self._lin(q, b["o_proj"])
+            self._lin(o, b["gate_proj"])
+            u = self._lin(o, b["up_proj"])
+            x = self._lin(u, b["down_proj"])
+        return x
+
+    def step(self, token):
+        """One greedy token (numpy int) -> the next token."""
+        np = self.np
+        if self.linears_only:
+            return self.step_linears(np.ones((1, self.h), np.float32))
+        p = self.pos
+        x = self.embed[token][None, :].copy()
+        g = self.heads // self.kv
+        for li, b in enumerate(self.blocks):
+            y = self._rms(x)
+            q = self._lin(y, b["q_proj"]).reshape(self.heads, self.hd)
+            k = self._lin(y, b["k_proj"]).reshape(self.kv, self.hd)
+            v = self._lin(y, b["v_proj"]).reshape(self.kv, self.hd)
+            if self.qk_norm:
+                q, k = self._rms(q), self._rms(k)
+            q, k = self._rope(q, p), self._rope(k, p)
+            self.kc[li, p], self.vc[li, p] = k, v
+            keys, vals = self.kc[li, :p + 1], self.vc[li, :p + 1]          # [T, kv, hd]
+            qg = q.reshape(self.kv, g, self.hd)
+            s = np.einsum("kgd,tkd->kgt", qg, keys) / np.sqrt(self.hd)
+            s = np.exp(s - s.max(-1, keepdims=True))
+            s /= s.sum(-1, keepdims=True)
+            att = np.einsum("kgt,tkd->kgd", s, vals).reshape(1, -1)
+            x = x + self._lin(att, b["o_proj"])
+            y = self._rms(x)
+            gt, up = self._lin(y, b["gate_proj"]), self._lin(y, b["up_proj"])
+            x = x + self._lin(gt / (1.0 + np.exp(-gt)) * up, b["down_proj"])
+        logits = self.lm_head @ self._rms(x)[0]
+        self.pos = p + 1 if p + 1 < self.kc.shape[1] else PROMPT
+        return int(np.argmax(logits))
+
+
+def cpu_reference(shape, layers, threads, steps=None, seconds=None, warmup=1, linears_only=False):
+    """(seconds per step list, decoder): timed steps of CpuReferenceDecoder."""
+    dec = CpuReferenceDecoder(shape, layers, threads, linears_only=linears_only,
+                              max_len=PROMPT + warmup + (steps or 64) + 2)
+    tok = 1
     for _ in range(warmup):
-        one_layer()
-    times = []
-    t_total = time.perf_counter()
+        tok = dec.step(tok)
+    times, t_all = [], time.perf_counter()
     while True:
         t0 = time.perf_counter()
-        one_layer()
+        tok = dec.step(tok)
         times.append(time.perf_counter() - t0)
-        if steps is not None:
-            if len(times) >= steps:
-                break
-        elif time.perf_counter() - t_total >= seconds:
+        if steps is not None and len(times) >= steps:
             break
-    per_layer = statistics.median(times)
-    tok_s = 1.0 / (per_layer * shapes.layers)
-    used = threads if threads > 0 else O.c_threads()
-    info = {"cores": used, "kind": "port",
-            "sample": f"1 of {shapes.layers} {model} layers (7 linears, f32 activations), "
-                      f"{len(times)} timed repetitions, median {per_layer*1e3:.1f} ms/layer; "
-                      f"tok/s = 1/({shapes.layers} x layer)"}
-    return tok_s, info
+        if seconds is not None and time.perf_counter() - t_all >= seconds:
+            break
+    return times, dec
 
 
 def run_reference(args, rank, world):
+    """The reference arm: rank 0 times the reference's CPU path on every host thread."""
     if rank != 0:
         return 0
-    tok_s, info = cpu_reference_sample(steps=args.steps, warmup=args.warmup, model=args.model)
+    threads = host_threads()
+    os.environ["OMP_NUM_THREADS"] = str(threads)
+    shape = SHAPES[args.model]
+    if args.mode == "model":
+        layers = args.layers or shape[1]
+        times, _ = cpu_reference(shape, layers, threads, steps=args.steps, warmup=args.warmup)
+        per_tok = sum(times) / len(times)
+        sample = (f"whole {args.model} decode tokens ({layers} layers, all {7 * layers} packed linears "
+                  f"+ attention, norms, lm_head) on {threads} threads, {len(times)} timed steps")
+    else:
+        total = args.layers or shape[1]
+        layers = min(8, total)
+        times, _ = cpu_reference(shape, layers, threads, steps=args.steps, warmup=args.warmup,
+                                 linears_only=True)
+        scale = total / layers
+        per_tok = scale * sum(times) / len(times)
+        sample = (f"{args.model} packed linears of {layers} of {total} layers per step on {threads} "
+                  f"threads ({len(times)} timed steps); tok/s = 1 / ({scale:g} x step time)")
+    tok_s = 1.0 / per_tok
+    _, cfg = workload(args, world)
     line = {
         "impl": "reference", "metric": METRIC, "value": round(tok_s, 4), "unit": UNIT,
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(1000.0 / tok_s, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "global_batch": 1, "parallelism": "host threads",
-                   "l2": "n/a (CPU)"},
-        "cpu_baseline": {"value": round(tok_s, 4), "unit": UNIT, **info},
-        "e2e": {"value": round(tok_s, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 0},
+        "n_gpus": world, "steps": len(times), "warmup": args.warmup,
+        "ms_per_step": round(1000.0 * sum(times) / len(times), 3), "higher_is_better": True,
+        "scaling": "weak" if args.mode == "model" else "strong", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic", "config": cfg,
+        "cpu_baseline": {"value": round(tok_s, 4), "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(tok_s, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
 
 
 # ---------------------------------------------------------------------------
-# our arm
+# other workloads
 # ---------------------------------------------------------------------------
 def time_fallback(stack, x, steps):
     """The reference's GPU path without its Triton kernel, on the same step.
@@ -468,105 +606,183 @@ def run_embedding(args, rank, world, local_rank):
         }), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# our arm: the whole-model decode token (the headline)
+# ---------------------------------------------------------------------------
+def _max_over_ranks(vals, dev, world):
+    if world == 1:
+        return vals
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor(vals, dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(v) for v in t]
+
+
+def _timed_replays(fn, steps, dev, stream, clocks_index=None):
+    """CUDA-event time (ms) of ``steps`` calls of fn() on ``stream``, bracketed by syncs."""
+    import torch
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(clocks_index) if clocks_index is not None else None
+    if sampler:
+        sampler.__enter__()
+    e0.record(stream)
+    for _ in range(steps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    if sampler:
+        sampler.__exit__()
+    return e0.elapsed_time(e1), (sampler.summary() if sampler else None)
+
+
 def run_model(args, rank, world, local_rank):
-    """Greedy decode of the whole model (epure.model.PackedDecoder): packed linears
-    through libepq.so, attention / norms / RoPE / SwiGLU / lm_head in torch, one
-    CUDA graph per token (argmax and position update included)."""
+    """Greedy decode of the whole model (epure.model.PackedDecoder), one CUDA graph per token."""
     import torch
     import torch.distributed as dist
     from epure import synthetic
+    from epure.decode import GraphedLinearStack
     from epure.model import PackedDecoder
     from epure.synthetic import store_bytes
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     shapes = synthetic.SHAPES[args.model]
-    prompt_len = 128
-    max_len = prompt_len + args.warmup + args.steps + 2
+    max_len = PROMPT + args.warmup + args.steps + 2
     dec = PackedDecoder(shapes, layers=args.layers, device=dev, seed=1000 * rank, max_len=max_len,
                         fp32_logits=False, gpu_layout=args.layout).capture()
     g = torch.Generator().manual_seed(rank)
-    prompt = torch.randint(0, shapes.vocab, (prompt_len,), generator=g)
+    prompt = torch.randint(0, shapes.vocab, (PROMPT,), generator=g)
+    stream = torch.cuda.current_stream(dev)
 
     def restart():
         first = int(torch.argmax(dec.prefill(prompt)))
         dec.tok.fill_(first)
-        dec.pos.fill_(prompt_len)
+        dec.pos.fill_(PROMPT)
         torch.cuda.synchronize(dev)
 
+    # device-resident: K replays of the token graph; the next token stays on the device
     restart()
     for _ in range(args.warmup):
         dec._graph.replay()
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
-    stream = torch.cuda.current_stream(dev)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local_rank) as clocks:
-        ev0.record(stream)
-        for _ in range(args.steps):
-            dec._graph.replay()
-        ev1.record(stream)
-        torch.cuda.synchronize(dev)
-    ms = ev0.elapsed_time(ev1) / args.steps
-    # end to end: each token goes from pinned host memory into the graph's input
-    # and the next token is read back to the host, every step
-    restart()
+    ms, clocks = _timed_replays(dec._graph.replay, args.steps, dev, stream, local_rank)
+    if world > 1:
+        dist.barrier()
+
+    # end to end through the public greedy step: the token in from pinned host
+    # memory, the graph, the next token back to the host, every step
     th = torch.empty(1, dtype=torch.long, pin_memory=True)
-    th.copy_(dec.tok.cpu())
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
+
+    def e2e_step():
         dec.tok.copy_(th, non_blocking=True)
         dec._graph.replay()
         th.copy_(dec.tok, non_blocking=True)
         stream.synchronize()
-    e1.record(stream)
-    torch.cuda.synchronize(dev)
-    e2e_ms = e0.elapsed_time(e1) / args.steps
+
+    restart()
+    th.copy_(dec.tok.cpu())
+    for _ in range(args.warmup):
+        e2e_step()
+    restart()
+    th.copy_(dec.tok.cpu())
     if world > 1:
-        t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, e2e_ms = float(t[0]), float(t[1])
-    # algorithmic bytes of one token: packed stores, lm_head, one embedding row, and
-    # the K/V of the positions attended (averaged over the timed steps)
+        dist.barrier()
+    t0 = time.perf_counter()
+    e2e_ms, _ = _timed_replays(e2e_step, args.steps, dev, stream)
+    e2e_ms = max(e2e_ms, (time.perf_counter() - t0) * 1e3)
+
+    # the dominant kernel alone: the token's packed launches (gemv_mma_kernel) in one graph
+    lin = GraphedLinearStack(dec.stack, m=1, dtype=torch.bfloat16, device=dev).capture()
+    lin.x.copy_(torch.randn(lin.x.shape, generator=torch.Generator(device=dev).manual_seed(rank),
+                            device=dev).to(torch.bfloat16))
+    for _ in range(args.warmup):
+        lin.replay()
+    lin_ms, _ = _timed_replays(lin.replay, args.steps, dev, torch.cuda.current_stream(dev))
+    ms, e2e_ms, lin_ms = _max_over_ranks([ms / args.steps, e2e_ms / args.steps, lin_ms / args.steps],
+                                         dev, world)
+
     packed = sum(store_bytes(st) for b in dec.stack.blocks for st in b.values())
     lm = dec.lm_head.numel() * dec.lm_head.element_size()
-    pos_avg = prompt_len + args.warmup + args.steps / 2
+    pos_avg = PROMPT + args.warmup + args.steps / 2
     kv = 2 * dec.layers * pos_avg * shapes.kv_heads * shapes.head_dim * 2
-    step_bytes = int(packed + lm + shapes.hidden * 2 + kv)
+    token_bytes = int(packed + lm + shapes.hidden * 2 + kv)
+    lin_bytes = dec.stack.algorithmic_bytes(m=1, act_bytes=2)
     hbm_peak, peak_kind = _peaks()
-    achieved = step_bytes / (ms * 1e-3) / 1e9
+    lin_gbs = lin_bytes / (lin_ms * 1e-3) / 1e9
+    tok_gbs = token_bytes / (ms * 1e-3) / 1e9
+    full = args.model == "llama3-8b" and dec.layers == shapes.layers
     if rank == 0:
-        layers_note = (f" (first {dec.layers} of {shapes.layers} layers)"
-                       if dec.layers != shapes.layers else "")
+        name, cfg = workload(args, world)
+        cfg.update({"layout": args.layout, "bytes_per_step": token_bytes,
+                    "bytes_split": {"packed": packed, "lm_head": lm, "kv": int(kv),
+                                    "embedding_row": shapes.hidden * 2}})
         line = {
-            "metric": f"greedy decode tok/s bs1 @{args.model} (whole model: packed linears + "
-                      "attention, norms, lm_head)",
+            "metric": METRIC,
             "value": round(world * 1000.0 / ms, 2), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic",
-            "config": {"workload": f"{args.model} greedy decode after a {prompt_len}-token prompt"
-                                   + layers_note, "layout": args.layout,
-                       "mode": "model", "global_batch": world, "seq_len": max_len,
-                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                       "l2": f"inputs larger than L2 ({step_bytes / 1e9:.2f} GB moved per step)",
-                       "bytes_per_step": step_bytes,
-                       "bytes_split": {"packed": packed, "lm_head": lm, "kv": int(kv)}},
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak,
-                         "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
-                         "peak_kind": peak_kind,
-                         "kernel": ("whole token graph: " + ("gemv_mma_kernel" if args.layout == "mma16"
-                                                              else "gemv_lut_kernel") +
-                                    " (packed) + decode glue kernels + cuBLAS lm_head"),
-                         "traffic": None},
+            "data": "synthetic (seeded random weights in the benchmark format; uniform random prompt ids)",
+            "config": cfg,
+            "roofline": {"bound": "hbm", "achieved": round(lin_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(lin_gbs / hbm_peak, 4), "peak_kind": peak_kind,
+                         "kernel": "gemv_mma_kernel (the token's packed launches replayed alone)",
+                         "launches": 4 * dec.layers, "launch_avg_us": round(lin_ms * 1e3 / (4 * dec.layers), 3),
+                         "bytes_per_launch_avg": int(lin_bytes / (4 * dec.layers)),
+                         "traffic": int(lin_bytes * NCU_TRAFFIC_RATIO["per-linear"]) if full else None,
+                         "traffic_note": "ncu dram bytes / algorithmic bytes of one gate+up launch (profiles/), "
+                                         "times the token's packed bytes"},
+            "token_roofline": {"bound": "hbm", "bytes_per_token": token_bytes, "achieved": round(tok_gbs, 1),
+                               "peak": hbm_peak, "unit": "GB/s", "frac": round(tok_gbs / hbm_peak, 4),
+                               "roofline_tok_s": round(hbm_peak * 1e9 / token_bytes, 1)},
             "e2e": {"value": round(world * 1000.0 / e2e_ms, 2), "unit": UNIT,
                     "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8},
-            "gpu_launches": 4 * dec.layers * args.steps,
-            "clocks": clocks.summary(),
+            "gpu_launches": (5 * dec.layers + 2) * args.steps,
+            "clocks": clocks,
         }
+        if world == 1 and not args.no_cpu_baseline:
+            threads = host_threads()
+            times, _ = cpu_reference(SHAPES[args.model], dec.layers, threads, seconds=args.cpu_seconds)
+            per = sum(times) / len(times)
+            line["cpu_baseline"] = {
+                "value": round(1.0 / per, 4), "unit": UNIT, "cores": threads, "kind": "port",
+                "sample": f"{len(times)} whole decode tokens ({dec.layers} layers: packed linears through the "
+                          f"lib.rs restatement, the rest numpy) in ~{args.cpu_seconds:g} s"}
         print(json.dumps(line), flush=True)
+    return 0
+
+
+def tp_check(shapes, rank, world, dev, layers=2):
+    """Max relative error of the tensor-parallel chain against the single-GPU chain
+    on a ``layers``-layer, full-width slice of one seeded model (fp32 outputs)."""
+    import torch
+    import torch.distributed as dist
+    from epure import _native, synthetic
+    from epure.decode import ChainedLinearStack
+    from epure.tp import TPChainedLinearStack, shard_blocks
+
+    full = synthetic.LinearStack(shapes, layers=layers, device=dev, seed=4242, gpu_layout="tiled")
+    shards = synthetic.LinearStack.from_blocks(shapes, shard_blocks(full.blocks, rank, world, device=dev), dev)
+    runner = TPChainedLinearStack(shards, dtype=torch.bfloat16, device=dev)
+    x = torch.randn(1, shapes.hidden, generator=torch.Generator(device=dev).manual_seed(7),
+                    device=dev).to(torch.bfloat16)
+    got = torch.zeros(1, shapes.hidden, dtype=torch.float32, device=dev)
+    _native.chain_run(runner.ws, x, got)
+    torch.cuda.synchronize(dev)
+    err = torch.zeros(1, dtype=torch.float64, device=dev)
+    if rank == 0:
+        one = ChainedLinearStack(full, device=dev)
+        want = torch.zeros_like(got)
+        _native.chain_run(one.ws, x, want)
+        torch.cuda.synchronize(dev)
+        err[0] = float((got - want).abs().max() / want.abs().max())
+    dist.broadcast(err, 0)
+    dist.barrier()
+    runner.release()
+    return float(err[0])
 
 
 def run_ours(args, rank, world, local_rank):
@@ -582,6 +798,15 @@ def run_ours(args, rank, world, local_rank):
     chain = args.mode == "chain"
     prefill = args.mode == "prefill"
     m = args.tokens if prefill else args.batch
+    check = None
+    if use_tp and chain:
+        err = tp_check(shapes, rank, world, dev)
+        check = {"what": "TP chain vs the single-GPU chain, 2 layers of the same seeded model at full width, "
+                         "fp32 outputs", "max_rel_err": err, "bound": 1e-4, "ok": err <= 1e-4}
+        if not check["ok"]:
+            if rank == 0:
+                print(json.dumps({"metric": METRIC, "error": "tp_check failed", "tp_check": check}), flush=True)
+            return 1
     if use_tp:
         # every rank draws its own shards of one model (same seed on every rank)
         stack = synthetic.LinearStack(shapes, layers=args.layers, device=dev, seed=1000,
@@ -666,14 +891,13 @@ def run_ours(args, rank, world, local_rank):
 
     hbm_peak, peak_kind = _peaks()
     achieved_gbs = step_bytes / (ms * 1e-3) / 1e9
-    workload = WORKLOAD.replace("llama3-8b", args.model).replace(
-        "224 linears", f"{7 * stack.layers} linears")
+    workload_name = f"{args.model} packed linears, batch-1 decode token ({7 * stack.layers} linears)"
     if prefill:
-        workload = workload.replace("batch-1 decode token", f"{m}-token prefill")
+        workload_name = workload_name.replace("batch-1 decode token", f"{m}-token prefill")
     elif m > 1:
-        workload = workload.replace("batch-1 decode token", f"batch-{m} decode step ({m} tokens)")
+        workload_name = workload_name.replace("batch-1 decode token", f"batch-{m} decode step ({m} tokens)")
     if stack.layers != shapes.layers:
-        workload += f" (first {stack.layers} of {shapes.layers} layers)"
+        workload_name += f" (first {stack.layers} of {shapes.layers} layers)"
     if prefill:
         tf_peak, tf_kind = _tensor_peak()
         achieved_tf = step_flops / (ms * 1e-3) / 1e12
@@ -691,7 +915,9 @@ def run_ours(args, rank, world, local_rank):
                     "traffic": (int(step_bytes * NCU_TRAFFIC_RATIO[args.mode])
                                 if NCU_TRAFFIC_RATIO.get(args.mode) and stack.layers == 32
                                 and args.model == "llama3-8b" and m == 1 else None),
-                    "traffic_note": TRAFFIC_NOTE.get(args.mode)}
+                    "traffic_note": ("per step, scaled from one ncu capture (profiles/): dram bytes / "
+                                     "algorithmic bytes of the " + ("4-layer chain" if chain else "gate+up launch")
+                                     if NCU_TRAFFIC_RATIO.get(args.mode) else None)}
     streams = 1 if use_tp else world          # independent token streams across the job
     if use_tp:
         # aggregate over the ranks: each streams its shard bytes in the same step time
@@ -721,7 +947,7 @@ def run_ours(args, rank, world, local_rank):
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic",
-            "config": {"workload": workload,
+            "config": {"workload": workload_name,
                        "mode": ("tp-" + args.mode) if use_tp else args.mode,
                        "global_batch": streams * m,
                        "seq_len": m,
@@ -737,11 +963,22 @@ def run_ours(args, rank, world, local_rank):
             "gpu_launches": launches * args.steps,
             "clocks": clocks.summary(),
         }
+        if check is not None:
+            line["tp_check"] = check
+            _, line["config"] = workload(args, world)
+            line["config"].update({"bytes_per_step": step_bytes, "flops_per_step": step_flops})
+            line["metric"] = METRIC + f" (tensor-parallel {args.model} packed linears over {world} GPUs)"
         if args.fallback:
             line["fallback"] = time_fallback(stack, runner.x, steps=max(1, min(args.steps, 3)))
-        if world == 1 and not args.no_cpu_baseline and args.mode != "prefill":
-            tok_s, info = cpu_reference_sample(seconds=args.cpu_seconds, model=args.model)
-            line["cpu_baseline"] = {"value": round(tok_s, 4), "unit": UNIT, **info}
+        if world == 1 and not args.no_cpu_baseline and args.mode != "prefill" and m == 1:
+            threads = host_threads()
+            times, _ = cpu_reference(SHAPES[args.model], stack.layers, threads, seconds=args.cpu_seconds,
+                                     linears_only=True)
+            per = sum(times) / len(times)
+            line["cpu_baseline"] = {
+                "value": round(1.0 / per, 4), "unit": UNIT, "cores": threads, "kind": "port",
+                "sample": f"{len(times)} tokens of the {7 * stack.layers} packed linears through the lib.rs "
+                          f"restatement in ~{args.cpu_seconds:g} s"}
         print(json.dumps(line), flush=True)
     if use_tp:
         runner.release()        # the graph holds NCCL work: drop it before the group goes
@@ -752,14 +989,14 @@ def run_ours(args, rank, world, local_rank):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--mode", choices=["chain", "per-linear", "prefill", "finetune", "model", "embedding"],
-                    default="chain")
-    ap.add_argument("--model", choices=["qwen3-1.7b", "llama3-8b", "llama3-70b"], default=None)
+    ap.add_argument("--mode", choices=["model", "chain", "per-linear", "prefill", "finetune", "embedding"],
+                    default=None, help="default: model at N = 1 (and with --replicas), tensor-parallel chain at N > 1")
+    ap.add_argument("--model", choices=sorted(SHAPES), default=None)
     ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--tokens", type=int, default=None)
     ap.add_argument("--batch", type=int, default=1,
@@ -769,23 +1006,29 @@ def main():
                     help="--mode model: index layout of the packed stores (tensor-core GEMV or LUT GEMV "
                          "at batch 1)")
     ap.add_argument("--tp", action="store_true",
-                    help="at N > 1: one model tensor-parallel over the N GPUs instead of N replicas")
+                    help="at N > 1 with --mode chain / per-linear: one model tensor-parallel over the N GPUs")
+    ap.add_argument("--replicas", action="store_true",
+                    help="at N > 1: N independent copies of the N = 1 workload instead of tensor parallelism")
     ap.add_argument("--fallback", action="store_true",
                     help="also time the reference's bf16 fallback path on the same step (GPU)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    args.model_set = args.model is not None
-    if args.model is None:
-        args.model = "qwen3-1.7b" if args.mode == "finetune" else "llama3-8b"
-    if args.tokens is None:
-        args.tokens = 8 * 2048 if args.mode == "finetune" else 2048
-    if args.batch != 1 and args.mode != "per-linear":
-        ap.error("--batch applies to --mode per-linear (the chain kernel is batch-1)")
-
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.mode is None:
+        if world > 1 and not args.replicas:
+            args.mode, args.tp = "chain", True
+        else:
+            args.mode = "model"
+    if args.model is None:
+        args.model = ("qwen3-1.7b" if args.mode == "finetune" else
+                      "llama3-70b" if (args.tp and world > 1) else "llama3-8b")
+    if args.tokens is None:
+        args.tokens = 8 * 2048 if args.mode == "finetune" else 2048
+    if args.batch != 1 and args.mode != "per-linear":
+        ap.error("--batch applies to --mode per-linear")
 
     if args.impl == "reference":
         return run_reference(args, rank, world)
