@@ -37,6 +37,27 @@ __device__ __forceinline__ void pdl_enter() {
 }
 
 template <typename... KArgs, typename... Args>
+int launch_pdl_cluster(void (*kern)(KArgs...), dim3 grid, dim3 block, unsigned cluster_x, cudaStream_t st,
+                       const char* what, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = cluster_x;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+    return check_launch(what);
+}
+
+template <typename... KArgs, typename... Args>
 int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, const char* what,
                Args... args) {
     cudaLaunchConfig_t cfg = {};
@@ -471,6 +492,168 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_rope_split_kernel(
     if (threadIdx.x == 0) counters[kvh] = 0u;
 }
 
+// Decode attention as thread-block clusters: the kClusterSplits CTAs of one
+// cluster split the positions of one kv head, and their partial softmax
+// records are merged over distributed shared memory by the cluster's rank 0
+// (no workspace round trip, fence or completion counter).  Otherwise as
+// attn_rope_split_kernel: (q/k RMSNorm and) RoPE inside, this position's k / v
+// from registers and written into the caches by rank 0; each warp prefetches
+// the K / V rows of its next position while it scores the current one.
+constexpr int kClusterSplits = 8;
+
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float ld_cluster_f32(const float* local, uint32_t rank) {
+    uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(local)), r;
+    float v;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(r) : "memory");
+    return v;
+}
+
+template <int kDims, int kGroup>
+__global__ void __launch_bounds__(kAttnWarps * 32) attn_rope_cluster_kernel(
+    const __nv_bfloat16* __restrict__ q_in, const __nv_bfloat16* __restrict__ k_in,
+    const __nv_bfloat16* __restrict__ v_in, __nv_bfloat16* __restrict__ k_cache,
+    __nv_bfloat16* __restrict__ v_cache, const int64_t* __restrict__ pos, int KV,
+    const float* __restrict__ cos_t, const float* __restrict__ sin_t, int qk_norm, float eps, float scale,
+    __nv_bfloat16* __restrict__ out, int64_t max_len) {
+    pdl_enter();
+    constexpr int hd = kDims * 32;
+    constexpr int kRec = hd + 2;                   // merged acc[hd], max, sum of one head
+    __shared__ float wm[kAttnWarps][kGroup], wl[kAttnWarps][kGroup];
+    __shared__ float wacc[kAttnWarps][kGroup][hd];
+    __shared__ float rec[kGroup * kRec];            // this CTA's record, read by rank 0
+    const int split = blockIdx.x, kvh = blockIdx.y;   // the cluster spans the splits of one kv head
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t P = pos[0];
+    if (P < 0 || P >= max_len) {   // the same position for every CTA: the whole cluster returns here
+        if (split == 0) {
+            for (int e = threadIdx.x; e < kGroup * hd; e += kAttnWarps * 32)
+                out[(int64_t)kvh * kGroup * hd + e] = __float2bfloat16_rn(0.f);
+            if (threadIdx.x == 0) atomicExch(&g_glue_position_error, 1);
+        }
+        return;
+    }
+    const int64_t n = P + 1;
+    const int64_t chunk = (n + kClusterSplits - 1) / kClusterSplits;
+    const int64_t t0 = split * chunk, t1 = min(n, t0 + chunk);
+    // the cached rows this warp will read first, issued before anything else
+    auto load_row = [&](int64_t t, float (&kr)[kDims], float (&vr)[kDims]) {
+        const int64_t kb = (t * KV + kvh) * hd + lane * kDims;
+#pragma unroll
+        for (int d = 0; d < kDims; ++d) {
+            kr[d] = __bfloat162float(k_cache[kb + d]);
+            vr[d] = __bfloat162float(v_cache[kb + d]);
+        }
+    };
+    float kn[kDims], vn[kDims];
+    int64_t t = t0 + warp;
+    if (t < t1 && t != P) load_row(t, kn, vn);
+    float qv[kGroup][kDims], acc[kGroup][kDims], m[kGroup], l[kGroup];
+#pragma unroll
+    for (int g = 0; g < kGroup; ++g) {
+        m[g] = -INFINITY;
+        l[g] = 0.f;
+#pragma unroll
+        for (int d = 0; d < kDims; ++d) {
+            qv[g][d] = __bfloat162float(q_in[(int64_t)(kvh * kGroup + g) * hd + lane * kDims + d]);
+            acc[g][d] = 0.f;
+        }
+        rope_head<kDims>(qv[g], lane, P, cos_t, sin_t, qk_norm, eps);
+    }
+    float kc[kDims], vc[kDims];
+#pragma unroll
+    for (int d = 0; d < kDims; ++d) {
+        kc[d] = __bfloat162float(k_in[(int64_t)kvh * hd + lane * kDims + d]);
+        vc[d] = __bfloat162float(v_in[(int64_t)kvh * hd + lane * kDims + d]);
+    }
+    rope_head<kDims>(kc, lane, P, cos_t, sin_t, qk_norm, eps);
+    if (split == 0 && warp == 0) {
+        const int64_t cb = (P * KV + kvh) * hd + lane * kDims;
+#pragma unroll
+        for (int d = 0; d < kDims; ++d) {
+            k_cache[cb + d] = __float2bfloat16_rn(kc[d]);
+            v_cache[cb + d] = __float2bfloat16_rn(vc[d]);
+        }
+    }
+    for (; t < t1; t += kAttnWarps) {
+        float kr[kDims], vr[kDims];
+#pragma unroll
+        for (int d = 0; d < kDims; ++d) {
+            kr[d] = t == P ? kc[d] : kn[d];
+            vr[d] = t == P ? vc[d] : vn[d];
+        }
+        const int64_t tn = t + kAttnWarps;
+        if (tn < t1 && tn != P) load_row(tn, kn, vn);   // next row in flight while this one is scored
+#pragma unroll
+        for (int g = 0; g < kGroup; ++g) {
+            float sc = 0.f;
+#pragma unroll
+            for (int d = 0; d < kDims; ++d) sc += qv[g][d] * kr[d];
+            for (int o = 16; o > 0; o >>= 1) sc += __shfl_xor_sync(0xffffffffu, sc, o);
+            sc *= scale;
+            const float mn = fmaxf(m[g], sc);
+            const float corr = expf(m[g] - mn), pw = expf(sc - mn);
+            l[g] = l[g] * corr + pw;
+#pragma unroll
+            for (int d = 0; d < kDims; ++d) acc[g][d] = acc[g][d] * corr + pw * vr[d];
+            m[g] = mn;
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < kGroup; ++g) {
+        if (lane == 0) {
+            wm[warp][g] = m[g];
+            wl[warp][g] = l[g];
+        }
+#pragma unroll
+        for (int d = 0; d < kDims; ++d) wacc[warp][g][lane * kDims + d] = acc[g][d];
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < kGroup * hd; e += kAttnWarps * 32) {
+        const int g = e / hd, d = e - g * hd;
+        float mx = -INFINITY;
+        for (int w = 0; w < kAttnWarps; ++w) mx = fmaxf(mx, wm[w][g]);
+        float num = 0.f, den = 0.f;
+        for (int w = 0; w < kAttnWarps; ++w) {
+            if (wm[w][g] == -INFINITY) continue;
+            const float f = expf(wm[w][g] - mx);
+            num += f * wacc[w][g][d];
+            den += f * wl[w][g];
+        }
+        rec[g * kRec + d] = num;
+        if (d == 0) {
+            rec[g * kRec + hd] = mx;
+            rec[g * kRec + hd + 1] = den;
+        }
+    }
+    cluster_sync_all();   // every split's record is in its shared memory
+    if (split == 0) {
+        for (int e = threadIdx.x; e < kGroup * hd; e += kAttnWarps * 32) {
+            const int g = e / hd, d = e - g * hd;
+            float mxs[kClusterSplits];
+            float mx = -INFINITY;
+#pragma unroll
+            for (int r = 0; r < kClusterSplits; ++r) {
+                mxs[r] = ld_cluster_f32(&rec[g * kRec + hd], (uint32_t)r);
+                mx = fmaxf(mx, mxs[r]);
+            }
+            float num = 0.f, den = 0.f;
+#pragma unroll
+            for (int r = 0; r < kClusterSplits; ++r) {
+                if (mxs[r] == -INFINITY) continue;   // a split that saw no position
+                const float f = expf(mxs[r] - mx);
+                num += f * ld_cluster_f32(&rec[g * kRec + d], (uint32_t)r);
+                den += f * ld_cluster_f32(&rec[g * kRec + hd + 1], (uint32_t)r);
+            }
+            out[(int64_t)(kvh * kGroup + g) * hd + d] = __float2bfloat16_rn(num / den);
+        }
+    }
+    cluster_sync_all();   // no CTA leaves while rank 0 still reads its record
+}
+
 // Arg-max of n floats (first index of the maximum, as torch.argmax): every CTA
 // reduces a strided share, the last CTA to finish merges the per-CTA results.
 constexpr int kArgBlocks = 64;
@@ -724,19 +907,17 @@ int epq_attn_rope_decode(const void* q, const void* k, const void* v, const int6
                          (long long)workspace_bytes,
                          (long long)epq_attn_decode_workspace_bytes(heads, kv_heads, head_dim));
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    unsigned* ctr = static_cast<unsigned*>(workspace);
-    float* ws = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + 256);
     const auto* qb = static_cast<const __nv_bfloat16*>(q);
     const auto* kb = static_cast<const __nv_bfloat16*>(k);
     const auto* vb = static_cast<const __nv_bfloat16*>(v);
     auto* kcb = static_cast<__nv_bfloat16*>(k_cache);
     auto* vcb = static_cast<__nv_bfloat16*>(v_cache);
     auto* ob = static_cast<__nv_bfloat16*>(out);
-    const dim3 grid(kv_heads, kAttnSplits);
-#define EPQ_ATTN_ROPE(D, G)                                                                                 \
-    return launch_pdl(attn_rope_split_kernel<D, G>, grid, dim3(kAttnWarps * 32), 0, st, "epq_attn_rope_decode", \
-                      qb, kb, vb, kcb, vcb, pos, (int)kv_heads, cos_tab, sin_tab, (int)qk_norm, eps, scale, ob, ws, ctr, \
-                      max_len)
+    const dim3 grid(kClusterSplits, kv_heads);
+#define EPQ_ATTN_ROPE(D, G)                                                                                     \
+    return launch_pdl_cluster(attn_rope_cluster_kernel<D, G>, grid, dim3(kAttnWarps * 32), kClusterSplits, st, \
+                              "epq_attn_rope_decode", qb, kb, vb, kcb, vcb, pos, (int)kv_heads, cos_tab, sin_tab,  \
+                              (int)qk_norm, eps, scale, ob, max_len)
     if (head_dim == 128) {
         if (group == 1) EPQ_ATTN_ROPE(4, 1);
         if (group == 2) EPQ_ATTN_ROPE(4, 2);

@@ -23,10 +23,11 @@
 //   ({2q, 2q+1, 2q+8, 2q+9}) are the four weights of ONE codebook vector: a
 //   thread's A fragment for a row is one 8-byte codebook entry (one 64-bit
 //   shared load) times the row's scale (two packed multiplies).
-// * The codebook is replicated 32 times in shared memory (entry e, copy c at
-//   byte e * 256 + c * 8) and lane l reads copy l: one byte permute forms the
-//   gather address, and the 32 lanes' random gathers fill every bank pair
-//   exactly twice (the 2-wavefront minimum of a 256-byte request).
+// * The codebook is replicated 16 times in shared memory at a 64 KiB-aligned
+//   window address (entry e, copy c at e * 256 + c * 8; the other half of each
+//   256-byte row holds the second store of a paired launch) and lane l reads
+//   copy l % 16: one byte permute forms the gather's whole address, and a
+//   half-warp's random gathers never share a bank pair.
 // * Activations are staged in shared memory in the B-fragment order of two
 //   consecutive k-steps per 16-byte word: one 128-bit load feeds two MMAs, and
 //   the four lanes of a row read one contiguous 64-byte run (no conflicts).
@@ -34,7 +35,7 @@
 //   lane 4*r + q holds the indices of rows r and r + 8 at positions q + 4s,
 //   s = 0..7.  Tiles run group-fastest, so the groups of one 16-row block are
 //   one contiguous run.
-// * A producer warp streams 32-group chunks through a 4-stage shared-memory
+// * A producer warp streams 32-group chunks through a 3-stage shared-memory
 //   ring guarded by mbarriers, two copies per chunk into this CTA's shared
 //   memory only: the index tiles (cp.async.bulk, one contiguous run) and the
 //   chunk's 16 x 32 scales (one 2-D cp.async.bulk.tensor box over the
@@ -68,15 +69,25 @@ namespace {
 constexpr int kConsumerWarps = 16;
 constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kThreads = kConsumers + 32;       // + one producer warp
-constexpr int kStages = 4;
+constexpr int kStages = 3;
 constexpr int kSlots = kStages + 1;             // unit reduction slots (see the ring argument below)
 constexpr int kChunkGroups = 32;                // groups per chunk
 constexpr int kStageIdx = kChunkGroups * 512;   // 16 KB of index tiles
 constexpr int kStageBytes = kStageIdx + kChunkGroups * 64;
-constexpr int kReplicaBytes = 256 * 32 * 8;     // 256 entries x 32 copies x 8 B
 constexpr int kBarBytes = 256;                  // mbarriers + slot counters
 constexpr int kMaxXSmem = 64 * 1024;            // activations staged in shared memory up to this
 constexpr int kMaxSmem = 227 * 1024;
+// Shared-window layout.  The dynamic block starts at a small window address
+// `base`; the codebook replicas sit at the fixed, 64 KiB-aligned window range
+// [kRepWin, 2 kRepWin): entry e occupies bytes e * 256 + [0, 256), the first
+// 128 the 16 copies of store part 0 (8 B each), the next 128 those of part 1.
+// Because the low 16 bits of kRepWin are zero, one byte permute of an index
+// word and a per-lane constant yields a gather's whole window address.  Below
+// it: mbarriers + counters, then the stage ring (so base + kLowBytes <=
+// kRepWin); above it: the reduction slots, then the staged activations.
+constexpr uint32_t kRepWin = 65536;
+constexpr uint32_t kLowBytes = kBarBytes + kStages * kStageBytes;
+constexpr uint32_t kHighWin = 2 * kRepWin;
 constexpr uint32_t kWaitLimit = 1u << 22;       // bounded mbarrier waits
 
 __device__ int g_mma_wait_timeout = 0;
@@ -222,21 +233,30 @@ __device__ __forceinline__ void pdl_trigger() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
-// Codebook of store S -> 32 interleaved copies in the activation type: entry e,
-// copy c at byte e * 256 + c * 8.  Consumer thread t converts entry t / 2 once
-// and writes 16 of its copies.
+// Codebook of store S -> 16 copies in the activation type in its half (`part`)
+// of the replica block: entry e, copy c at byte e * 256 + part * 128 + c * 8;
+// lane l reads copy l % 16, so a half-warp's random gathers never share a bank
+// pair.  Consumer threads 0..255 first convert one entry each into `stage`
+// (2 KB); after a consumer barrier thread t writes slots t, t + 512, ..., so a
+// warp's 32 stores cover two 128-byte runs (no bank conflicts).
 template <bool kBf16>
-__device__ void build_replica(const MmaStore& S, uint2* rep) {
-    static_assert(kConsumers == 2 * 256, "two consumer threads per codebook entry");
-    const int e = threadIdx.x >> 1, c0 = (threadIdx.x & 1) * 16;
-    uint2 v = make_uint2(0u, 0u);
-    if (e < S.levels) {
-        const int64_t b = (int64_t)e * 4;
-        v.x = cvt_pair<kBf16>(load_f(S.cb, S.cb_dtype, b), load_f(S.cb, S.cb_dtype, b + 1));
-        v.y = cvt_pair<kBf16>(load_f(S.cb, S.cb_dtype, b + 2), load_f(S.cb, S.cb_dtype, b + 3));
+__device__ void build_replica(const MmaStore& S, uint2* rep, int part, uint2* stage) {
+    const int t = threadIdx.x;
+    if (t < 256) {
+        uint2 v = make_uint2(0u, 0u);
+        if (t < S.levels) {
+            const int64_t b = (int64_t)t * 4;
+            v.x = cvt_pair<kBf16>(load_f(S.cb, S.cb_dtype, b), load_f(S.cb, S.cb_dtype, b + 1));
+            v.y = cvt_pair<kBf16>(load_f(S.cb, S.cb_dtype, b + 2), load_f(S.cb, S.cb_dtype, b + 3));
+        }
+        stage[t] = v;
     }
+    consumers_sync();
 #pragma unroll
-    for (int i = 0; i < 16; ++i) rep[e * 32 + c0 + i] = v;
+    for (int i = 0; i < 4096 / kConsumers; ++i) {
+        const int slot = t + i * kConsumers;   // entry slot / 16, copy slot % 16
+        rep[(slot >> 4) * 32 + part * 16 + (slot & 15)] = stage[slot >> 4];
+    }
 }
 
 // kT (1 or 2) tiles of one chunk, interleaved so their gathers and MMAs overlap:
@@ -245,9 +265,9 @@ __device__ void build_replica(const MmaStore& S, uint2* rep) {
 // load no activations (their B columns are never stored).
 template <bool kBf16, int kNT, bool kScaleF32, bool kXSmem, int kT>
 __device__ __forceinline__ void mma_tiles(float (&acc)[2][kNT][4], const uint32_t sdst, const int gl0, const int g0,
-                                          const uint32_t rep_l, const uint32_t xs0, const uint32_t xs1,
+                                          const uint32_t lanebase, const uint32_t xs0, const uint32_t xs1,
                                           const uint16_t* xg0, const uint16_t* xg1, const int k_lane,
-                                          const bool xon0, const bool xon1, const int lane) {
+                                          const int lane) {
     constexpr int kScaleBytes = kScaleF32 ? 4 : 2;
     const int gq = lane >> 2;
     uint32_t wlo[kT][2], whi[kT][2], sc0[kT], sc1[kT];
@@ -265,47 +285,41 @@ __device__ __forceinline__ void mma_tiles(float (&acc)[2][kNT][4], const uint32_
         sc0[t] = cvt_pair<kBf16>(s0, s0);
         sc1[t] = cvt_pair<kBf16>(s1, s1);
     }
-    const uint32_t lanebase = (uint32_t)lane << 3;
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
         uint4 bx[kT], by[kT];
 #pragma unroll
         for (int t = 0; t < kT; ++t) {
             const int gidx = g0 + gl0 + 16 * t;
-            bx[t] = by[t] = make_uint4(0u, 0u, 0u, 0u);
+            // Lanes whose activation row is past m read row m - 1 (their output
+            // columns are never stored), so every lane loads and none is predicated.
             if constexpr (kXSmem) {
-                if (xon0) bx[t] = lds128(xs0 + (gidx * 4 + p) * 64);
-                if constexpr (kNT == 2)
-                    if (xon1) by[t] = lds128(xs1 + (gidx * 4 + p) * 64);
+                bx[t] = lds128(xs0 + (gidx * 4 + p) * 64);
+                if constexpr (kNT == 2) by[t] = lds128(xs1 + (gidx * 4 + p) * 64);
             } else {
                 const int col = gidx * 128 + 32 * p;
-                if (xon0) {
-                    const uint2 z = make_uint2(0u, 0u);
-                    const uint2 b0 = col < k_lane ? __ldg(reinterpret_cast<const uint2*>(xg0 + col)) : z;
-                    const uint2 b1 = col + 16 < k_lane ? __ldg(reinterpret_cast<const uint2*>(xg0 + col + 16)) : z;
-                    bx[t] = make_uint4(b0.x, b0.y, b1.x, b1.y);
-                }
+                const uint2 z = make_uint2(0u, 0u);
+                const uint2 b0 = col < k_lane ? __ldg(reinterpret_cast<const uint2*>(xg0 + col)) : z;
+                const uint2 b1 = col + 16 < k_lane ? __ldg(reinterpret_cast<const uint2*>(xg0 + col + 16)) : z;
+                bx[t] = make_uint4(b0.x, b0.y, b1.x, b1.y);
                 if constexpr (kNT == 2) {
-                    if (xon1) {
-                        const uint2 z = make_uint2(0u, 0u);
-                        const uint2 c0 = col < k_lane ? __ldg(reinterpret_cast<const uint2*>(xg1 + col)) : z;
-                        const uint2 c1 =
-                            col + 16 < k_lane ? __ldg(reinterpret_cast<const uint2*>(xg1 + col + 16)) : z;
-                        by[t] = make_uint4(c0.x, c0.y, c1.x, c1.y);
-                    }
+                    const uint2 c0 = col < k_lane ? __ldg(reinterpret_cast<const uint2*>(xg1 + col)) : z;
+                    const uint2 c1 = col + 16 < k_lane ? __ldg(reinterpret_cast<const uint2*>(xg1 + col + 16)) : z;
+                    by[t] = make_uint4(c0.x, c0.y, c1.x, c1.y);
                 }
             }
         }
 #pragma unroll
         for (int hs = 0; hs < 2; ++hs) {
             const int s = 2 * p + hs;
-            // result byte 0 = lane * 8, byte 1 = index byte s % 4, bytes 2-3 = 0
-            const uint32_t sel = 0x5504u | ((uint32_t)(s & 3) << 4);
+            // window address = byte 0 of lanebase (part * 128 + copy * 8), byte 1
+            // the index (entry * 256), bytes 2-3 of lanebase (kRepWin >> 16)
+            const uint32_t sel = 0x7604u | ((uint32_t)(s & 3) << 4);
             uint2 alo[kT], ahi[kT];
 #pragma unroll
             for (int t = 0; t < kT; ++t) {
-                alo[t] = lds64(rep_l + __byte_perm(wlo[t][s >> 2], lanebase, sel));
-                ahi[t] = lds64(rep_l + __byte_perm(whi[t][s >> 2], lanebase, sel));
+                alo[t] = lds64(__byte_perm(wlo[t][s >> 2], lanebase, sel));
+                ahi[t] = lds64(__byte_perm(whi[t][s >> 2], lanebase, sel));
             }
 #pragma unroll
             for (int t = 0; t < kT; ++t) {
@@ -336,15 +350,18 @@ __device__ __forceinline__ int xperm(int row, int kpad, int col) {
 template <bool kBf16, int kNT, bool kScaleF32, bool kXSmem>
 __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const __grid_constant__ MmaParams P) {
     extern __shared__ __align__(128) uint8_t smem[];
-    const int rep_bytes = P.parts * kReplicaBytes;
-    uint2* rep = reinterpret_cast<uint2*>(smem);
     const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
-    const uint32_t bar_full = sbase + rep_bytes;           // kStages x 8 B
+    if (sbase + kLowBytes > kRepWin) {   // the layout needs the dynamic block to start low (uniform)
+        if (threadIdx.x == 0) atomicExch(&g_mma_wait_timeout, 1);
+        return;
+    }
+    uint2* rep = reinterpret_cast<uint2*>(smem + (kRepWin - sbase));
+    const uint32_t bar_full = sbase;                       // kStages x 8 B
     const uint32_t bar_empty = bar_full + 8 * kStages;     // kStages x 8 B
-    int* cnt = reinterpret_cast<int*>(smem + rep_bytes + 16 * kStages);   // kSlots arrival counters
-    const uint32_t stage0 = sbase + rep_bytes + kBarBytes;
-    float* slots = reinterpret_cast<float*>(smem + rep_bytes + kBarBytes + kStages * kStageBytes);
-    uint16_t* xs = reinterpret_cast<uint16_t*>(smem + P.x_off);   // [m][kpad] when kXSmem
+    int* cnt = reinterpret_cast<int*>(smem + 16 * kStages);   // kSlots arrival counters
+    const uint32_t stage0 = sbase + kBarBytes;
+    float* slots = reinterpret_cast<float*>(smem + (kHighWin - sbase));
+    uint16_t* xs = reinterpret_cast<uint16_t*>(smem + (P.x_off - sbase));   // [m][kpad] when kXSmem
     constexpr int kScaleBytes = kScaleF32 ? 4 : 2;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -414,11 +431,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const __grid_cons
     const int gq = lane >> 2, q = lane & 3;
     int cur = P.parts == 2 ? 0 : store_of(P, u_begin);
     int c_next = (P.parts == 1 && cur + 1 < P.count) ? P.st[cur + 1].unit0 : INT_MAX;
+    uint2* cb_stage = reinterpret_cast<uint2*>(slots);   // 2 KB; slots are free until a unit ends
     if (u_begin < u_end) {
         for (int r = 0; r < P.parts; ++r) {
-            if constexpr (kBf16) build_replica<true>(P.st[P.parts == 2 ? r : cur], rep + r * (256 * 32));
-            else build_replica<false>(P.st[P.parts == 2 ? r : cur], rep + r * (256 * 32));
+            if (r) consumers_sync();   // the staging area is reused
+            if constexpr (kBf16) build_replica<true>(P.st[P.parts == 2 ? r : cur], rep, r, cb_stage);
+            else build_replica<false>(P.st[P.parts == 2 ? r : cur], rep, r, cb_stage);
         }
+        consumers_sync();   // the staging area is the RMSNorm scratch next
     }
     pdl_trigger();
     pdl_wait();   // x (and the output buffers) belong to the previous kernel until here
@@ -480,7 +500,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const __grid_cons
     consumers_sync();
 
     const int k_lane = P.k - 4 * q;   // global-load path: column c is in range iff c < k_lane
-    const bool xon0 = gq < P.m, xon1 = gq + 8 < P.m;
+    const uint32_t lane16 = (kRepWin & 0xffff0000u) | ((uint32_t)(lane & 15) << 3);
     // Two accumulator chains (the two tiles a warp takes per chunk) keep dependent MMAs apart.
     float acc[2][kNT][4];
 #pragma unroll
@@ -496,23 +516,23 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const __grid_cons
             consumers_sync();
             cur = store_of(P, u);
             c_next = cur + 1 < P.count ? P.st[cur + 1].unit0 : INT_MAX;
-            if constexpr (kBf16) build_replica<true>(P.st[cur], rep);
-            else build_replica<false>(P.st[cur], rep);
+            if constexpr (kBf16) build_replica<true>(P.st[cur], rep, 0, cb_stage);
+            else build_replica<false>(P.st[cur], rep, 0, cb_stage);
             consumers_sync();
         }
         const int sidx = P.parts == 2 ? part : cur;
         const int ng = P.st[sidx].ng;
-        const uint32_t rep_l = sbase + (P.parts == 2 ? part * kReplicaBytes : 0);
+        const uint32_t lanebase = lane16 | (uint32_t)((P.parts == 2 ? part : 0) << 7);
         const int g0 = c * kChunkGroups;
         const int ngc = min(kChunkGroups, ng - g0);
         mbar_wait(bar_full + 8 * stage, (i / kStages) & 1);
         const uint32_t sdst = stage0 + stage * kStageBytes;
         if (warp + kConsumerWarps < ngc)
-            mma_tiles<kBf16, kNT, kScaleF32, kXSmem, 2>(acc, sdst, warp, g0, rep_l, xs0, xs1, xg0, xg1, k_lane,
-                                                        xon0, xon1, lane);
+            mma_tiles<kBf16, kNT, kScaleF32, kXSmem, 2>(acc, sdst, warp, g0, lanebase, xs0, xs1, xg0, xg1, k_lane,
+                                                        lane);
         else if (warp < ngc)
-            mma_tiles<kBf16, kNT, kScaleF32, kXSmem, 1>(acc, sdst, warp, g0, rep_l, xs0, xs1, xg0, xg1, k_lane,
-                                                        xon0, xon1, lane);
+            mma_tiles<kBf16, kNT, kScaleF32, kXSmem, 1>(acc, sdst, warp, g0, lanebase, xs0, xs1, xg0, xg1, k_lane,
+                                                        lane);
         __syncwarp();
         if (lane == 0) mbar_arrive(bar_empty + 8 * stage);   // this warp is done with the stage
         if (++c < cpu) continue;
@@ -629,7 +649,9 @@ int launch_linear_mma_fused(const StoreD* s, int count, const void* x, int x_dty
     const int64_t kpad = s[0].ng * 128;
     const int64_t xbytes = m * kpad * 2;
     const int slot_floats = parts * kConsumerWarps * 16 * (int)m;
-    const int fixed = parts * kReplicaBytes + kBarBytes + kStages * kStageBytes + kSlots * slot_floats * 4;
+    // Requested as if the dynamic block started at window address 0 (it starts a
+    // little above, so the request always covers the layout).
+    const int fixed = (int)kHighWin + kSlots * slot_floats * 4;
     const bool xsm = xbytes <= kMaxXSmem && fixed + xbytes <= kMaxSmem;
     if (prologue == EPQ_PRO_RMSNORM && !xsm)
         return set_error(EPQ_EUNSUPPORTED, "decode linear: RMSNorm prologue needs m*k*2 <= %d bytes", kMaxXSmem);

@@ -58,7 +58,10 @@ int epq_attn_decode(const void* q, const void* k_cache, const void* v_cache, con
  * kv_heads of 1, 2, 4 or 8): q, k, v [heads or kv_heads, head_dim] are this token's
  * projections at position pos[0]; q and k get (qk_norm) RMSNorm and RoPE inside,
  * k and v are written into the caches at pos[0], and out receives the attention
- * over positions 0..pos[0].  Workspace as for epq_attn_decode (required). */
+ * over positions 0..pos[0].  The positions of each kv head are split over a
+ * thread-block cluster of 8 CTAs whose partial softmax records are merged in
+ * distributed shared memory.  The workspace of epq_attn_decode is still checked
+ * (kept for the ABI) but not used. */
 int epq_attn_rope_decode(const void* q, const void* k, const void* v, const int64_t* pos, int32_t heads,
                          int32_t kv_heads, int32_t head_dim, const float* cos_tab, const float* sin_tab,
                          void* k_cache, void* v_cache, int64_t max_len, int32_t qk_norm, float eps, float scale,
