@@ -45,7 +45,8 @@ N = 1: one whole 8B token per step.  N > 1: the 70B shapes' packed linears of
 Other workloads (each prints its own metric): --mode chain (the packed linears
 only, as one persistent chain launch per token, fp32 between layers), --mode
 per-linear [--batch B] (the per-linear GEMV / GEMM launches), --mode prefill
-[--tokens 2048], --mode finetune [--tokens 16384], --mode embedding;
+[--tokens 2048], --mode finetune [--batch 8 --seq 2048] (the whole Qwen3-1.7B
+model: forward, cross-entropy, backward, AdamW), --mode embedding;
 --model / --layers pick the shapes; --fallback also times the reference's bf16
 GPU fallback (materialize + F.linear, torch ops) on the same step.
 """
@@ -405,27 +406,56 @@ def time_fallback(stack, x, steps):
 
 
 def run_finetune(args, rank, world, local_rank):
-    """One compressed-state fine-tuning step over every packed linear (config 3)."""
+    """One compressed-state fine-tuning step of the whole model (config 3).
+
+    PackedCausalLM over random packed stores of ``args.model``'s shapes (Qwen3-1.7B
+    by default: q/k RMSNorm, tied lm_head, GQA): make_trainable(mode="both")
+    promotes every store's scales and codebook to fp32 parameters, and a step is
+    forward over ``--batch`` sequences of ``--seq`` tokens, next-token
+    cross-entropy, backward (libepq.so's packed GEMM forward and fused dX /
+    dscale / dcb backward; torch SDPA, RMSNorm, SiLU, the bf16 lm_head and the
+    softmax around them), and one fused AdamW update.  The reference's loop is
+    ScaleTuner.step (finetune.py:135-176) on the same model."""
     import torch
     import torch.distributed as dist
     from epure import synthetic
-    from epure.train import PackedTrainStep
+    from epure.finetune import make_trainable
+    from epure.model import PackedCausalLM, PackedDecoder
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    model = args.model
-    shapes = synthetic.SHAPES[model]
-    m = args.tokens
-    # make_trainable(mode="both") keeps scales and codebooks as fp32 parameters
-    stack = synthetic.LinearStack(shapes, layers=args.layers, device=dev, seed=1000 * rank,
-                                  gpu_layout="mma16", scale_dtype=torch.float32,
-                                  cb_dtype=torch.float32)
-    trainer = PackedTrainStep(stack, m, device=dev, seed=rank)
+    model_name = args.model
+    shapes = synthetic.SHAPES[model_name]
+    B, T = args.batch or 8, args.seq
+    dec = PackedDecoder(shapes, layers=args.layers, device=dev, seed=1000 * rank, max_len=T,
+                        fused_glue=False)
+    model = PackedCausalLM(dec, "ours")
+    params = make_trainable(model, "both")
+    opt = torch.optim.AdamW(params, lr=1e-5, fused=True)
     g = torch.Generator(device=dev).manual_seed(rank)
-    x = torch.randn(m, shapes.hidden, generator=g, device=dev).to(torch.bfloat16)
-    flops = trainer.flops()
+    ids = torch.randint(0, shapes.vocab, (B, T), generator=g, device=dev)
+
+    def step(batch):
+        loss = model(batch).loss
+        loss.backward()
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+        return loss
+
+    L = dec.layers
+    m = B * T
+    lin = dec.stack.flops(m)                                  # 2 m sum(n k) over the packed linears
+    qkv0 = sum(2 * m * st.out_features * st.in_features
+               for n_, st in dec.stack.blocks[0].items() if n_ in ("q_proj", "k_proj", "v_proj"))
+    # forward + dscale/dcb contraction everywhere, dX everywhere but layer 0's q/k/v
+    # (its input, the frozen embedding, needs no gradient)
+    flops = 3 * lin - qkv0
+    flops += 4 * m * shapes.vocab * shapes.hidden             # lm_head forward + dX
+    flops += 7 * B * shapes.heads * T * T * shapes.head_dim * L   # causal attention fwd (2) + bwd (5) halves
+    launches = 7 * L + 7 * L + (7 * L - 3)                    # forward, dscale/dcb, dX kernels of libepq.so
+
     for _ in range(args.warmup):
-        trainer.step(x)
+        step(ids)
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
@@ -435,7 +465,7 @@ def run_finetune(args, rank, world, local_rank):
     with ClockSampler(local_rank) as clocks:
         ev0.record(stream)
         for _ in range(args.steps):
-            trainer.step(x)
+            step(ids)
         ev1.record(stream)
         torch.cuda.synchronize(dev)
     ms = ev0.elapsed_time(ev1) / args.steps
@@ -443,16 +473,15 @@ def run_finetune(args, rank, world, local_rank):
         t = torch.tensor([ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    # end to end: the token batch from pinned host memory, the step, one gradient read back
-    xh = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
-    xh.copy_(x.cpu())
-    gh = torch.empty(1, dtype=torch.float32, pin_memory=True)
+    # end to end: the token batch from pinned host memory, the step, the loss read back
+    idh = torch.empty(ids.shape, dtype=ids.dtype, pin_memory=True)
+    idh.copy_(ids.cpu())
+    lh = torch.empty(1, dtype=torch.float32, pin_memory=True)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(args.steps):
-        xd = xh.to(dev, non_blocking=True)
-        trainer.step(xd)
-        gh.copy_(trainer.grads[0]["q_proj"][1][:1], non_blocking=True)
+        loss = step(idh.to(dev, non_blocking=True))
+        lh.copy_(loss.detach().view(1), non_blocking=True)
         stream.synchronize()
     e1.record(stream)
     torch.cuda.synchronize(dev)
@@ -465,67 +494,51 @@ def run_finetune(args, rank, world, local_rank):
     achieved = flops / (ms * 1e-3) / 1e12
     if rank == 0:
         line = {
-            "metric": f"fine-tune tok/s @{model} (packed linears fwd + dX + dscale/dcb, {m} tokens/step)",
+            "metric": f"fine-tune tok/s @{model_name} (whole model: fwd + CE + bwd + AdamW, "
+                      f"{B}x{T} tokens/step)",
             "value": round(world * m * 1000.0 / ms, 2), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic",
-            "config": {"workload": f"{model} packed linears, compressed-state fine-tune step "
-                                   f"({7 * stack.layers} linears, fp32 scales and codebooks)",
-                       "mode": "finetune", "global_batch": world * m, "seq_len": m,
+            "data": "synthetic (random packed stores, random token ids)",
+            "config": {"workload": f"{model_name} whole-model compressed-state fine-tune step "
+                                   f"({L} layers, {7 * L} packed linears, fp32 scales and codebooks, "
+                                   f"make_trainable mode=both, AdamW)",
+                       "mode": "finetune", "global_batch": world * B, "seq_len": T,
                        "parallelism": f"data-parallel replicas x{world}" if world > 1 else "single GPU",
-                       "flops_per_step": flops},
+                       "flops_per_step": flops, "final_loss": round(float(lh.item()), 4)},
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": tf_peak,
                          "unit": "TFLOP/s", "frac": round(achieved / tf_peak, 4), "peak_kind": tf_kind,
-                         "kernel": "gemm_tc_kernel + bwd_dx_tc_kernel + bwd_dw_tc_kernel",
+                         "kernel": "whole step (packed gemm_tc + bwd_dx_tc + bwd_dw_tc, SDPA, lm_head)",
                          "traffic": None},
             "e2e": {"value": round(world * m * 1000.0 / e2e_ms, 2), "unit": UNIT,
-                    "h2d_bytes_per_step": x.numel() * x.element_size(), "d2h_bytes_per_step": 4},
-            "gpu_launches": (4 + 7) * stack.layers * args.steps,
+                    "h2d_bytes_per_step": ids.numel() * ids.element_size(), "d2h_bytes_per_step": 4},
+            "gpu_launches": launches * args.steps,
             "clocks": clocks.summary(),
         }
         if args.fallback:
-            line["fallback"] = time_fallback_finetune(stack, x, steps=max(1, min(args.steps, 2)))
+            line["fallback"] = time_fallback_finetune(dec, ids, steps=max(1, min(args.steps, 2)))
         print(json.dumps(line), flush=True)
     return 0
 
 
-def time_fallback_finetune(stack, x, steps):
-    """The reference's fine-tuning autograd on the same step (GPU, torch ops).
+def time_fallback_finetune(dec, ids, steps):
+    """The reference's fine-tuning autograd on the same model and batch (GPU, torch ops).
 
     make_trainable (finetune.py:49-102) + PackedLinear.forward's fallback
     F.linear(x, materialize(bf16)) (runtime.py:78-89, 123-124): torch autograd
-    differentiates the gather/scale expansion and the GEMM; fp32 parameters.
+    differentiates the gather/scale expansion and the GEMM; fp32 parameters,
+    the same AdamW update.
     """
     import torch
-    import torch.nn.functional as F
-    params = []
-    for b in stack.blocks:
-        pb = {}
-        for name, st in b.items():
-            pb[name] = (st.index_rows().long(), st.cb.float().clone().requires_grad_(True),
-                        st.scale.float().clone().requires_grad_(True), st)
-        params.append(pb)
-
-    def weight(p):
-        idx, cb, sc, st = p
-        w = cb.to(torch.bfloat16)[idx].reshape(st.out_features, -1)[:, :st.in_features]
-        return w * sc.to(torch.bfloat16).repeat_interleave(st.group, dim=1)[:, :st.in_features]
+    from epure.model import PackedCausalLM
+    model = PackedCausalLM(dec, "reference")
+    params = [p for b in model.layers for mod in b.children() for p in (mod.store.scale, mod.store.cb)]
+    opt = torch.optim.AdamW(params, lr=1e-5, fused=True)
 
     def step():
-        h = x.detach().requires_grad_(True)
-        outs = []
-        for pb in params:
-            q = F.linear(h, weight(pb["q_proj"]))
-            k = F.linear(h, weight(pb["k_proj"]))
-            v = F.linear(h, weight(pb["v_proj"]))
-            o = F.linear(q, weight(pb["o_proj"]))
-            gt = F.linear(o, weight(pb["gate_proj"]))
-            u = F.linear(o, weight(pb["up_proj"]))
-            h = F.linear(u, weight(pb["down_proj"]))
-            outs += [k, v, gt]
-        loss = h.float().square().mean() + sum(t.float().mean() for t in outs)
-        loss.backward()
+        model(ids).loss.backward()
+        opt.step()
+        opt.zero_grad(set_to_none=True)
 
     step()
     torch.cuda.synchronize()
@@ -537,8 +550,8 @@ def time_fallback_finetune(stack, x, steps):
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / steps
     return {"what": "reference fine-tune autograd: F.linear(x, materialize(bf16)) per store, "
-                    "fp32 scale/codebook parameters (torch ops)",
-            "ms_per_step": round(ms, 3), "value": round(x.shape[0] * 1000.0 / ms, 2), "unit": UNIT,
+                    "fp32 scale/codebook parameters (torch ops), same model and AdamW",
+            "ms_per_step": round(ms, 3), "value": round(ids.numel() * 1000.0 / ms, 2), "unit": UNIT,
             "steps": steps}
 
 
@@ -999,7 +1012,8 @@ def main():
     ap.add_argument("--model", choices=sorted(SHAPES), default=None)
     ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--tokens", type=int, default=None)
-    ap.add_argument("--batch", type=int, default=1,
+    ap.add_argument("--seq", type=int, default=2048, help="--mode finetune: tokens per sequence")
+    ap.add_argument("--batch", type=int, default=None,
                     help="decode batch (tokens per step) for --mode per-linear: M rows through "
                          "every linear (tensor-core GEMV up to 16, the tcgen05 GEMM above)")
     ap.add_argument("--layout", choices=["mma16", "tiled"], default="mma16",
@@ -1027,8 +1041,10 @@ def main():
                       "llama3-70b" if (args.tp and world > 1) else "llama3-8b")
     if args.tokens is None:
         args.tokens = 8 * 2048 if args.mode == "finetune" else 2048
-    if args.batch != 1 and args.mode != "per-linear":
-        ap.error("--batch applies to --mode per-linear")
+    if args.batch is not None and args.mode not in ("per-linear", "finetune"):
+        ap.error("--batch applies to --mode per-linear and --mode finetune")
+    if args.batch is None and args.mode != "finetune":
+        args.batch = 1
 
     if args.impl == "reference":
         return run_reference(args, rank, world)

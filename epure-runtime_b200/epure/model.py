@@ -284,3 +284,100 @@ class PackedDecoder:
 
     def teacher_forced_argmax(self, prompt, tokens):
         return torch.argmax(self.teacher_forced_logits(prompt, tokens), dim=-1).cpu()
+
+
+class PackedCausalLM(torch.nn.Module):
+    """The same decoder as a trainable module tree, for compressed-state fine-tuning.
+
+    The reference fine-tunes a Hugging Face causal LM whose linears ``apply_to``
+    swapped for PackedLinear (epure/finetune.py:49-176, fine-tuning/codebook.py):
+    ``make_trainable`` promotes every store's scales and codebook to fp32
+    parameters, the indices stay frozen, and the loss is next-token
+    cross-entropy.  This is that model family written out: a bf16 embedding
+    (tied to the lm_head for Qwen3, a separate one for Llama-3; both frozen),
+    per layer RMSNorm, q/k/v (with per-head q/k RMSNorm for Qwen3), RoPE,
+    causal grouped-query attention (torch SDPA), o, residual, RMSNorm, SwiGLU
+    gate/up/down, residual; final RMSNorm, lm_head, cross-entropy.  Every
+    projection is a ``PackedLinear`` over the stores of ``decoder.stack``, so on
+    a GPU it runs libepq.so's tensor-core GEMM forward and its fused
+    compressed-state backward (dX, dscale, dcb; dW never formed).
+    ``linear_mode="reference"`` instead differentiates the reference's fallback
+    ``F.linear(x, materialize(bf16))`` (runtime.py:78-89, 123-124) with torch
+    ops, the formulation the gradients are checked against.
+
+    ``forward(input_ids [B, T], labels=None)`` returns an object with ``.loss``
+    (labels default to the inputs, shifted by one inside), so ``ScaleTuner``
+    can drive it."""
+
+    def __init__(self, decoder, linear_mode="ours"):
+        super().__init__()
+        import types
+        from .runtime import PackedLinear
+        if linear_mode not in ("ours", "reference"):
+            raise ValueError("linear_mode must be 'ours' or 'reference'")
+        self._types = types
+        self.shapes = decoder.shapes
+        self.mode = linear_mode
+        self.eps = decoder.eps
+        self.qk_norm = decoder.qk_norm
+        self.cos, self.sin = decoder.cos, decoder.sin
+        self.register_buffer("embed_w", decoder.embed.detach(), persistent=False)
+        self.register_buffer("head_w", decoder.lm_head.detach(), persistent=False)
+        self.layers = torch.nn.ModuleList()
+        for b in decoder.stack.blocks:
+            blk = torch.nn.Module()
+            for name, st in b.items():
+                setattr(blk, name, PackedLinear(st))
+            self.layers.append(blk)
+
+    def _lin(self, mod, x):
+        if self.mode == "ours":
+            return mod(x)
+        return F.linear(x, mod.store.materialize(x.dtype))
+
+    def _rms(self, x):
+        xf = x.float()
+        return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps)).to(x.dtype)
+
+    def _rope(self, x):
+        # x [B, T, heads, hd], positions 0..T-1 (rotate-half)
+        T = x.shape[1]
+        c, s = self.cos[:T][None, :, None, :], self.sin[:T][None, :, None, :]
+        xf = x.float()
+        half = x.shape[-1] // 2
+        x1, x2 = xf[..., :half], xf[..., half:]
+        return torch.cat([x1 * c - x2 * s, x2 * c + x1 * s], dim=-1).to(x.dtype)
+
+    def logits(self, input_ids):
+        """bf16 logits [B, T, vocab] of every position (causal)."""
+        sh = self.shapes
+        B, T = input_ids.shape
+        H, KV, hd = sh.heads, sh.kv_heads, sh.head_dim
+        if T > self.cos.shape[0]:
+            raise ValueError(f"epure: sequence of {T} tokens exceeds the rotary table ({self.cos.shape[0]})")
+        x = F.embedding(input_ids, self.embed_w)                              # [B, T, hidden] bf16
+        for blk in self.layers:
+            h = self._rms(x)
+            q = self._lin(blk.q_proj, h).view(B, T, H, hd)
+            k = self._lin(blk.k_proj, h).view(B, T, KV, hd)
+            v = self._lin(blk.v_proj, h).view(B, T, KV, hd)
+            if self.qk_norm:
+                q, k = self._rms(q), self._rms(k)
+            q, k = self._rope(q), self._rope(k)
+            att = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
+                                                 is_causal=True, scale=1.0 / math.sqrt(hd), enable_gqa=True)
+            att = att.transpose(1, 2).reshape(B, T, H * hd)
+            x = x + self._lin(blk.o_proj, att)
+            h = self._rms(x)
+            g, u = self._lin(blk.gate_proj, h), self._lin(blk.up_proj, h)
+            x = x + self._lin(blk.down_proj, (F.silu(g.float()) * u.float()).to(x.dtype))
+        return F.linear(self._rms(x), self.head_w)
+
+    def forward(self, input_ids, labels=None):
+        """Next-token cross-entropy (fp32 softmax over bf16 logits) of ``labels``
+        (default ``input_ids``) shifted by one."""
+        logits = self.logits(input_ids)
+        labels = input_ids if labels is None else labels
+        loss = F.cross_entropy(logits[:, :-1].reshape(-1, logits.shape[-1]).float(),
+                               labels[:, 1:].reshape(-1))
+        return self._types.SimpleNamespace(loss=loss)
