@@ -80,7 +80,18 @@ RMS_EPS = {"qwen3-1.7b": 1e-6, "llama3-8b": 1e-5, "llama3-70b": 1e-5}
 # (dram__bytes_read.sum + dram__bytes_write.sum over the launch's algorithmic
 # bytes); chain = chain_kernel on a 4-layer chain.
 NCU_TRAFFIC_RATIO = {"per-linear": 31249152 / 31264768,
-                     "chain": (232937728 + 24145664) / 232349696}
+                     "chain": (232937728 + 24145664) / 232349696,
+                     "program": None}
+
+
+def _traffic(ratio, algorithmic_bytes, full):
+    """The roofline's `traffic`: the ncu-measured DRAM bytes / algorithmic bytes of
+    the kernel (a small capture, profiles/) times this launch's algorithmic bytes."""
+    if ratio is None or not full:
+        return {"traffic": None, "traffic_note": "no ncu capture of this kernel at this size"}
+    return {"traffic": int(algorithmic_bytes * ratio),
+            "traffic_note": "ncu dram bytes / algorithmic bytes of a small capture (profiles/), "
+                            "times this launch's algorithmic bytes"}
 
 
 def linears(shape):
@@ -148,34 +159,49 @@ class ClockSampler:
         except Exception:
             return nv.nvmlDeviceGetHandleByIndex(self.device_index)
 
-    def _run(self, nv, h):
+    def _sample(self):
+        nv, h = self._nv, self._h
+        try:
+            sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+            reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+            power = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+            self.samples.append((sm, reasons, power))
+        except Exception:
+            pass
+
+    def _run(self):
         while not self._stop:
-            try:
-                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
-                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
-                power = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
-                self.samples.append((sm, reasons, power))
-            except Exception:
-                pass
+            self._sample()
             time.sleep(self.interval)
 
     def __enter__(self):
+        # The sampler thread competes for the GIL with the launching loop: a
+        # 1 ms switch interval lets it in, and the region opens only once the
+        # first sample is in; __exit__ adds one more taken before the GPU idles.
+        self._switch = sys.getswitchinterval()
         try:
             import threading
             import pynvml as nv
             nv.nvmlInit()
-            h = self._handle(nv)
-            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
-            self._thread = threading.Thread(target=self._run, args=(nv, h), daemon=True)
+            self._nv, self._h = nv, self._handle(nv)
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(self._h, nv.NVML_CLOCK_SM)
+            sys.setswitchinterval(0.001)
+            self._thread = threading.Thread(target=self._run, daemon=True)
             self._thread.start()
+            t0 = time.time()
+            while not self.samples and time.time() - t0 < 0.5:
+                time.sleep(0.001)
         except Exception:
             self._thread = None
         return self
 
     def __exit__(self, *a):
+        if self._thread is not None:
+            self._sample()
         self._stop = True
         if self._thread is not None:
             self._thread.join(timeout=2)
+        sys.setswitchinterval(self._switch)
 
     def summary(self):
         if not self.samples:
@@ -664,7 +690,7 @@ def run_model(args, rank, world, local_rank):
     shapes = synthetic.SHAPES[args.model]
     max_len = PROMPT + args.warmup + args.steps + 2
     dec = PackedDecoder(shapes, layers=args.layers, device=dev, seed=1000 * rank, max_len=max_len,
-                        fp32_logits=False, gpu_layout=args.layout).capture()
+                        fp32_logits=False, gpu_layout=args.layout, program=args.program).capture()
     g = torch.Generator().manual_seed(rank)
     prompt = torch.randint(0, shapes.vocab, (PROMPT,), generator=g)
     stream = torch.cuda.current_stream(dev)
@@ -708,22 +734,49 @@ def run_model(args, rank, world, local_rank):
     e2e_ms, _ = _timed_replays(e2e_step, args.steps, dev, stream)
     e2e_ms = max(e2e_ms, (time.perf_counter() - t0) * 1e3)
 
-    # the dominant kernel alone: the token's packed launches (gemv_mma_kernel) in one graph
-    lin = GraphedLinearStack(dec.stack, m=1, dtype=torch.bfloat16, device=dev).capture()
-    lin.x.copy_(torch.randn(lin.x.shape, generator=torch.Generator(device=dev).manual_seed(rank),
-                            device=dev).to(torch.bfloat16))
-    for _ in range(args.warmup):
-        lin.replay()
-    lin_ms, _ = _timed_replays(lin.replay, args.steps, dev, torch.cuda.current_stream(dev))
-    ms, e2e_ms, lin_ms = _max_over_ranks([ms / args.steps, e2e_ms / args.steps, lin_ms / args.steps],
-                                         dev, world)
-
     packed = sum(store_bytes(st) for b in dec.stack.blocks for st in b.values())
     lm = dec.lm_head.numel() * dec.lm_head.element_size()
     pos_avg = PROMPT + args.warmup + args.steps / 2
     kv = 2 * dec.layers * pos_avg * shapes.kv_heads * shapes.head_dim * 2
     token_bytes = int(packed + lm + shapes.hidden * 2 + kv)
-    lin_bytes = dec.stack.algorithmic_bytes(m=1, act_bytes=2)
+    if dec.use_program:
+        # the dominant kernel alone: the token's decode program (every packed
+        # linear and the attention of every layer, one launch) replayed in a graph
+        # at the position the timed tokens averaged
+        dec._ppos.fill_(int(pos_avg))
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            dec._program.run()
+        stream.wait_stream(side)
+        torch.cuda.synchronize(dev)
+        pg = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(pg):
+            dec._program.run()
+        for _ in range(args.warmup):
+            pg.replay()
+        lin_ms, _ = _timed_replays(pg.replay, args.steps, dev, stream)
+        # packed stores + this position's K/V rows + the activations in and out of every step
+        lin_bytes = int(dec.stack.algorithmic_bytes(m=1, act_bytes=2)
+                        + 2 * dec.layers * (int(pos_avg) + 1) * shapes.kv_heads * shapes.head_dim * 2)
+        kern = {"kernel": "decode_program_kernel (every layer's packed linears and attention, one launch)",
+                "launches": 1, "launch_avg_us": None}
+        n_launch = 1
+    else:
+        # the dominant kernel alone: the token's packed launches (gemv_mma_kernel) in one graph
+        lin = GraphedLinearStack(dec.stack, m=1, dtype=torch.bfloat16, device=dev).capture()
+        lin.x.copy_(torch.randn(lin.x.shape, generator=torch.Generator(device=dev).manual_seed(rank),
+                                device=dev).to(torch.bfloat16))
+        for _ in range(args.warmup):
+            lin.replay()
+        lin_ms, _ = _timed_replays(lin.replay, args.steps, dev, stream)
+        lin_bytes = dec.stack.algorithmic_bytes(m=1, act_bytes=2)
+        n_launch = 4 * dec.layers
+        kern = {"kernel": "gemv_mma_kernel (the token's packed launches replayed alone)", "launches": n_launch}
+    ms, e2e_ms, lin_ms = _max_over_ranks([ms / args.steps, e2e_ms / args.steps, lin_ms / args.steps],
+                                         dev, world)
+    kern["launch_avg_us"] = round(lin_ms * 1e3 / n_launch, 3)
+    kern["bytes_per_launch_avg"] = int(lin_bytes / n_launch)
     hbm_peak, peak_kind = _peaks()
     lin_gbs = lin_bytes / (lin_ms * 1e-3) / 1e9
     tok_gbs = token_bytes / (ms * 1e-3) / 1e9
@@ -731,6 +784,8 @@ def run_model(args, rank, world, local_rank):
     if rank == 0:
         name, cfg = workload(args, world)
         cfg.update({"layout": args.layout, "bytes_per_step": token_bytes,
+                    "decode_path": ("one persistent decode program per token" if dec.use_program
+                                    else "five fused launches per layer"),
                     "bytes_split": {"packed": packed, "lm_head": lm, "kv": int(kv),
                                     "embedding_row": shapes.hidden * 2}})
         line = {
@@ -740,20 +795,17 @@ def run_model(args, rank, world, local_rank):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded random weights in the benchmark format; uniform random prompt ids)",
             "config": cfg,
-            "roofline": {"bound": "hbm", "achieved": round(lin_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
-                         "frac": round(lin_gbs / hbm_peak, 4), "peak_kind": peak_kind,
-                         "kernel": "gemv_mma_kernel (the token's packed launches replayed alone)",
-                         "launches": 4 * dec.layers, "launch_avg_us": round(lin_ms * 1e3 / (4 * dec.layers), 3),
-                         "bytes_per_launch_avg": int(lin_bytes / (4 * dec.layers)),
-                         "traffic": int(lin_bytes * NCU_TRAFFIC_RATIO["per-linear"]) if full else None,
-                         "traffic_note": "ncu dram bytes / algorithmic bytes of one gate+up launch (profiles/), "
-                                         "times the token's packed bytes"},
+            "roofline": dict({"bound": "hbm", "achieved": round(lin_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
+                              "frac": round(lin_gbs / hbm_peak, 4), "peak_kind": peak_kind}, **kern,
+                             **_traffic(NCU_TRAFFIC_RATIO["program" if dec.use_program else "per-linear"],
+                                        lin_bytes, full)),
             "token_roofline": {"bound": "hbm", "bytes_per_token": token_bytes, "achieved": round(tok_gbs, 1),
                                "peak": hbm_peak, "unit": "GB/s", "frac": round(tok_gbs / hbm_peak, 4),
                                "roofline_tok_s": round(hbm_peak * 1e9 / token_bytes, 1)},
             "e2e": {"value": round(world * 1000.0 / e2e_ms, 2), "unit": UNIT,
                     "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8},
-            "gpu_launches": (5 * dec.layers + 2) * args.steps,
+            # ours per token: program (or 5 per layer) + final RMSNorm + argmax
+            "gpu_launches": ((3 if dec.use_program else 5 * dec.layers + 2)) * args.steps,
             "clocks": clocks,
         }
         if world == 1 and not args.no_cpu_baseline:
@@ -1023,6 +1075,8 @@ def main():
                     help="at N > 1 with --mode chain / per-linear: one model tensor-parallel over the N GPUs")
     ap.add_argument("--replicas", action="store_true",
                     help="at N > 1: N independent copies of the N = 1 workload instead of tensor parallelism")
+    ap.add_argument("--program", action="store_true",
+                    help="--mode model: run each token's layers as one persistent decode program")
     ap.add_argument("--fallback", action="store_true",
                     help="also time the reference's bf16 fallback path on the same step (GPU)")
     args = ap.parse_args()

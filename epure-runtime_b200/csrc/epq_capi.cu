@@ -154,8 +154,8 @@ int epq_device_error(int* flag) {
     // bit 0: LUT placement check; bit 1: a bounded wait gave up (GEMV, GEMM, backward or chain);
     // bit 2: the chain kernel's placement or grid check failed; bit 3: an embedding id was
     // outside the store's rows; bit 4: a decode position was at or past the KV cache's capacity
-    *flag = (lut ? 1 : 0) | ((mma || tc || bwd || chain == 1) ? 2 : 0) | (chain == 2 ? 4 : 0) |
-            (emb ? 8 : 0) | (glue ? 16 : 0);
+    *flag = (lut ? 1 : 0) | (((mma & 1) || tc || bwd || chain == 1) ? 2 : 0) | (chain == 2 ? 4 : 0) |
+            (emb ? 8 : 0) | ((glue || (mma & 2)) ? 16 : 0);
     return EPQ_OK;
 }
 

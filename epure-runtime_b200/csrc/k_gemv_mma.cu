@@ -57,10 +57,14 @@
 //   before the previous kernel (which produces x) finishes.
 // * Every mbarrier wait is bounded; a wait that gives up sets a device error
 //   flag (read by epq_device_error) and the kernel runs to completion.
+#include <algorithm>
 #include <climits>
+#include <new>
+#include <vector>
 
 #include "epq_common.cuh"
 #include "epq_decode.h"
+#include "epq_rope.cuh"
 #include "epq_sm100.cuh"
 
 namespace epq {
@@ -347,106 +351,120 @@ __device__ __forceinline__ int xperm(int row, int kpad, int col) {
     return row * kpad + (((g * 4 + (s >> 1)) * 4 + q) << 3) + ((s & 1) << 2) + j;
 }
 
-template <bool kBf16, int kNT, bool kScaleF32, bool kXSmem>
-__global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const __grid_constant__ MmaParams P) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
-    if (sbase + kLowBytes > kRepWin) {   // the layout needs the dynamic block to start low (uniform)
-        if (threadIdx.x == 0) atomicExch(&g_mma_wait_timeout, 1);
-        return;
+// Loads of data another CTA of a persistent program wrote during this launch go
+// to L2 (.cg): L1 is not coherent across SMs, and a program reuses its
+// activation buffers layer after layer.  A single launch reads only what the
+// previous kernel wrote, so it may use plain loads.
+template <bool kProg>
+__device__ __forceinline__ uint2 ld_x8(const uint16_t* p) {
+    if constexpr (kProg) return __ldcg(reinterpret_cast<const uint2*>(p));
+    else return *reinterpret_cast<const uint2*>(p);
+}
+template <bool kProg>
+__device__ __forceinline__ float ld_act(const void* p, int dt, int64_t o) {
+    if constexpr (kProg) {
+        const unsigned short r = __ldcg(static_cast<const unsigned short*>(p) + o);
+        return dt == EPQ_BF16 ? __uint_as_float((uint32_t)r << 16) : __half2float(__ushort_as_half(r));
+    } else {
+        return load_f(p, dt, o);
     }
-    uint2* rep = reinterpret_cast<uint2*>(smem + (kRepWin - sbase));
-    const uint32_t bar_full = sbase;                       // kStages x 8 B
-    const uint32_t bar_empty = bar_full + 8 * kStages;     // kStages x 8 B
-    int* cnt = reinterpret_cast<int*>(smem + 16 * kStages);   // kSlots arrival counters
+}
+
+// The CTA's contiguous, balanced range of units (16-row blocks) of a linear.
+__device__ __forceinline__ void unit_range(int U, int& u_begin, int& u_end) {
+    const int G = gridDim.x;
+    u_begin = (int)((int64_t)U * blockIdx.x / G);
+    u_end = (int)((int64_t)U * (blockIdx.x + 1) / G);
+}
+
+// Producer warp: streams the chunks of units [u_begin, u_end) of P into the
+// ring.  `ring` counts the ring positions used so far (a persistent program
+// keeps counting across its linears, so the stage parities line up).
+template <bool kScaleF32>
+__device__ __forceinline__ void produce_linear(const MmaParams& P, int u_begin, int u_end, uint32_t bar_full,
+                                               uint32_t bar_empty, uint32_t stage0, int lane, uint32_t& ring) {
+    constexpr int kScaleBytes = kScaleF32 ? 4 : 2;
+    const int cpu = P.chunks_per_unit, parts = P.parts, count = P.count;
+    const int n_chunks = (u_end - u_begin) * cpu * parts;
+    int si = parts == 2 ? 0 : store_of(P, u_begin);
+    int s_next = (parts == 1 && si + 1 < count) ? P.st[si + 1].unit0 : INT_MAX;
+    int u = u_begin, part = 0, c = 0;
+    for (int j = 0; j < n_chunks; ++j, ++ring) {
+        const uint32_t stage = ring % kStages;
+        if (ring >= (uint32_t)kStages) mbar_wait(bar_empty + 8 * stage, ((ring / kStages) - 1) & 1);
+        int rb;
+        if (parts == 2) {
+            si = part;
+            rb = u;
+        } else {
+            if (u >= s_next) {
+                si = store_of(P, u);
+                s_next = si + 1 < count ? P.st[si + 1].unit0 : INT_MAX;
+            }
+            rb = u - P.st[si].unit0;
+        }
+        const MmaStore& S = P.st[si];
+        const int g0 = c * kChunkGroups;
+        const int ngc = min(kChunkGroups, S.ng - g0);
+        const uint32_t dst = stage0 + stage * kStageBytes;
+        // Two copies per chunk: the index tiles (one contiguous run) and the
+        // scales of its 16 rows x 32 groups (one 2-D tensor box; groups past
+        // the store's last are zero-filled, and the full box is counted).
+        if (lane == 0) {
+            mbar_expect_tx(bar_full + 8 * stage, ngc * 512 + kChunkGroups * 16 * kScaleBytes);
+            bulk_g2s(dst, S.idx + ((int64_t)rb * S.ng + g0) * 512, ngc * 512, bar_full + 8 * stage);
+            sm100::tma_load_2d(dst + kStageIdx, &S.smap, bar_full + 8 * stage, rb * 16, g0);
+        }
+        __syncwarp();
+        if (++c == cpu) {
+            c = 0;
+            if (++part == parts) {
+                part = 0;
+                ++u;
+            }
+        }
+    }
+}
+
+// Consumers: the codebook replica(s) of the store(s) the CTA's first unit reads
+// (nothing when the CTA has no unit).  Ends with a consumer barrier.
+template <bool kBf16>
+__device__ __forceinline__ void prepare_linear(const MmaParams& P, int u_begin, int u_end, uint2* rep,
+                                               uint2* cb_stage) {
+    if (u_begin >= u_end) return;
+    const int cur = P.parts == 2 ? 0 : store_of(P, u_begin);
+    for (int r = 0; r < P.parts; ++r) {
+        if (r) consumers_sync();   // the staging area is reused
+        build_replica<kBf16>(P.st[P.parts == 2 ? r : cur], rep, r, cb_stage);
+    }
+    consumers_sync();   // the staging area is the RMSNorm scratch next
+}
+
+// Consumers: stage x (kXSmem; RMSNorm prologue), run the chunks of units
+// [u_begin, u_end) from the ring, reduce each unit and run the epilogue.
+// prepare_linear must have run for this range.
+template <bool kBf16, int kNT, bool kScaleF32, bool kXSmem, bool kProg>
+__device__ __forceinline__ void run_linear(const MmaParams& P, int u_begin, int u_end, uint8_t* smem,
+                                           uint32_t sbase, uint32_t& ring) {
+    const uint32_t bar_full = sbase;
+    const uint32_t bar_empty = bar_full + 8 * kStages;
+    int* cnt = reinterpret_cast<int*>(smem + 16 * kStages);
     const uint32_t stage0 = sbase + kBarBytes;
+    uint2* rep = reinterpret_cast<uint2*>(smem + (kRepWin - sbase));
     float* slots = reinterpret_cast<float*>(smem + (kHighWin - sbase));
     uint16_t* xs = reinterpret_cast<uint16_t*>(smem + (P.x_off - sbase));   // [m][kpad] when kXSmem
-    constexpr int kScaleBytes = kScaleF32 ? 4 : 2;
-
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-    // Contiguous, balanced range of units (16-row blocks) for this CTA.
-    const int U = P.total_units, G = gridDim.x;
-    const int u_begin = (int)((int64_t)U * blockIdx.x / G);
-    const int u_end = (int)((int64_t)U * (blockIdx.x + 1) / G);
-    const int cpu = P.chunks_per_unit;
-    const int n_chunks = (u_end - u_begin) * cpu * P.parts;
-
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; ++s) {
-            mbar_init(bar_full + 8 * s, 1);
-            mbar_init(bar_empty + 8 * s, kConsumerWarps);
-        }
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    if (threadIdx.x < kSlots) cnt[threadIdx.x] = 0;
-    __syncthreads();
-
-    if (warp == kConsumerWarps) {
-        // ---------------- producer: stream chunks into the ring ----------------
-        int si = P.parts == 2 ? 0 : store_of(P, u_begin);
-        int s_next = (P.parts == 1 && si + 1 < P.count) ? P.st[si + 1].unit0 : INT_MAX;
-        int u = u_begin, part = 0, c = 0;
-        for (int i = 0; i < n_chunks; ++i) {
-            const int stage = i % kStages;
-            if (i >= kStages) mbar_wait(bar_empty + 8 * stage, ((i / kStages) - 1) & 1);
-            int rb;
-            if (P.parts == 2) {
-                si = part;
-                rb = u;
-            } else {
-                if (u >= s_next) {
-                    si = store_of(P, u);
-                    s_next = si + 1 < P.count ? P.st[si + 1].unit0 : INT_MAX;
-                }
-                rb = u - P.st[si].unit0;
-            }
-            const MmaStore& S = P.st[si];
-            const int g0 = c * kChunkGroups;
-            const int ngc = min(kChunkGroups, S.ng - g0);
-            const uint32_t dst = stage0 + stage * kStageBytes;
-            // Two copies per chunk: the index tiles (one contiguous run) and the
-            // scales of its 16 rows x 32 groups (one 2-D tensor box; groups past
-            // the store's last are zero-filled, and the full box is counted).
-            if (lane == 0) {
-                mbar_expect_tx(bar_full + 8 * stage, ngc * 512 + kChunkGroups * 16 * kScaleBytes);
-                bulk_g2s(dst, S.idx + ((int64_t)rb * S.ng + g0) * 512, ngc * 512, bar_full + 8 * stage);
-                sm100::tma_load_2d(dst + kStageIdx, &S.smap, bar_full + 8 * stage, rb * 16, g0);
-            }
-            __syncwarp();
-            if (++c == cpu) {
-                c = 0;
-                if (++part == P.parts) {
-                    part = 0;
-                    ++u;
-                }
-            }
-        }
-        pdl_trigger();
-        return;
-    }
-
-    // ---------------- consumers ----------------
-    const int gq = lane >> 2, q = lane & 3;
-    int cur = P.parts == 2 ? 0 : store_of(P, u_begin);
-    int c_next = (P.parts == 1 && cur + 1 < P.count) ? P.st[cur + 1].unit0 : INT_MAX;
     uint2* cb_stage = reinterpret_cast<uint2*>(slots);   // 2 KB; slots are free until a unit ends
-    if (u_begin < u_end) {
-        for (int r = 0; r < P.parts; ++r) {
-            if (r) consumers_sync();   // the staging area is reused
-            if constexpr (kBf16) build_replica<true>(P.st[P.parts == 2 ? r : cur], rep, r, cb_stage);
-            else build_replica<false>(P.st[P.parts == 2 ? r : cur], rep, r, cb_stage);
-        }
-        consumers_sync();   // the staging area is the RMSNorm scratch next
-    }
-    pdl_trigger();
-    pdl_wait();   // x (and the output buffers) belong to the previous kernel until here
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int cpu = P.chunks_per_unit, parts = P.parts, count = P.count, M = P.m;
+    const int n_chunks = (u_end - u_begin) * cpu * parts;
+    const int gq = lane >> 2, q = lane & 3;
+    int cur = parts == 2 ? 0 : store_of(P, u_begin);
+    int c_next = (parts == 1 && cur + 1 < count) ? P.st[cur + 1].unit0 : INT_MAX;
 
     // Activation B fragments: lane (gq, q) supplies column gq = activation row
     // min(gq, m - 1) (columns >= m are computed and never stored).
-    const int xr0 = gq < P.m ? gq : P.m - 1;
-    const int xr1 = gq + 8 < P.m ? gq + 8 : P.m - 1;
+    const int xr0 = gq < M ? gq : M - 1;
+    const int xr1 = gq + 8 < M ? gq + 8 : M - 1;
     const uint16_t* xg0 = static_cast<const uint16_t*>(P.x) + (int64_t)xr0 * P.ldx + 4 * q;
     const uint16_t* xg1 = static_cast<const uint16_t*>(P.x) + (int64_t)xr1 * P.ldx + 4 * q;
     uint32_t xs0 = 0, xs1 = 0;
@@ -454,14 +472,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const __grid_cons
         // Stage x (or RMSNorm(x)) in the permuted B-fragment order.
         const int per_row = P.kpad >> 2;
         const bool norm = P.prologue == EPQ_PRO_RMSNORM;
-        for (int row = 0; row < P.m; ++row) {
+        for (int row = 0; row < M; ++row) {
             float ss = 0.f;
             for (int i = threadIdx.x; i < per_row; i += kConsumers) {
                 const int c4 = i * 4;
                 uint2 v = make_uint2(0u, 0u);
-                if (c4 < P.k)
-                    v = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(P.x) +
-                                                        (int64_t)row * P.ldx + c4);
+                if (c4 < P.k) v = ld_x8<kProg>(static_cast<const uint16_t*>(P.x) + (int64_t)row * P.ldx + c4);
                 if (norm) {
                     const float a = act_to_f<kBf16>(v.x & 0xffffu), b = act_to_f<kBf16>(v.x >> 16);
                     const float c = act_to_f<kBf16>(v.y & 0xffffu), d = act_to_f<kBf16>(v.y >> 16);
@@ -476,7 +492,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const __grid_cons
         }
         if (norm) {
             consumers_sync();
-            for (int row = 0; row < P.m; ++row) {
+            for (int row = 0; row < M; ++row) {
                 float ss = 0.f;
 #pragma unroll
                 for (int w = 0; w < kConsumerWarps; ++w) ss += slots[row * kConsumerWarps + w];
@@ -508,24 +524,23 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const __grid_cons
 #pragma unroll
         for (int h = 0; h < kNT; ++h) acc[e][h][0] = acc[e][h][1] = acc[e][h][2] = acc[e][h][3] = 0.f;
     int u = u_begin, part = 0, c = 0, uslot = 0;
-    for (int i = 0; i < n_chunks; ++i) {
-        const int stage = i % kStages;
-        if (P.parts == 1 && c == 0 && u >= c_next) {
+    for (int j = 0; j < n_chunks; ++j, ++ring) {
+        const uint32_t stage = ring % kStages;
+        if (parts == 1 && c == 0 && u >= c_next) {
             // New store (CTA-uniform): rebuild the codebook replica once every warp
             // is past the previous store's gathers.
             consumers_sync();
             cur = store_of(P, u);
-            c_next = cur + 1 < P.count ? P.st[cur + 1].unit0 : INT_MAX;
-            if constexpr (kBf16) build_replica<true>(P.st[cur], rep, 0, cb_stage);
-            else build_replica<false>(P.st[cur], rep, 0, cb_stage);
+            c_next = cur + 1 < count ? P.st[cur + 1].unit0 : INT_MAX;
+            build_replica<kBf16>(P.st[cur], rep, 0, cb_stage);
             consumers_sync();
         }
-        const int sidx = P.parts == 2 ? part : cur;
+        const int sidx = parts == 2 ? part : cur;
         const int ng = P.st[sidx].ng;
-        const uint32_t lanebase = lane16 | (uint32_t)((P.parts == 2 ? part : 0) << 7);
+        const uint32_t lanebase = lane16 | (uint32_t)((parts == 2 ? part : 0) << 7);
         const int g0 = c * kChunkGroups;
         const int ngc = min(kChunkGroups, ng - g0);
-        mbar_wait(bar_full + 8 * stage, (i / kStages) & 1);
+        mbar_wait(bar_full + 8 * stage, (ring / kStages) & 1);
         const uint32_t sdst = stage0 + stage * kStageBytes;
         if (warp + kConsumerWarps < ngc)
             mma_tiles<kBf16, kNT, kScaleF32, kXSmem, 2>(acc, sdst, warp, g0, lanebase, xs0, xs1, xg0, xg1, k_lane,
@@ -540,15 +555,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const __grid_cons
         // End of one part of a unit: this warp's partial sums into the unit's slot,
         // laid out [part][warp][m][16 rows].
         {
-            float* mine = slots + uslot * P.slot_floats + (part * kConsumerWarps + warp) * 16 * P.m;
+            float* mine = slots + uslot * P.slot_floats + (part * kConsumerWarps + warp) * 16 * M;
 #pragma unroll
             for (int h = 0; h < kNT; ++h) {
                 const int m0 = 8 * h + 2 * q;
-                if (m0 < P.m) {
+                if (m0 < M) {
                     mine[m0 * 16 + gq] = acc[0][h][0] + acc[1][h][0];
                     mine[m0 * 16 + gq + 8] = acc[0][h][2] + acc[1][h][2];
                 }
-                if (m0 + 1 < P.m) {
+                if (m0 + 1 < M) {
                     mine[(m0 + 1) * 16 + gq] = acc[0][h][1] + acc[1][h][1];
                     mine[(m0 + 1) * 16 + gq + 8] = acc[0][h][3] + acc[1][h][3];
                 }
@@ -556,7 +571,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const __grid_cons
                 for (int e = 0; e < 2; ++e) acc[e][h][0] = acc[e][h][1] = acc[e][h][2] = acc[e][h][3] = 0.f;
             }
         }
-        if (++part < P.parts) continue;
+        if (++part < parts) continue;
         part = 0;
         // Count this warp in; the 16th warp to arrive reduces the unit.  A slot is
         // reused kSlots units later: by then its reducer is done, because a warp
@@ -572,32 +587,35 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const __grid_cons
         if (last) {
             __syncwarp();
             __threadfence_block();
-            const int sidx0 = P.parts == 2 ? 0 : cur;
+            const int sidx0 = parts == 2 ? 0 : cur;
             const MmaStore& S = P.st[sidx0];
-            const int rowbase = (P.parts == 2 ? u : u - S.unit0) * 16;
+            const int rowbase = (parts == 2 ? u : u - S.unit0) * 16;
             const float* base = slots + uslot * P.slot_floats;
-            const int per = 16 * P.m;   // floats per warp per part
+            const int per = 16 * M;   // floats per warp per part
+            const int n_rows = S.n;
+            void* const out = S.out;
+            const int64_t ldo = S.ldo;
             for (int e = lane; e < per; e += 32) {
                 const int rr = e & 15, mm = e >> 4;
                 const int row = rowbase + rr;
                 float v0 = 0.f, v1 = 0.f;
 #pragma unroll
                 for (int ww = 0; ww < kConsumerWarps; ++ww) v0 += base[ww * per + e];
-                if (P.parts == 2) {
+                if (parts == 2) {
 #pragma unroll
                     for (int ww = 0; ww < kConsumerWarps; ++ww) v1 += base[(kConsumerWarps + ww) * per + e];
                 }
-                if (row < S.n) {
-                    const int64_t o = (int64_t)mm * S.ldo + row;
+                if (row < n_rows) {
+                    const int64_t o = (int64_t)mm * ldo + row;
                     if (P.epilogue == EPQ_EPI_RESIDUAL) {
                         const int dt = kBf16 ? EPQ_BF16 : EPQ_F16;
-                        store_f(S.out, dt, o, load_f(S.out, dt, o) + round_to(v0, dt));
+                        store_f(out, dt, o, ld_act<kProg>(out, dt, o) + round_to(v0, dt));
                     } else if (P.epilogue == EPQ_EPI_SILU_MUL) {
                         const int dt = kBf16 ? EPQ_BF16 : EPQ_F16;
                         const float gv = round_to(v0, dt), uv = round_to(v1, dt);
-                        store_f(S.out, dt, o, gv / (1.f + expf(-gv)) * uv);
+                        store_f(out, dt, o, gv / (1.f + expf(-gv)) * uv);
                     } else {
-                        store_f(S.out, P.out_dtype, o, v0);
+                        store_f(out, P.out_dtype, o, v0);
                     }
                 }
             }
@@ -609,11 +627,383 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const __grid_cons
     }
 }
 
+template <bool kBf16, int kNT, bool kScaleF32, bool kXSmem>
+__global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const __grid_constant__ MmaParams P) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+    if (sbase + kLowBytes > kRepWin) {   // the layout needs the dynamic block to start low (uniform)
+        if (threadIdx.x == 0) atomicExch(&g_mma_wait_timeout, 1);
+        return;
+    }
+    const uint32_t bar_full = sbase;                       // kStages x 8 B
+    const uint32_t bar_empty = bar_full + 8 * kStages;     // kStages x 8 B
+    int* cnt = reinterpret_cast<int*>(smem + 16 * kStages);   // kSlots arrival counters
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int u_begin, u_end;
+    unit_range(P.total_units, u_begin, u_end);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(bar_full + 8 * s, 1);
+            mbar_init(bar_empty + 8 * s, kConsumerWarps);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (threadIdx.x < kSlots) cnt[threadIdx.x] = 0;
+    __syncthreads();
+
+    uint32_t ring = 0;
+    if (warp == kConsumerWarps) {
+        // Weights do not depend on the previous kernel: stream them right away.
+        produce_linear<kScaleF32>(P, u_begin, u_end, bar_full, bar_empty, sbase + kBarBytes, lane, ring);
+        pdl_trigger();
+        return;
+    }
+    uint2* rep = reinterpret_cast<uint2*>(smem + (kRepWin - sbase));
+    uint2* cb_stage = reinterpret_cast<uint2*>(smem + (kHighWin - sbase));
+    prepare_linear<kBf16>(P, u_begin, u_end, rep, cb_stage);
+    pdl_trigger();
+    pdl_wait();   // x (and the output buffers) belong to the previous kernel until here
+    run_linear<kBf16, kNT, kScaleF32, kXSmem, false>(P, u_begin, u_end, smem, sbase, ring);
+}
+
+// ---------------------------------------------------------------------------
+// Decode program: the steps of a whole decode token (every layer's fused packed
+// linears and its attention) run by ONE persistent cooperative kernel, one CTA
+// per SM.  The producer warp streams the weight chunks of all linear steps back
+// to back through the ring -- weights never depend on activations, so HBM keeps
+// streaming across step boundaries -- while the consumer warps run the steps in
+// order, separated by a grid-wide arrival counter per step (an activation step
+// needs every CTA's rows of the previous one).  A CTA rebuilds the codebook
+// replica for its next step while it waits for the others.
+// ---------------------------------------------------------------------------
+constexpr int kStepLinear = 0, kStepAttention = 1;
+constexpr int kProgMaxSplits = 16;
+constexpr uint32_t kGridSpinLimit = 1u << 23;   // grid-barrier polls (about a second with the naps)
+
+__device__ int g_prog_position_error = 0;
+
+struct AttnStep {
+    const uint16_t* q;       // [heads, hd] bf16 (this token's projections)
+    const uint16_t* k;       // [kv_heads, hd]
+    const uint16_t* v;
+    uint16_t* k_cache;       // [max_len, kv_heads, hd]
+    uint16_t* v_cache;
+    const int64_t* pos;      // device position of this token
+    int64_t max_len;
+    const float* cos_t;      // [max_len, hd / 2]
+    const float* sin_t;
+    uint16_t* out;           // [heads, hd]
+    int heads, kv_heads, head_dim, qk_norm, splits;
+    float eps, scale;
+};
+
+struct ProgStep {
+    MmaParams lin;
+    AttnStep attn;
+    int kind;
+};
+
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Consumers wait until every CTA has arrived at `bar` (thread 0 polls with
+// acquire loads, bounded; the consumer barrier passes the acquisition on).
+__device__ __forceinline__ void grid_wait(const unsigned* bar, unsigned target) {
+    if (threadIdx.x == 0) {
+        for (uint32_t n = 0; ld_acquire_u32(bar) < target; ++n) {
+            if (n == kGridSpinLimit) {
+                atomicExch(&g_mma_wait_timeout, 1);
+                break;
+            }
+            __nanosleep(64);
+        }
+    }
+    consumers_sync();
+}
+// The consumer barrier orders every consumer's writes of the step before thread
+// 0's release-add at GPU scope (the cumulative release publishes them).
+__device__ __forceinline__ void grid_arrive(unsigned* bar) {
+    consumers_sync();
+    if (threadIdx.x == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
+}
+
+__device__ __forceinline__ float bf16_bits(uint16_t r) { return __uint_as_float((uint32_t)r << 16); }
+__device__ __forceinline__ uint16_t to_bf16_bits(float v) { return __bfloat16_as_ushort(__float2bfloat16_rn(v)); }
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+    const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+constexpr int kAttnRows = 64;   // cache positions staged in shared memory per pass
+
+// Stages cache rows [base, base + cnt) of kv head kvh (except position P, which
+// comes from registers) into kst / vst with asynchronous 16-byte copies.
+template <int kDims>
+__device__ __forceinline__ void stage_kv(const AttnStep& A, int kvh, int64_t base, int cnt, int64_t P, uint16_t* kst,
+                                         uint16_t* vst) {
+    constexpr int hd = kDims * 32, pieces = hd / 8;
+    const int KV = A.kv_heads;
+    for (int i = threadIdx.x; i < cnt * pieces; i += kConsumers) {
+        const int r = i / pieces, c = i - r * pieces;
+        const int64_t t = base + r;
+        if (t == P) continue;
+        const int64_t off = (t * KV + kvh) * hd + c * 8;
+        cp_async16(kst + r * hd + c * 8, A.k_cache + off);
+        cp_async16(vst + r * hd + c * 8, A.v_cache + off);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+// Attention step.  The positions 0..P are split over S CTAs per kv head, S the
+// fewest splits (at most A.splits) that keep a CTA's range within kAttnRows, so
+// a short context needs no cross-CTA merge.  A CTA stages its K / V rows in
+// shared memory with asynchronous copies issued first, then applies (q/k
+// RMSNorm and) RoPE to q and to this position's k meanwhile; split 0 writes k, v
+// into the caches.  The kGroup query heads of the kv head share the 16 consumer
+// warps (16 / group per head, every (16 / group)-th position each, four
+// positions per step of the loop); per-warp online softmax, merged per head in
+// the CTA; with S > 1 one record per (split, head) goes to global memory and
+// the last CTA of the kv head merges them in split order.  Same arithmetic as
+// the epq_attn_rope_decode kernels (their split merge order aside).
+template <int kDims>
+__device__ void prog_attention(const AttnStep& A, float* scr, uint16_t* kst, uint16_t* vst, float* recs,
+                               unsigned* counters) {
+    constexpr int hd = kDims * 32, kRec = hd + 2;
+    const int KV = A.kv_heads, group = A.heads / KV;
+    const int blk = blockIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t P = A.pos[0];
+    if (P < 0 || P >= A.max_len) {   // every CTA sees the same position
+        if (blk < KV) {
+            for (int e = threadIdx.x; e < group * hd; e += kConsumers) A.out[(int64_t)blk * group * hd + e] = 0;
+            if (threadIdx.x == 0) atomicExch(&g_prog_position_error, 1);
+        }
+        return;
+    }
+    const int64_t n = P + 1;
+    const int S = (int)min((int64_t)A.splits, (n + kAttnRows - 1) / kAttnRows);
+    if (blk >= KV * S) return;
+    const int kvh = blk / S, split = blk - kvh * S;
+    const int wpg = kConsumerWarps / group;
+    const int g = warp / wpg, wsub = warp - g * wpg;
+    const int64_t chunk = (n + S - 1) / S;
+    const int64_t t0 = split * chunk, t1 = min(n, t0 + chunk);
+    int64_t base = t0;
+    int cnt = (int)min((int64_t)kAttnRows, t1 - base);
+    if (cnt > 0) stage_kv<kDims>(A, kvh, base, cnt, P, kst, vst);
+
+    const int qh = kvh * group + g;
+    float qv[kDims], acc[kDims], kc[kDims], vc[kDims];
+#pragma unroll
+    for (int d = 0; d < kDims; ++d) {
+        qv[d] = bf16_bits(__ldcg(A.q + (int64_t)qh * hd + lane * kDims + d));
+        kc[d] = bf16_bits(__ldcg(A.k + (int64_t)kvh * hd + lane * kDims + d));
+        vc[d] = bf16_bits(__ldcg(A.v + (int64_t)kvh * hd + lane * kDims + d));
+        acc[d] = 0.f;
+    }
+    rope_head<kDims>(qv, lane, P, A.cos_t, A.sin_t, A.qk_norm, A.eps);
+    rope_head<kDims>(kc, lane, P, A.cos_t, A.sin_t, A.qk_norm, A.eps);
+    if (split == 0 && warp == 0) {
+        const int64_t cb = (P * KV + kvh) * hd + lane * kDims;
+#pragma unroll
+        for (int d = 0; d < kDims; ++d) {
+            A.k_cache[cb + d] = to_bf16_bits(kc[d]);
+            A.v_cache[cb + d] = to_bf16_bits(vc[d]);
+        }
+    }
+    float m = -INFINITY, l = 0.f;
+    while (cnt > 0) {
+        cp_async_wait_all();
+        if (warp == 0 && P >= base && P < base + cnt) {   // this position from registers
+#pragma unroll
+            for (int d = 0; d < kDims; ++d) {
+                kst[(P - base) * hd + lane * kDims + d] = to_bf16_bits(kc[d]);
+                vst[(P - base) * hd + lane * kDims + d] = to_bf16_bits(vc[d]);
+            }
+        }
+        consumers_sync();
+        for (int j0 = wsub; j0 < cnt; j0 += 4 * wpg) {
+            float sc[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int j = j0 + u * wpg;
+                float s = 0.f;
+                if (j < cnt) {
+#pragma unroll
+                    for (int d = 0; d < kDims; ++d) s += qv[d] * bf16_bits(kst[j * hd + lane * kDims + d]);
+                }
+                sc[u] = s;
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+                for (int u = 0; u < 4; ++u) sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], o);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int j = j0 + u * wpg;
+                if (j >= cnt) break;
+                const float s = sc[u] * A.scale;
+                const float mn = fmaxf(m, s);
+                const float corr = expf(m - mn), pw = expf(s - mn);
+                l = l * corr + pw;
+#pragma unroll
+                for (int d = 0; d < kDims; ++d) acc[d] = acc[d] * corr + pw * bf16_bits(vst[j * hd + lane * kDims + d]);
+                m = mn;
+            }
+        }
+        base += cnt;
+        cnt = (int)min((int64_t)kAttnRows, t1 - base);
+        consumers_sync();   // every warp is done with the staged rows
+        if (cnt > 0) stage_kv<kDims>(A, kvh, base, cnt, P, kst, vst);
+    }
+    if (lane == 0) {
+        scr[warp * kRec + hd] = m;
+        scr[warp * kRec + hd + 1] = l;
+    }
+#pragma unroll
+    for (int d = 0; d < kDims; ++d) scr[warp * kRec + lane * kDims + d] = acc[d];
+    consumers_sync();
+    float* rec = recs + ((int64_t)(kvh * S + split) * group) * kRec;
+    for (int e = threadIdx.x; e < group * hd; e += kConsumers) {
+        const int gg = e / hd, d = e - gg * hd;
+        float mx = -INFINITY;
+        for (int w = gg * wpg; w < (gg + 1) * wpg; ++w) mx = fmaxf(mx, scr[w * kRec + hd]);
+        float num = 0.f, den = 0.f;
+        for (int w = gg * wpg; w < (gg + 1) * wpg; ++w) {
+            if (scr[w * kRec + hd] == -INFINITY) continue;   // a warp that saw no position
+            const float f = expf(scr[w * kRec + hd] - mx);
+            num += f * scr[w * kRec + d];
+            den += f * scr[w * kRec + hd + 1];
+        }
+        if (S == 1) {
+            A.out[(int64_t)(kvh * group + gg) * hd + d] = to_bf16_bits(num / den);
+        } else {
+            rec[gg * kRec + d] = num;
+            if (d == 0) {
+                rec[gg * kRec + hd] = mx;
+                rec[gg * kRec + hd + 1] = den;
+            }
+        }
+    }
+    if (S == 1) return;
+    __threadfence();
+    consumers_sync();
+    int* last = reinterpret_cast<int*>(scr + kConsumerWarps * kRec);
+    if (threadIdx.x == 0) *last = atomicAdd(&counters[kvh], 1u) == (unsigned)(S - 1);
+    consumers_sync();
+    if (!*last) return;
+    __threadfence();
+    // The S records' (max, sum) first, all loads in flight at once.
+    const float* rbase = recs + (int64_t)kvh * S * group * kRec;
+    float* ml = scr;   // [S][group][2]; the warp records are consumed
+    for (int i = threadIdx.x; i < S * group; i += kConsumers) {
+        ml[2 * i] = __ldcg(rbase + i * kRec + hd);
+        ml[2 * i + 1] = __ldcg(rbase + i * kRec + hd + 1);
+    }
+    consumers_sync();
+    for (int e = threadIdx.x; e < group * hd; e += kConsumers) {
+        const int gg = e / hd, d = e - gg * hd;
+        float v[kProgMaxSplits];
+#pragma unroll
+        for (int sp = 0; sp < kProgMaxSplits; ++sp)
+            v[sp] = sp < S ? __ldcg(rbase + (sp * group + gg) * kRec + d) : 0.f;
+        float mx = -INFINITY;
+        for (int sp = 0; sp < S; ++sp) mx = fmaxf(mx, ml[2 * (sp * group + gg)]);
+        float num = 0.f, den = 0.f;
+#pragma unroll
+        for (int sp = 0; sp < kProgMaxSplits; ++sp) {
+            if (sp >= S) break;
+            const float rm = ml[2 * (sp * group + gg)];
+            if (rm == -INFINITY) continue;   // an empty split
+            const float f = expf(rm - mx);
+            num += f * v[sp];
+            den += f * ml[2 * (sp * group + gg) + 1];
+        }
+        A.out[(int64_t)(kvh * group + gg) * hd + d] = to_bf16_bits(num / den);
+    }
+    if (threadIdx.x == 0) counters[kvh] = 0u;
+}
+
+template <bool kBf16, bool kScaleF32>
+__global__ void __launch_bounds__(kThreads, 1)
+    decode_program_kernel(const ProgStep* __restrict__ steps, int n_steps, unsigned* bars, unsigned* attn_counters,
+                          float* recs, uint32_t scr_off, uint32_t kv_off) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+    if (sbase + kLowBytes > kRepWin) {   // uniform over CTAs: every CTA returns here
+        if (threadIdx.x == 0) atomicExch(&g_mma_wait_timeout, 1);
+        return;
+    }
+    const uint32_t bar_full = sbase;
+    const uint32_t bar_empty = bar_full + 8 * kStages;
+    int* cnt = reinterpret_cast<int*>(smem + 16 * kStages);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(bar_full + 8 * s, 1);
+            mbar_init(bar_empty + 8 * s, kConsumerWarps);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (threadIdx.x < kSlots) cnt[threadIdx.x] = 0;
+    __syncthreads();
+
+    uint32_t ring = 0;
+    int u_begin, u_end;
+    if (warp == kConsumerWarps) {
+        for (int s = 0; s < n_steps; ++s) {
+            if (steps[s].kind != kStepLinear) continue;
+            unit_range(steps[s].lin.total_units, u_begin, u_end);
+            produce_linear<kScaleF32>(steps[s].lin, u_begin, u_end, bar_full, bar_empty, sbase + kBarBytes, lane,
+                                      ring);
+        }
+        return;
+    }
+    uint2* rep = reinterpret_cast<uint2*>(smem + (kRepWin - sbase));
+    uint2* cb_stage = reinterpret_cast<uint2*>(smem + (kHighWin - sbase));
+    float* scr = reinterpret_cast<float*>(smem + (scr_off - sbase));
+    // the staged K / V rows follow the warp records (16-byte aligned)
+    uint16_t* kst = reinterpret_cast<uint16_t*>(smem + (kv_off - sbase));
+    if (n_steps > 0 && steps[0].kind == kStepLinear) {
+        unit_range(steps[0].lin.total_units, u_begin, u_end);
+        prepare_linear<kBf16>(steps[0].lin, u_begin, u_end, rep, cb_stage);
+    }
+    for (int s = 0; s < n_steps; ++s) {
+        const ProgStep& T = steps[s];
+        if (s > 0) grid_wait(&bars[s - 1], gridDim.x);
+        if (T.kind == kStepLinear) {
+            unit_range(T.lin.total_units, u_begin, u_end);
+            if (u_begin < u_end) run_linear<kBf16, 1, kScaleF32, true, true>(T.lin, u_begin, u_end, smem, sbase, ring);
+        } else if (T.attn.head_dim == 128) {
+            prog_attention<4>(T.attn, scr, kst, kst + kAttnRows * 128, recs, attn_counters);
+        } else {
+            prog_attention<2>(T.attn, scr, kst, kst + kAttnRows * 64, recs, attn_counters);
+        }
+        grid_arrive(&bars[s]);
+        if (s + 1 < n_steps && steps[s + 1].kind == kStepLinear) {
+            // The next store's codebook does not depend on the other CTAs.
+            unit_range(steps[s + 1].lin.total_units, u_begin, u_end);
+            prepare_linear<kBf16>(steps[s + 1].lin, u_begin, u_end, rep, cb_stage);
+        }
+    }
+}
+
 }  // namespace
 
+// Bit 0: a bounded wait gave up (GEMV or decode program); bit 1: a decode
+// program's position was outside its KV caches.
 int mma_read_device_error(int* flag) {
-    if (cudaMemcpyFromSymbol(flag, g_mma_wait_timeout, sizeof(int)) != cudaSuccess)
-        return check_launch("read gemv_mma error flag");
+    int w = 0, p = 0;
+    if (cudaMemcpyFromSymbol(&w, g_mma_wait_timeout, sizeof(int)) != cudaSuccess ||
+        cudaMemcpyFromSymbol(&p, g_prog_position_error, sizeof(int)) != cudaSuccess)
+        return check_launch("read gemv_mma error flags");
+    *flag = (w ? 1 : 0) | (p ? 2 : 0);
     return EPQ_OK;
 }
 
@@ -628,17 +1018,18 @@ bool mma_eligible(const StoreD& s, int64_t m, int x_dtype) {
            s.k > 0 && s.k < (1 << 30);
 }
 
-int launch_linear_mma_fused(const StoreD* s, int count, const void* x, int x_dtype, int64_t m, int64_t ldx,
+// Checks a fused GEMV and fills its parameters (everything but x_off); `fixed`
+// = shared bytes below the staged activations, `xbytes` = their size.
+static int build_mma_params(const StoreD* s, int count, const void* x, int x_dtype, int64_t m, int64_t ldx,
                             void* const* outs, const int64_t* ldo, int out_dtype, int prologue, int epilogue,
-                            float eps, cudaStream_t st) {
+                            float eps, MmaParams& P, int& fixed, int64_t& xbytes) {
     if ((reinterpret_cast<uintptr_t>(x) & 7) || (ldx & 3))
         return set_error(EPQ_EALIGN, "linear: x must be 8-byte aligned with ldx a multiple of 4");
-    const bool bf = x_dtype == EPQ_BF16;
-    const int nt = m > 8 ? 2 : 1;
     const bool sf32 = s[0].scale_dtype == EPQ_F32;
     for (int i = 1; i < count; ++i)
         if ((s[i].scale_dtype == EPQ_F32) != sf32)
             return set_error(EPQ_EDTYPE, "linear: fused stores need one scale dtype");
+    (void)x_dtype;
     const int parts = epilogue == EPQ_EPI_SILU_MUL ? 2 : 1;
     if (parts == 2 && (count != 2 || s[0].n != s[1].n))
         return set_error(EPQ_ESHAPE, "decode linear: the SiLU epilogue takes two stores of equal rows");
@@ -647,36 +1038,12 @@ int launch_linear_mma_fused(const StoreD* s, int count, const void* x, int x_dty
     if (epilogue != EPQ_EPI_STORE && out_dtype != x_dtype)
         return set_error(EPQ_EDTYPE, "decode linear: fused epilogues write the activation dtype");
     const int64_t kpad = s[0].ng * 128;
-    const int64_t xbytes = m * kpad * 2;
+    xbytes = m * kpad * 2;
     const int slot_floats = parts * kConsumerWarps * 16 * (int)m;
     // Requested as if the dynamic block started at window address 0 (it starts a
     // little above, so the request always covers the layout).
-    const int fixed = (int)kHighWin + kSlots * slot_floats * 4;
-    const bool xsm = xbytes <= kMaxXSmem && fixed + xbytes <= kMaxSmem;
-    if (prologue == EPQ_PRO_RMSNORM && !xsm)
-        return set_error(EPQ_EUNSUPPORTED, "decode linear: RMSNorm prologue needs m*k*2 <= %d bytes", kMaxXSmem);
-    if (fixed > kMaxSmem)
-        return set_error(EPQ_EUNSUPPORTED, "decode linear: m=%lld needs %d bytes of shared memory", (long long)m,
-                         fixed);
-    const int smem = fixed + (xsm ? (int)xbytes : 0);
-    const int variant = (bf ? 1 : 0) + (nt == 2 ? 2 : 0) + (sf32 ? 4 : 0) + (xsm ? 8 : 0);
-    using KernT = void (*)(MmaParams);
-    static const KernT kernels[16] = {
-        gemv_mma_kernel<false, 1, false, false>, gemv_mma_kernel<true, 1, false, false>,
-        gemv_mma_kernel<false, 2, false, false>, gemv_mma_kernel<true, 2, false, false>,
-        gemv_mma_kernel<false, 1, true, false>,  gemv_mma_kernel<true, 1, true, false>,
-        gemv_mma_kernel<false, 2, true, false>,  gemv_mma_kernel<true, 2, true, false>,
-        gemv_mma_kernel<false, 1, false, true>,  gemv_mma_kernel<true, 1, false, true>,
-        gemv_mma_kernel<false, 2, false, true>,  gemv_mma_kernel<true, 2, false, true>,
-        gemv_mma_kernel<false, 1, true, true>,   gemv_mma_kernel<true, 1, true, true>,
-        gemv_mma_kernel<false, 2, true, true>,   gemv_mma_kernel<true, 2, true, true>};
-    const KernT kern = kernels[variant];
-    {
-        const int arc = set_smem_limit(reinterpret_cast<const void*>(kern), kMaxSmem,
-                                       "cudaFuncSetAttribute(gemv_mma_kernel)");
-        if (arc != EPQ_OK) return arc;
-    }
-    MmaParams P{};
+    fixed = (int)kHighWin + kSlots * slot_floats * 4;
+    P = MmaParams{};
     P.count = count;
     P.x = x;
     P.ldx = ldx;
@@ -690,7 +1057,6 @@ int launch_linear_mma_fused(const StoreD* s, int count, const void* x, int x_dty
     P.epilogue = epilogue;
     P.eps = eps;
     P.slot_floats = slot_floats;
-    P.x_off = fixed;
     int64_t units = 0;
     for (int i = 0; i < count; ++i) {
         MmaStore& S = P.st[i];
@@ -715,8 +1081,50 @@ int launch_linear_mma_fused(const StoreD* s, int count, const void* x, int x_dty
     if (parts == 2) units = s[0].rb;
     if (units >= (int64_t(1) << 30)) return set_error(EPQ_EUNSUPPORTED, "linear: too many rows");
     P.total_units = (int)units;
+    return EPQ_OK;
+}
+
+int launch_linear_mma_fused(const StoreD* s, int count, const void* x, int x_dtype, int64_t m, int64_t ldx,
+                            void* const* outs, const int64_t* ldo, int out_dtype, int prologue, int epilogue,
+                            float eps, cudaStream_t st) {
+    const bool bf = x_dtype == EPQ_BF16;
+    const int nt = m > 8 ? 2 : 1;
+    MmaParams P;
+    int fixed = 0;
+    int64_t xbytes = 0;
+    {
+        const int rc = build_mma_params(s, count, x, x_dtype, m, ldx, outs, ldo, out_dtype, prologue, epilogue, eps,
+                                        P, fixed, xbytes);
+        if (rc != EPQ_OK) return rc;
+    }
+    const bool sf32 = s[0].scale_dtype == EPQ_F32;
+    const bool xsm = xbytes <= kMaxXSmem && fixed + xbytes <= kMaxSmem;
+    if (prologue == EPQ_PRO_RMSNORM && !xsm)
+        return set_error(EPQ_EUNSUPPORTED, "decode linear: RMSNorm prologue needs m*k*2 <= %d bytes", kMaxXSmem);
+    if (fixed > kMaxSmem)
+        return set_error(EPQ_EUNSUPPORTED, "decode linear: m=%lld needs %d bytes of shared memory", (long long)m,
+                         fixed);
+    const int smem = fixed + (xsm ? (int)xbytes : 0);
+    P.x_off = fixed;
+    const int variant = (bf ? 1 : 0) + (nt == 2 ? 2 : 0) + (sf32 ? 4 : 0) + (xsm ? 8 : 0);
+    using KernT = void (*)(MmaParams);
+    static const KernT kernels[16] = {
+        gemv_mma_kernel<false, 1, false, false>, gemv_mma_kernel<true, 1, false, false>,
+        gemv_mma_kernel<false, 2, false, false>, gemv_mma_kernel<true, 2, false, false>,
+        gemv_mma_kernel<false, 1, true, false>,  gemv_mma_kernel<true, 1, true, false>,
+        gemv_mma_kernel<false, 2, true, false>,  gemv_mma_kernel<true, 2, true, false>,
+        gemv_mma_kernel<false, 1, false, true>,  gemv_mma_kernel<true, 1, false, true>,
+        gemv_mma_kernel<false, 2, false, true>,  gemv_mma_kernel<true, 2, false, true>,
+        gemv_mma_kernel<false, 1, true, true>,   gemv_mma_kernel<true, 1, true, true>,
+        gemv_mma_kernel<false, 2, true, true>,   gemv_mma_kernel<true, 2, true, true>};
+    const KernT kern = kernels[variant];
+    {
+        const int arc = set_smem_limit(reinterpret_cast<const void*>(kern), kMaxSmem,
+                                       "cudaFuncSetAttribute(gemv_mma_kernel)");
+        if (arc != EPQ_OK) return arc;
+    }
     int grid = device_sms();
-    if (grid > units) grid = (int)units;
+    if (grid > P.total_units) grid = P.total_units;
 
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -769,4 +1177,231 @@ extern "C" int epq_decode_linear(const epq_store* stores, int32_t count, const v
     if (ldx < s[0].k) return set_error(EPQ_ESHAPE, "epq_decode_linear: ldx < k");
     return launch_linear_mma_fused(s, count, x, x_dtype, m, ldx, outs, ldo, x_dtype, prologue, epilogue, eps,
                                    static_cast<cudaStream_t>(stream));
+}
+
+// ---------------------------------------------------------------------------
+// decode program (host side)
+// ---------------------------------------------------------------------------
+struct epq_program {
+    std::vector<ProgStep> steps;
+    bool sf32 = false, sf32_set = false, finalized = false;
+    int max_xbytes = 0, max_slot_floats = 0;
+    int max_kv = 0, max_heads = 0, max_hd = 0;
+    int grid = 0, splits = 1;
+    int64_t steps_bytes = 0, bars_off = 0, counters_off = 0, recs_off = 0, total_bytes = 0;
+    uint8_t* ws = nullptr;
+};
+
+namespace epq {
+namespace {
+
+int program_layout(epq_program* p) {
+    p->grid = device_sms();
+    if (p->grid <= 0) return check_launch("decode program: SM count");
+    p->splits = 1;
+    if (p->max_kv > 0) p->splits = std::max(1, std::min(kProgMaxSplits, p->grid / p->max_kv));
+    auto up = [](int64_t v) { return (v + 255) & ~int64_t(255); };
+    const int64_t n = (int64_t)p->steps.size();
+    p->steps_bytes = up(n * (int64_t)sizeof(ProgStep));
+    p->bars_off = p->steps_bytes;
+    p->counters_off = p->bars_off + up(std::max<int64_t>(n, 1) * 4);
+    p->recs_off = p->counters_off + up(std::max(p->max_kv, 1) * 4);
+    p->total_bytes = p->recs_off + up((int64_t)p->splits * std::max(p->max_heads, 1) * (p->max_hd + 2) * 4);
+    return EPQ_OK;
+}
+
+// Shared bytes: the GEMV layout (replicas, slots), the staged activations of the
+// widest step, the attention scratch (16 warp records + a flag), then the
+// attention's staged K / V rows.
+int program_smem(const epq_program* p, int* x_off, int* scr_off, int* kv_off) {
+    const int fixed = (int)kHighWin + kSlots * std::max(p->max_slot_floats, 1) * 4;
+    const int hd = std::max(p->max_hd, 64);
+    *x_off = fixed;
+    *scr_off = fixed + ((p->max_xbytes + 15) & ~15);
+    *kv_off = *scr_off + (((kConsumerWarps * (hd + 2) + 4) * 4 + 15) & ~15);
+    return *kv_off + (p->max_hd > 0 ? 2 * kAttnRows * hd * 2 : 0);
+}
+
+}  // namespace
+}  // namespace epq
+
+extern "C" int epq_program_create(epq_program** out) {
+    if (!out) return set_error(EPQ_EINVAL, "epq_program_create: out is NULL");
+    *out = new (std::nothrow) epq_program();
+    if (!*out) return set_error(EPQ_EINVAL, "epq_program_create: out of host memory");
+    return EPQ_OK;
+}
+
+extern "C" void epq_program_destroy(epq_program* p) { delete p; }
+
+extern "C" int epq_program_add_linear(epq_program* p, const epq_store* stores, int32_t count, const void* x,
+                                      int64_t ldx, int32_t prologue, float eps, void* const* outs,
+                                      const int64_t* ldo, int32_t epilogue) {
+    if (!p || !stores || !x || !outs || count < 1 || count > kLutMaxStores)
+        return set_error(EPQ_EINVAL, "epq_program_add_linear: bad arguments");
+    if (p->finalized) return set_error(EPQ_EINVAL, "epq_program_add_linear: the program is finalized");
+    if (prologue != EPQ_PRO_NONE && prologue != EPQ_PRO_RMSNORM)
+        return set_error(EPQ_EINVAL, "epq_program_add_linear: prologue=%d", prologue);
+    if (epilogue != EPQ_EPI_STORE && epilogue != EPQ_EPI_RESIDUAL && epilogue != EPQ_EPI_SILU_MUL)
+        return set_error(EPQ_EINVAL, "epq_program_add_linear: epilogue=%d", epilogue);
+    StoreD s[kLutMaxStores];
+    for (int i = 0; i < count; ++i) {
+        const int rc = make_store(&stores[i], &s[i], "epq_program_add_linear");
+        if (rc != EPQ_OK) return rc;
+        if (!mma_eligible(s[i], 1, EPQ_BF16))
+            return set_error(EPQ_ELAYOUT,
+                             "epq_program_add_linear: store %d is not an EPQ_LAYOUT_MMA16 vec-4 group-128 store "
+                             "with group-major f16/f32 scales",
+                             i);
+        if (s[i].k != s[0].k) return set_error(EPQ_ESHAPE, "epq_program_add_linear: stores differ in k");
+        if (!outs[i]) return set_error(EPQ_EINVAL, "epq_program_add_linear: output %d is NULL", i);
+        if (ldo && ldo[i] < s[i].n) return set_error(EPQ_ESHAPE, "epq_program_add_linear: ldo[%d] < n", i);
+        if ((reinterpret_cast<uintptr_t>(outs[i]) & 1))
+            return set_error(EPQ_EALIGN, "epq_program_add_linear: output %d is not 2-byte aligned", i);
+    }
+    if (ldx < s[0].k) return set_error(EPQ_ESHAPE, "epq_program_add_linear: ldx < k");
+    const bool sf32 = s[0].scale_dtype == EPQ_F32;
+    if (p->sf32_set && sf32 != p->sf32)
+        return set_error(EPQ_EDTYPE, "epq_program_add_linear: every step needs the same scale dtype");
+    ProgStep T{};
+    T.kind = kStepLinear;
+    int fixed = 0;
+    int64_t xbytes = 0;
+    const int rc = build_mma_params(s, count, x, EPQ_BF16, 1, ldx, outs, ldo, EPQ_BF16, prologue, epilogue, eps,
+                                    T.lin, fixed, xbytes);
+    if (rc != EPQ_OK) return rc;
+    if (xbytes > kMaxXSmem)
+        return set_error(EPQ_EUNSUPPORTED, "epq_program_add_linear: k=%lld is wider than %d staged values",
+                         (long long)s[0].k, kMaxXSmem / 2);
+    p->sf32 = sf32;
+    p->sf32_set = true;
+    p->max_xbytes = std::max(p->max_xbytes, (int)xbytes);
+    p->max_slot_floats = std::max(p->max_slot_floats, T.lin.slot_floats);
+    p->steps.push_back(T);
+    return EPQ_OK;
+}
+
+extern "C" int epq_program_add_attention(epq_program* p, const void* q, const void* k, const void* v,
+                                         const int64_t* pos, int32_t heads, int32_t kv_heads, int32_t head_dim,
+                                         const float* cos_tab, const float* sin_tab, void* k_cache, void* v_cache,
+                                         int64_t max_len, int32_t qk_norm, float eps, float scale, void* out) {
+    if (!p || !q || !k || !v || !pos || !cos_tab || !sin_tab || !k_cache || !v_cache || !out)
+        return set_error(EPQ_EINVAL, "epq_program_add_attention: NULL pointer");
+    if (p->finalized) return set_error(EPQ_EINVAL, "epq_program_add_attention: the program is finalized");
+    if (head_dim != 64 && head_dim != 128)
+        return set_error(EPQ_EUNSUPPORTED, "epq_program_add_attention: head_dim=%d (64 or 128)", head_dim);
+    if (kv_heads < 1 || heads < kv_heads || heads % kv_heads)
+        return set_error(EPQ_ESHAPE, "epq_program_add_attention: heads=%d kv_heads=%d", heads, kv_heads);
+    const int group = heads / kv_heads;
+    if (group > kConsumerWarps || kConsumerWarps % group)
+        return set_error(EPQ_EUNSUPPORTED, "epq_program_add_attention: %d query heads per kv head (1, 2, 4, 8, 16)",
+                         group);
+    if (max_len < 1) return set_error(EPQ_ESHAPE, "epq_program_add_attention: max_len=%lld", (long long)max_len);
+    const uintptr_t al = reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
+                         reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(k_cache) |
+                         reinterpret_cast<uintptr_t>(v_cache) | reinterpret_cast<uintptr_t>(out);
+    if (al & 1) return set_error(EPQ_EALIGN, "epq_program_add_attention: bf16 tensors must be 2-byte aligned");
+    if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15)
+        return set_error(EPQ_EALIGN, "epq_program_add_attention: the KV caches must be 16-byte aligned");
+    ProgStep T{};
+    T.kind = kStepAttention;
+    AttnStep& A = T.attn;
+    A.q = static_cast<const uint16_t*>(q);
+    A.k = static_cast<const uint16_t*>(k);
+    A.v = static_cast<const uint16_t*>(v);
+    A.k_cache = static_cast<uint16_t*>(k_cache);
+    A.v_cache = static_cast<uint16_t*>(v_cache);
+    A.pos = pos;
+    A.max_len = max_len;
+    A.cos_t = cos_tab;
+    A.sin_t = sin_tab;
+    A.out = static_cast<uint16_t*>(out);
+    A.heads = heads;
+    A.kv_heads = kv_heads;
+    A.head_dim = head_dim;
+    A.qk_norm = qk_norm;
+    A.eps = eps;
+    A.scale = scale;
+    p->max_kv = std::max(p->max_kv, (int)kv_heads);
+    p->max_heads = std::max(p->max_heads, (int)heads);
+    p->max_hd = std::max(p->max_hd, (int)head_dim);
+    p->steps.push_back(T);
+    return EPQ_OK;
+}
+
+extern "C" int64_t epq_program_workspace_bytes(epq_program* p) {
+    if (!p) return set_error(EPQ_EINVAL, "epq_program_workspace_bytes: NULL program");
+    const int rc = program_layout(p);
+    if (rc != EPQ_OK) return rc;
+    return p->total_bytes;
+}
+
+extern "C" int epq_program_finalize(epq_program* p, void* workspace, int64_t workspace_bytes, void* stream) {
+    if (!p || !workspace) return set_error(EPQ_EINVAL, "epq_program_finalize: NULL argument");
+    if (p->steps.empty()) return set_error(EPQ_EINVAL, "epq_program_finalize: the program has no steps");
+    if (reinterpret_cast<uintptr_t>(workspace) & 255)
+        return set_error(EPQ_EALIGN, "epq_program_finalize: workspace must be 256-byte aligned");
+    int rc = program_layout(p);
+    if (rc != EPQ_OK) return rc;
+    if (workspace_bytes < p->total_bytes)
+        return set_error(EPQ_ESHAPE, "epq_program_finalize: workspace of %lld bytes, %lld needed",
+                         (long long)workspace_bytes, (long long)p->total_bytes);
+    int x_off = 0, scr_off = 0, kv_off = 0;
+    if (program_smem(p, &x_off, &scr_off, &kv_off) > kMaxSmem)
+        return set_error(EPQ_EUNSUPPORTED, "epq_program_finalize: needs more shared memory than an SM has");
+    for (ProgStep& T : p->steps) {
+        if (T.kind == kStepLinear) T.lin.x_off = x_off;
+        else T.attn.splits = p->splits;
+    }
+    p->ws = static_cast<uint8_t*>(workspace);
+    // The table must outlive the copy: it stays in the program object.
+    if (cudaMemcpyAsync(p->ws, p->steps.data(), p->steps.size() * sizeof(ProgStep), cudaMemcpyHostToDevice,
+                        static_cast<cudaStream_t>(stream)) != cudaSuccess)
+        return check_launch("epq_program_finalize: step table copy");
+    if (cudaMemsetAsync(p->ws + p->counters_off, 0, p->recs_off - p->counters_off,
+                        static_cast<cudaStream_t>(stream)) != cudaSuccess)
+        return check_launch("epq_program_finalize: counters");
+    if (cudaStreamSynchronize(static_cast<cudaStream_t>(stream)) != cudaSuccess)
+        return check_launch("epq_program_finalize");
+    p->finalized = true;
+    return EPQ_OK;
+}
+
+extern "C" int epq_program_run(epq_program* p, void* stream) {
+    if (!p) return set_error(EPQ_EINVAL, "epq_program_run: NULL program");
+    if (!p->finalized) return set_error(EPQ_EINVAL, "epq_program_run: finalize the program first");
+    if (device_sms() != p->grid)
+        return set_error(EPQ_EINVAL, "epq_program_run: the program was finalized for another device");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int x_off = 0, scr_off = 0, kv_off = 0;
+    const int smem = program_smem(p, &x_off, &scr_off, &kv_off);
+    using KernT = void (*)(const ProgStep*, int, unsigned*, unsigned*, float*, uint32_t, uint32_t);
+    static const KernT kernels[2] = {decode_program_kernel<true, false>, decode_program_kernel<true, true>};
+    const KernT kern = kernels[p->sf32 ? 1 : 0];
+    {
+        const int arc = set_smem_limit(reinterpret_cast<const void*>(kern), kMaxSmem,
+                                       "cudaFuncSetAttribute(decode_program_kernel)");
+        if (arc != EPQ_OK) return arc;
+    }
+    // Step counters start from zero every token (one memset node in a graph).
+    if (cudaMemsetAsync(p->ws + p->bars_off, 0, p->counters_off - p->bars_off, st) != cudaSuccess)
+        return check_launch("epq_program_run: step counters");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p->grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;   // every CTA resident: the step counters are grid barriers
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const ProgStep* steps = reinterpret_cast<const ProgStep*>(p->ws);
+    unsigned* bars = reinterpret_cast<unsigned*>(p->ws + p->bars_off);
+    unsigned* counters = reinterpret_cast<unsigned*>(p->ws + p->counters_off);
+    float* recs = reinterpret_cast<float*>(p->ws + p->recs_off);
+    if (cudaLaunchKernelEx(&cfg, kern, steps, (int)p->steps.size(), bars, counters, recs, (uint32_t)scr_off,
+                           (uint32_t)kv_off) != cudaSuccess)
+        return check_launch("decode_program_kernel");
+    return check_launch("decode_program_kernel");
 }

@@ -59,7 +59,9 @@ EXPORTS = (
     "epq_chain_workspace_bytes", "epq_chain_prepare", "epq_chain_run", "epq_chain_set_tp",
     "epq_add_rmsnorm", "epq_rope_kv", "epq_attn_decode", "epq_attn_decode_workspace_bytes",
     "epq_silu_mul", "epq_argmax", "epq_argmax_workspace_bytes", "epq_attn_rope_decode",
-    "epq_embedding", "epq_decode_linear",
+    "epq_embedding", "epq_decode_linear", "epq_program_create", "epq_program_add_linear",
+    "epq_program_add_attention", "epq_program_workspace_bytes", "epq_program_finalize", "epq_program_run",
+    "epq_program_destroy",
 )
 
 _lib = None
@@ -113,6 +115,15 @@ def load_library(path=None):
         lib.epq_argmax_workspace_bytes.argtypes = []
         lib.epq_silu_mul.argtypes = [P, P, P, I64, I32, P]
         lib.epq_decode_linear.argtypes = [SP, I32, P, I32, I64, I64, I32, F32, P, P, I32, P]
+        lib.epq_program_create.argtypes = [ctypes.POINTER(P)]
+        lib.epq_program_add_linear.argtypes = [P, SP, I32, P, I64, I32, F32, P, P, I32]
+        lib.epq_program_add_attention.argtypes = [P, P, P, P, P, I32, I32, I32, P, P, P, P, I64, I32, F32, F32, P]
+        lib.epq_program_workspace_bytes.restype = I64
+        lib.epq_program_workspace_bytes.argtypes = [P]
+        lib.epq_program_finalize.argtypes = [P, P, I64, P]
+        lib.epq_program_run.argtypes = [P, P]
+        lib.epq_program_destroy.restype = None
+        lib.epq_program_destroy.argtypes = [P]
         for name in EXPORTS:
             getattr(lib, name)          # every declared entry point must be exported
         if lib.epq_abi_version() != 1:
@@ -478,3 +489,69 @@ def decode_linear(x, stores, prologue=PRO_NONE, epilogue=EPI_STORE, outs=None, e
                                  int(prologue), float(eps), out_ptrs, ldo, int(epilogue),
                                  _stream_ptr(x.device)), "epq_decode_linear")
     return outs
+
+
+class DecodeProgram:
+    """A whole decode token as one persistent kernel (epq_program_*).
+
+    Record the token's steps in order with ``linear`` (as ``decode_linear``, m = 1)
+    and ``attention`` (as ``attn_rope_decode``), then ``finalize()`` once and
+    ``run()`` per token.  The program keeps the data pointers of every tensor it
+    was given: they (and the stores) must stay alive and in place; the object
+    holds references to them."""
+
+    def __init__(self, device):
+        self.lib = load_library()
+        self.device = torch.device(device)
+        self._keep = []
+        h = ctypes.c_void_p()
+        _check(self.lib.epq_program_create(ctypes.byref(h)), "epq_program_create")
+        self._h = h
+        self.ws = None
+        self.steps = 0
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h is not None and h.value:
+            self.lib.epq_program_destroy(h)
+            self._h = None
+
+    def linear(self, x, stores, outs, prologue=PRO_NONE, epilogue=EPI_STORE, eps=1e-6):
+        k = stores[0].in_features
+        if x.dtype != torch.bfloat16 or x.device != self.device or x.numel() != k or not x.is_contiguous():
+            raise RuntimeError("epure: a program linear takes one contiguous bf16 row of k values on its device")
+        count = len(stores)
+        for o in outs:
+            if o.dtype != x.dtype or o.device != x.device or not o.is_contiguous():
+                raise RuntimeError("epure: program outputs must be contiguous bf16 rows on the program's device")
+        wr = outs if len(outs) == count else outs + [outs[0]] * (count - len(outs))
+        descs = (EpqStore * count)(*[describe_store(s) for s in stores])
+        out_ptrs = (ctypes.c_void_p * count)(*[o.data_ptr() for o in wr])
+        ldo = (ctypes.c_int64 * count)(*[s.out_features for s in stores])
+        _check(self.lib.epq_program_add_linear(self._h, descs, count, x.data_ptr(), k, int(prologue), float(eps),
+                                               out_ptrs, ldo, int(epilogue)), "epq_program_add_linear")
+        self._keep += [x, *outs, *stores]
+        self.steps += 1
+
+    def attention(self, q, k, v, pos, cos, sin, k_cache, v_cache, qk_norm, eps, scale, out):
+        H, hd = q.shape[-2], q.shape[-1]
+        _check(self.lib.epq_program_add_attention(
+            self._h, q.data_ptr(), k.data_ptr(), v.data_ptr(), pos.data_ptr(), H, k.shape[-2], hd,
+            cos.data_ptr(), sin.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape[0],
+            int(qk_norm), float(eps), float(scale), out.data_ptr()), "epq_program_add_attention")
+        self._keep += [q, k, v, pos, cos, sin, k_cache, v_cache, out]
+        self.steps += 1
+
+    def finalize(self):
+        with torch.cuda.device(self.device):
+            n = int(self.lib.epq_program_workspace_bytes(self._h))
+            if n < 0:
+                _check(n, "epq_program_workspace_bytes")
+            self.ws = torch.empty(n, dtype=torch.uint8, device=self.device)
+            _check(self.lib.epq_program_finalize(self._h, self.ws.data_ptr(), n, _stream_ptr(self.device)),
+                   "epq_program_finalize")
+        return self
+
+    def run(self):
+        with torch.cuda.device(self.device):
+            _check(self.lib.epq_program_run(self._h, _stream_ptr(self.device)), "epq_program_run")

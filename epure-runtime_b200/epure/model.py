@@ -7,11 +7,12 @@ written out directly -- the Llama-3 / Qwen3 block: RMSNorm, q/k/v, (Qwen3:
 per-head q/k RMSNorm), RoPE, grouped-query attention over a static KV cache, o,
 residual, RMSNorm, SwiGLU gate/up/down, residual; final RMSNorm; lm_head -- so
 that a decode step has static shapes and can be captured in one CUDA graph.
-Per token the ``7 x layers`` packed linears run through libepq.so (q/k/v and
-gate/up as one launch each), and so do the block's non-linear parts at decode
-(include/epq_decode.h: residual add + RMSNorm, q/k norm + RoPE + KV write,
-attention, SiLU * up; ``fused_glue=False`` runs them as torch ops instead); the
-prompt (prefill) and the lm_head use torch.
+Per token the ``7 x layers`` packed linears run through libepq.so, and so do the
+block's non-linear parts at decode (include/epq_decode.h: RMSNorm, q/k norm +
+RoPE + KV write, attention, SiLU * up, the residual adds): by default every
+layer is five launches (epq_decode_linear / epq_attn_rope_decode); with
+``program=True`` the same steps of all layers run inside ONE persistent kernel
+per token (epq_program_run); ``fused_glue=False`` runs the glue as torch ops.  The prompt (prefill) and the lm_head use torch.
 
 Weights are random (no checkpoints offline): the packed stores of
 ``synthetic.LinearStack``, a bf16 N(0, 0.02) embedding (tied to lm_head for
@@ -44,7 +45,7 @@ _EPS = {"qwen3-1.7b": 1e-6, "llama3-8b": 1e-5, "llama3-70b": 1e-5}
 class PackedDecoder:
     def __init__(self, shapes, layers=None, device="cuda", seed=0, max_len=512,
                  linear_mode="ours", stack=None, embed=None, lm_head=None, fp32_logits=True,
-                 fused_glue=True, gpu_layout="mma16"):
+                 fused_glue=True, gpu_layout="mma16", program=False):
         if linear_mode not in ("ours", "reference", "fp32"):
             raise ValueError("linear_mode must be 'ours', 'reference' or 'fp32'")
         self.shapes = shapes
@@ -83,6 +84,9 @@ class PackedDecoder:
             self.attn_ws = _native.attn_decode_workspace(shapes.heads, shapes.kv_heads, hd, self.device)
             self.arg_ws = _native.argmax_workspace(self.device)
         self._fusable = all(st.layout == "mma16" for b in self.stack.blocks for st in b.values())
+        # One persistent kernel per token (epq_program_*) instead of five launches per layer.
+        self.use_program = program and self._fusable and self.fused_glue and self.dtype == torch.bfloat16
+        self._program = None
 
     def share_weights(self, linear_mode):
         """The same model (stores, embedding, lm_head) with another linear mode."""
@@ -149,6 +153,43 @@ class PackedDecoder:
             _native.decode_linear(a, [b["down_proj"]], epilogue=_native.EPI_RESIDUAL, outs=[h])
         return self._logits(_native.add_rmsnorm(h, eps=self.eps))
 
+    def _build_program(self):
+        """Records every layer's five fused steps (as ``_decode_fused`` launches
+        them) into one decode program over fixed buffers."""
+        sh = self.shapes
+        H, KV, hd = sh.heads, sh.kv_heads, sh.head_dim
+        dev, bf = self.device, torch.bfloat16
+        self._ph = torch.zeros(1, sh.hidden, dtype=bf, device=dev)        # residual stream
+        self._ppos = torch.zeros(1, dtype=torch.long, device=dev)
+        q = torch.empty(H * hd, dtype=bf, device=dev)
+        k = torch.empty(KV * hd, dtype=bf, device=dev)
+        v = torch.empty(KV * hd, dtype=bf, device=dev)
+        att = torch.empty(H * hd, dtype=bf, device=dev)
+        act = torch.empty(sh.intermediate, dtype=bf, device=dev)
+        prog = _native.DecodeProgram(dev)
+        for li, b in enumerate(self.stack.blocks):
+            prog.linear(self._ph, [b["q_proj"], b["k_proj"], b["v_proj"]], [q, k, v],
+                        prologue=_native.PRO_RMSNORM, eps=self.eps)
+            prog.attention(q.view(H, hd), k.view(KV, hd), v.view(KV, hd), self._ppos, self.cos, self.sin,
+                           self.k_cache[li], self.v_cache[li], self.qk_norm, self.eps, 1.0 / math.sqrt(hd),
+                           att.view(H, hd))
+            prog.linear(att, [b["o_proj"]], [self._ph], epilogue=_native.EPI_RESIDUAL)
+            prog.linear(self._ph, [b["gate_proj"], b["up_proj"]], [act], prologue=_native.PRO_RMSNORM,
+                        epilogue=_native.EPI_SILU_MUL, eps=self.eps)
+            prog.linear(act, [b["down_proj"]], [self._ph], epilogue=_native.EPI_RESIDUAL)
+        self._program = prog.finalize()
+
+    def _decode_program(self, ids, pos):
+        """One token as ONE persistent kernel (epq_program_run) plus the final
+        RMSNorm, lm_head and the token's input copies: the same steps and
+        rounding points as ``_decode_fused``."""
+        if self._program is None:
+            self._build_program()
+        torch.index_select(self.embed, 0, ids.reshape(-1), out=self._ph)
+        self._ppos.copy_(pos.reshape(-1)[:1])
+        self._program.run()
+        return self._logits(_native.add_rmsnorm(self._ph, eps=self.eps))
+
     def _decode_unfused(self, ids, pos):
         """One token with the per-linear launches and the separate glue kernels
         (residual add + RMSNorm, RoPE + KV write + attention, SiLU * up)."""
@@ -172,6 +213,8 @@ class PackedDecoder:
         """Logits (float32) of the last position of ``ids`` [T] at positions ``pos`` [T];
         writes the KV cache at those positions.  Static shapes for a fixed T."""
         if self.mode == "ours" and ids.shape[0] == 1 and self.fused_glue:
+            if self.use_program:
+                return self._decode_program(ids, pos)
             return self._decode_fused(ids, pos)
         sh = self.shapes
         T = ids.shape[0]

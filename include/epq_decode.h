@@ -101,6 +101,41 @@ int epq_decode_linear(const epq_store* stores, int32_t count, const void* x, int
                       int64_t ldx, int32_t prologue, float eps, void* const* outs, const int64_t* ldo,
                       int32_t epilogue, void* stream);
 
+/* A decode program: the steps of one batch-1 decode token -- every layer's
+ * epq_decode_linear and epq_attn_rope_decode calls, in order -- recorded once
+ * and then run as ONE persistent cooperative kernel per token (one CTA per SM).
+ * Its weight stream runs through all linear steps without a break; the steps
+ * themselves are separated by grid-wide completion counters.  Results are those
+ * of the same calls made one by one (the attention's split merge order aside).
+ *
+ * Steps keep the pointers they are given: the activation buffers, KV caches,
+ * position and stores must stay where they are for the program's lifetime (copy
+ * a new token's input into the same buffer, write the position into the same
+ * int64).  Linear steps: m = 1, bf16 activations, EPQ_LAYOUT_MMA16 stores,
+ * k <= 32768, one scale dtype for the whole program.  Attention steps: bf16,
+ * head_dim 64 or 128, heads / kv_heads of 1, 2, 4, 8 or 16, 16-byte aligned
+ * caches.
+ *
+ * Life cycle: epq_program_create; epq_program_add_linear / _add_attention per
+ * step; epq_program_workspace_bytes; epq_program_finalize (uploads the step
+ * table into the caller's workspace, 256-byte aligned, on `stream`, and
+ * synchronizes it); epq_program_run per token (a counter reset and one kernel
+ * launch on `stream`; capturable in a CUDA graph); epq_program_destroy.  A
+ * program is tied to the device it was finalized on, and two runs of one
+ * program must not overlap. */
+typedef struct epq_program epq_program;
+int epq_program_create(epq_program** out);
+int epq_program_add_linear(epq_program* p, const epq_store* stores, int32_t count, const void* x, int64_t ldx,
+                           int32_t prologue, float eps, void* const* outs, const int64_t* ldo, int32_t epilogue);
+int epq_program_add_attention(epq_program* p, const void* q, const void* k, const void* v, const int64_t* pos,
+                              int32_t heads, int32_t kv_heads, int32_t head_dim, const float* cos_tab,
+                              const float* sin_tab, void* k_cache, void* v_cache, int64_t max_len, int32_t qk_norm,
+                              float eps, float scale, void* out);
+int64_t epq_program_workspace_bytes(epq_program* p);
+int epq_program_finalize(epq_program* p, void* workspace, int64_t workspace_bytes, void* stream);
+int epq_program_run(epq_program* p, void* stream);
+void epq_program_destroy(epq_program* p);
+
 #ifdef __cplusplus
 }
 #endif
