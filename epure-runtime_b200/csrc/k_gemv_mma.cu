@@ -43,10 +43,11 @@
 //   interleaved so their gathers and MMAs overlap.
 // * Full rows per CTA (no split over k between CTAs): one CTA per SM owns a
 //   contiguous range of 16-row blocks ("units").  At the end of a unit every
-//   warp drops its partial sums into one of kSlots shared-memory slots and
-//   counts itself in with a shared-memory atomic; the last warp to arrive adds
-//   the 16 warps' sums in warp order (deterministic) and runs the epilogue.
-//   No CTA-wide barrier per unit, so warps run ahead by up to the ring depth.
+//   consumer warp drops its partial sums into one of kSlots shared-memory slots
+//   and arrives on the slot's mbarrier; a dedicated reducer warp adds the 16
+//   warps' sums in warp order (deterministic), runs the epilogue and frees the
+//   slot.  No CTA-wide barrier per unit and no consumer warp held up by a
+//   reduction, so warps run ahead by up to the ring depth.
 // * Fused decode glue (epq_decode_linear): the prologue can replace x by
 //   RMSNorm(x) (weight 1) while staging it, the epilogue can add the result
 //   into a residual stream in place (h = h + dtype(out)), and a paired launch
@@ -72,13 +73,16 @@ namespace {
 
 constexpr int kConsumerWarps = 16;
 constexpr int kConsumers = kConsumerWarps * 32;
-constexpr int kThreads = kConsumers + 32;       // + one producer warp
+constexpr int kProducerWarp = kConsumerWarps;   // streams the ring
+constexpr int kReducerWarp = kConsumerWarps + 1; // sums finished units and runs the epilogue
+constexpr int kThreads = kConsumers + 64;
 constexpr int kStages = 3;
 constexpr int kSlots = kStages + 1;             // unit reduction slots (see the ring argument below)
 constexpr int kChunkGroups = 32;                // groups per chunk
 constexpr int kStageIdx = kChunkGroups * 512;   // 16 KB of index tiles
 constexpr int kStageBytes = kStageIdx + kChunkGroups * 64;
-constexpr int kBarBytes = 256;                  // mbarriers + slot counters
+constexpr int kBarBytes = 256;                  // ring and slot mbarriers
+constexpr int kCbStageBytes = 2048;             // codebook staging for the replica build / RMSNorm scratch
 constexpr int kMaxXSmem = 64 * 1024;            // activations staged in shared memory up to this
 constexpr int kMaxSmem = 227 * 1024;
 // Shared-window layout.  The dynamic block starts at a small window address
@@ -90,7 +94,7 @@ constexpr int kMaxSmem = 227 * 1024;
 // it: mbarriers + counters, then the stage ring (so base + kLowBytes <=
 // kRepWin); above it: the reduction slots, then the staged activations.
 constexpr uint32_t kRepWin = 65536;
-constexpr uint32_t kLowBytes = kBarBytes + kStages * kStageBytes;
+constexpr uint32_t kLowBytes = kBarBytes + kStages * kStageBytes + kCbStageBytes;
 constexpr uint32_t kHighWin = 2 * kRepWin;
 constexpr uint32_t kWaitLimit = 1u << 22;       // bounded mbarrier waits
 
@@ -170,6 +174,18 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
                  : "r"(addr));
     return v;
 }
+// A 128-bit shared load done only by lanes with `p` set; the others get zeros
+// without issuing a request (so a warp whose upper lanes are idle costs one
+// shared-memory wavefront instead of four).
+__device__ __forceinline__ uint4 lds128_if(uint32_t addr, int p) {
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    asm volatile(
+        "{\n .reg .pred q;\n setp.ne.b32 q, %5, 0;\n"
+        " @q ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n}\n"
+        : "+r"(v.x), "+r"(v.y), "+r"(v.z), "+r"(v.w)
+        : "r"(addr), "r"(p));
+    return v;
+}
 template <bool kF32>
 __device__ __forceinline__ float lds_scale(uint32_t addr) {
     if constexpr (kF32) {
@@ -232,6 +248,29 @@ __device__ __forceinline__ void consumers_sync() {
     asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory");
 }
 
+// Shared-memory barriers at the start of the dynamic block: the ring's full /
+// empty pairs, then per reduction slot a "full" barrier (the 16 consumer warps
+// have written their partial sums) and a "free" one (the reducer warp is done).
+struct Bars {
+    uint32_t full, empty, slot_full, slot_free;
+    __device__ explicit Bars(uint32_t sbase)
+        : full(sbase), empty(sbase + 8 * kStages), slot_full(sbase + 16 * kStages),
+          slot_free(sbase + 16 * kStages + 8 * kSlots) {}
+};
+static_assert(16 * kStages + 16 * kSlots <= kBarBytes, "barrier block");
+
+__device__ __forceinline__ void init_bars(const Bars& B) {
+    for (int s = 0; s < kStages; ++s) {
+        mbar_init(B.full + 8 * s, 1);
+        mbar_init(B.empty + 8 * s, kConsumerWarps);
+    }
+    for (int s = 0; s < kSlots; ++s) {
+        mbar_init(B.slot_full + 8 * s, kConsumerWarps);
+        mbar_init(B.slot_free + 8 * s, 1);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -265,13 +304,14 @@ __device__ void build_replica(const MmaStore& S, uint2* rep, int part, uint2* st
 
 // kT (1 or 2) tiles of one chunk, interleaved so their gathers and MMAs overlap:
 // tile t is group gl0 + 16 t of the chunk (one 16-row block x 128 weights), its
-// products go to accumulator chain t.  Lanes whose activation row is past m
-// load no activations (their B columns are never stored).
+// products go to accumulator chain t.  Lanes whose B column is past the m
+// activation rows (xact0 / xact1 zero) load no activations: their columns of
+// the product are never stored, so they multiply zeros.
 template <bool kBf16, int kNT, bool kScaleF32, bool kXSmem, int kT>
 __device__ __forceinline__ void mma_tiles(float (&acc)[2][kNT][4], const uint32_t sdst, const int gl0, const int g0,
                                           const uint32_t lanebase, const uint32_t xs0, const uint32_t xs1,
                                           const uint16_t* xg0, const uint16_t* xg1, const int k_lane,
-                                          const int lane) {
+                                          const int lane, const int xact0, const int xact1) {
     constexpr int kScaleBytes = kScaleF32 ? 4 : 2;
     const int gq = lane >> 2;
     uint32_t wlo[kT][2], whi[kT][2], sc0[kT], sc1[kT];
@@ -295,12 +335,11 @@ __device__ __forceinline__ void mma_tiles(float (&acc)[2][kNT][4], const uint32_
 #pragma unroll
         for (int t = 0; t < kT; ++t) {
             const int gidx = g0 + gl0 + 16 * t;
-            // Lanes whose activation row is past m read row m - 1 (their output
-            // columns are never stored), so every lane loads and none is predicated.
             if constexpr (kXSmem) {
-                bx[t] = lds128(xs0 + (gidx * 4 + p) * 64);
-                if constexpr (kNT == 2) by[t] = lds128(xs1 + (gidx * 4 + p) * 64);
+                bx[t] = lds128_if(xs0 + (gidx * 4 + p) * 64, xact0);
+                if constexpr (kNT == 2) by[t] = lds128_if(xs1 + (gidx * 4 + p) * 64, xact1);
             } else {
+                // Global loads: lanes past m read row m - 1 (their columns are never stored).
                 const int col = gidx * 128 + 32 * p;
                 const uint2 z = make_uint2(0u, 0u);
                 const uint2 b0 = col < k_lane ? __ldg(reinterpret_cast<const uint2*>(xg0 + col)) : z;
@@ -445,15 +484,14 @@ __device__ __forceinline__ void prepare_linear(const MmaParams& P, int u_begin, 
 // prepare_linear must have run for this range.
 template <bool kBf16, int kNT, bool kScaleF32, bool kXSmem, bool kProg>
 __device__ __forceinline__ void run_linear(const MmaParams& P, int u_begin, int u_end, uint8_t* smem,
-                                           uint32_t sbase, uint32_t& ring) {
-    const uint32_t bar_full = sbase;
-    const uint32_t bar_empty = bar_full + 8 * kStages;
-    int* cnt = reinterpret_cast<int*>(smem + 16 * kStages);
+                                           uint32_t sbase, uint32_t& ring, uint32_t& uc) {
+    const Bars B(sbase);
     const uint32_t stage0 = sbase + kBarBytes;
     uint2* rep = reinterpret_cast<uint2*>(smem + (kRepWin - sbase));
     float* slots = reinterpret_cast<float*>(smem + (kHighWin - sbase));
     uint16_t* xs = reinterpret_cast<uint16_t*>(smem + (P.x_off - sbase));   // [m][kpad] when kXSmem
-    uint2* cb_stage = reinterpret_cast<uint2*>(slots);   // 2 KB; slots are free until a unit ends
+    uint2* cb_stage = reinterpret_cast<uint2*>(smem + kBarBytes + kStages * kStageBytes);
+    float* scratch = reinterpret_cast<float*>(cb_stage);   // RMSNorm partial sums (m x 16 floats)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int cpu = P.chunks_per_unit, parts = P.parts, count = P.count, M = P.m;
     const int n_chunks = (u_end - u_begin) * cpu * parts;
@@ -487,7 +525,7 @@ __device__ __forceinline__ void run_linear(const MmaParams& P, int u_begin, int 
             }
             if (norm) {
                 for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-                if (lane == 0) slots[row * kConsumerWarps + warp] = ss;   // slots are free until the first unit ends
+                if (lane == 0) scratch[row * kConsumerWarps + warp] = ss;
             }
         }
         if (norm) {
@@ -495,7 +533,7 @@ __device__ __forceinline__ void run_linear(const MmaParams& P, int u_begin, int 
             for (int row = 0; row < M; ++row) {
                 float ss = 0.f;
 #pragma unroll
-                for (int w = 0; w < kConsumerWarps; ++w) ss += slots[row * kConsumerWarps + w];
+                for (int w = 0; w < kConsumerWarps; ++w) ss += scratch[row * kConsumerWarps + w];
                 const float r = rsqrtf(ss / (float)P.k + P.eps);
                 for (int i = threadIdx.x; i < per_row; i += kConsumers) {
                     uint2* p = reinterpret_cast<uint2*>(xs + xperm(row, P.kpad, i * 4));
@@ -516,6 +554,7 @@ __device__ __forceinline__ void run_linear(const MmaParams& P, int u_begin, int 
     consumers_sync();
 
     const int k_lane = P.k - 4 * q;   // global-load path: column c is in range iff c < k_lane
+    const int xact0 = gq < M, xact1 = gq + 8 < M;   // this lane's B columns are activation rows
     const uint32_t lane16 = (kRepWin & 0xffff0000u) | ((uint32_t)(lane & 15) << 3);
     // Two accumulator chains (the two tiles a warp takes per chunk) keep dependent MMAs apart.
     float acc[2][kNT][4];
@@ -523,7 +562,7 @@ __device__ __forceinline__ void run_linear(const MmaParams& P, int u_begin, int 
     for (int e = 0; e < 2; ++e)
 #pragma unroll
         for (int h = 0; h < kNT; ++h) acc[e][h][0] = acc[e][h][1] = acc[e][h][2] = acc[e][h][3] = 0.f;
-    int u = u_begin, part = 0, c = 0, uslot = 0;
+    int u = u_begin, part = 0, c = 0;
     for (int j = 0; j < n_chunks; ++j, ++ring) {
         const uint32_t stage = ring % kStages;
         if (parts == 1 && c == 0 && u >= c_next) {
@@ -540,20 +579,23 @@ __device__ __forceinline__ void run_linear(const MmaParams& P, int u_begin, int 
         const uint32_t lanebase = lane16 | (uint32_t)((parts == 2 ? part : 0) << 7);
         const int g0 = c * kChunkGroups;
         const int ngc = min(kChunkGroups, ng - g0);
-        mbar_wait(bar_full + 8 * stage, (ring / kStages) & 1);
+        mbar_wait(B.full + 8 * stage, (ring / kStages) & 1);
         const uint32_t sdst = stage0 + stage * kStageBytes;
         if (warp + kConsumerWarps < ngc)
             mma_tiles<kBf16, kNT, kScaleF32, kXSmem, 2>(acc, sdst, warp, g0, lanebase, xs0, xs1, xg0, xg1, k_lane,
-                                                        lane);
+                                                        lane, xact0, xact1);
         else if (warp < ngc)
             mma_tiles<kBf16, kNT, kScaleF32, kXSmem, 1>(acc, sdst, warp, g0, lanebase, xs0, xs1, xg0, xg1, k_lane,
-                                                        lane);
+                                                        lane, xact0, xact1);
         __syncwarp();
-        if (lane == 0) mbar_arrive(bar_empty + 8 * stage);   // this warp is done with the stage
+        if (lane == 0) mbar_arrive(B.empty + 8 * stage);   // this warp is done with the stage
         if (++c < cpu) continue;
         c = 0;
         // End of one part of a unit: this warp's partial sums into the unit's slot,
-        // laid out [part][warp][m][16 rows].
+        // laid out [part][warp][m][16 rows].  A slot is reused kSlots units later,
+        // once the reducer warp has released it.
+        const uint32_t uslot = uc % kSlots;
+        if (part == 0 && uc >= (uint32_t)kSlots) mbar_wait(B.slot_free + 8 * uslot, ((uc / kSlots) - 1) & 1);
         {
             float* mine = slots + uslot * P.slot_floats + (part * kConsumerWarps + warp) * 16 * M;
 #pragma unroll
@@ -573,57 +615,65 @@ __device__ __forceinline__ void run_linear(const MmaParams& P, int u_begin, int 
         }
         if (++part < parts) continue;
         part = 0;
-        // Count this warp in; the 16th warp to arrive reduces the unit.  A slot is
-        // reused kSlots units later: by then its reducer is done, because a warp
-        // can run at most kStages chunks (>= units) ahead of the slowest warp and
-        // kSlots = kStages + 1.
-        __syncwarp();
-        int last = 0;
-        if (lane == 0) {
-            __threadfence_block();
-            last = atomicAdd(&cnt[uslot], 1) == kConsumerWarps - 1;
+        __syncwarp();   // the warp's partial sums precede lane 0's (releasing) arrival
+        if (lane == 0) mbar_arrive(B.slot_full + 8 * uslot);
+        ++u;
+        ++uc;
+    }
+}
+
+// Reducer warp: for every unit of [u_begin, u_end), in order, waits until the 16
+// consumer warps have dropped their partial sums into its slot, adds them in
+// warp order (deterministic), runs the epilogue and releases the slot.
+template <bool kBf16, int kNT, bool kProg>
+__device__ __forceinline__ void reduce_linear(const MmaParams& P, int u_begin, int u_end, uint8_t* smem,
+                                              uint32_t sbase, uint32_t& uc) {
+    const Bars B(sbase);
+    const float* slots = reinterpret_cast<const float*>(smem + (kHighWin - sbase));
+    const int lane = threadIdx.x & 31;
+    const int parts = P.parts, count = P.count, M = P.m;
+    const int per = 16 * M;   // floats per warp per part
+    int cur = parts == 2 ? 0 : store_of(P, u_begin);
+    int c_next = (parts == 1 && cur + 1 < count) ? P.st[cur + 1].unit0 : INT_MAX;
+    for (int u = u_begin; u < u_end; ++u, ++uc) {
+        if (parts == 1 && u >= c_next) {
+            cur = store_of(P, u);
+            c_next = cur + 1 < count ? P.st[cur + 1].unit0 : INT_MAX;
         }
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (last) {
-            __syncwarp();
-            __threadfence_block();
-            const int sidx0 = parts == 2 ? 0 : cur;
-            const MmaStore& S = P.st[sidx0];
-            const int rowbase = (parts == 2 ? u : u - S.unit0) * 16;
-            const float* base = slots + uslot * P.slot_floats;
-            const int per = 16 * M;   // floats per warp per part
-            const int n_rows = S.n;
-            void* const out = S.out;
-            const int64_t ldo = S.ldo;
-            for (int e = lane; e < per; e += 32) {
-                const int rr = e & 15, mm = e >> 4;
-                const int row = rowbase + rr;
-                float v0 = 0.f, v1 = 0.f;
+        const uint32_t uslot = uc % kSlots;
+        mbar_wait(B.slot_full + 8 * uslot, (uc / kSlots) & 1);
+        const MmaStore& S = P.st[parts == 2 ? 0 : cur];
+        const int rowbase = (parts == 2 ? u : u - S.unit0) * 16;
+        const float* base = slots + uslot * P.slot_floats;
+        const int n_rows = S.n;
+        void* const out = S.out;
+        const int64_t ldo = S.ldo;
+        for (int e = lane; e < per; e += 32) {
+            const int rr = e & 15, mm = e >> 4;
+            const int row = rowbase + rr;
+            float v0 = 0.f, v1 = 0.f;
 #pragma unroll
-                for (int ww = 0; ww < kConsumerWarps; ++ww) v0 += base[ww * per + e];
-                if (parts == 2) {
+            for (int ww = 0; ww < kConsumerWarps; ++ww) v0 += base[ww * per + e];
+            if (parts == 2) {
 #pragma unroll
-                    for (int ww = 0; ww < kConsumerWarps; ++ww) v1 += base[(kConsumerWarps + ww) * per + e];
-                }
-                if (row < n_rows) {
-                    const int64_t o = (int64_t)mm * ldo + row;
-                    if (P.epilogue == EPQ_EPI_RESIDUAL) {
-                        const int dt = kBf16 ? EPQ_BF16 : EPQ_F16;
-                        store_f(out, dt, o, ld_act<kProg>(out, dt, o) + round_to(v0, dt));
-                    } else if (P.epilogue == EPQ_EPI_SILU_MUL) {
-                        const int dt = kBf16 ? EPQ_BF16 : EPQ_F16;
-                        const float gv = round_to(v0, dt), uv = round_to(v1, dt);
-                        store_f(out, dt, o, gv / (1.f + expf(-gv)) * uv);
-                    } else {
-                        store_f(out, P.out_dtype, o, v0);
-                    }
+                for (int ww = 0; ww < kConsumerWarps; ++ww) v1 += base[(kConsumerWarps + ww) * per + e];
+            }
+            if (row < n_rows) {
+                const int64_t o = (int64_t)mm * ldo + row;
+                if (P.epilogue == EPQ_EPI_RESIDUAL) {
+                    const int dt = kBf16 ? EPQ_BF16 : EPQ_F16;
+                    store_f(out, dt, o, ld_act<kProg>(out, dt, o) + round_to(v0, dt));
+                } else if (P.epilogue == EPQ_EPI_SILU_MUL) {
+                    const int dt = kBf16 ? EPQ_BF16 : EPQ_F16;
+                    const float gv = round_to(v0, dt), uv = round_to(v1, dt);
+                    store_f(out, dt, o, gv / (1.f + expf(-gv)) * uv);
+                } else {
+                    store_f(out, P.out_dtype, o, v0);
                 }
             }
-            __syncwarp();
-            if (lane == 0) cnt[uslot] = 0;
         }
-        ++u;
-        if (++uslot == kSlots) uslot = 0;
+        __syncwarp();   // the slot's reads (and the epilogue's stores) precede the release
+        if (lane == 0) mbar_arrive(B.slot_free + 8 * uslot);
     }
 }
 
@@ -635,36 +685,32 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const __grid_cons
         if (threadIdx.x == 0) atomicExch(&g_mma_wait_timeout, 1);
         return;
     }
-    const uint32_t bar_full = sbase;                       // kStages x 8 B
-    const uint32_t bar_empty = bar_full + 8 * kStages;     // kStages x 8 B
-    int* cnt = reinterpret_cast<int*>(smem + 16 * kStages);   // kSlots arrival counters
+    const Bars B(sbase);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int u_begin, u_end;
     unit_range(P.total_units, u_begin, u_end);
-
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; ++s) {
-            mbar_init(bar_full + 8 * s, 1);
-            mbar_init(bar_empty + 8 * s, kConsumerWarps);
-        }
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    if (threadIdx.x < kSlots) cnt[threadIdx.x] = 0;
+    if (threadIdx.x == 0) init_bars(B);
     __syncthreads();
 
-    uint32_t ring = 0;
-    if (warp == kConsumerWarps) {
+    uint32_t ring = 0, uc = 0;
+    if (warp == kProducerWarp) {
         // Weights do not depend on the previous kernel: stream them right away.
-        produce_linear<kScaleF32>(P, u_begin, u_end, bar_full, bar_empty, sbase + kBarBytes, lane, ring);
+        produce_linear<kScaleF32>(P, u_begin, u_end, B.full, B.empty, sbase + kBarBytes, lane, ring);
         pdl_trigger();
         return;
     }
+    if (warp == kReducerWarp) {
+        pdl_trigger();
+        pdl_wait();   // the residual stream belongs to the previous kernel until here
+        reduce_linear<kBf16, kNT, false>(P, u_begin, u_end, smem, sbase, uc);
+        return;
+    }
     uint2* rep = reinterpret_cast<uint2*>(smem + (kRepWin - sbase));
-    uint2* cb_stage = reinterpret_cast<uint2*>(smem + (kHighWin - sbase));
+    uint2* cb_stage = reinterpret_cast<uint2*>(smem + kBarBytes + kStages * kStageBytes);
     prepare_linear<kBf16>(P, u_begin, u_end, rep, cb_stage);
     pdl_trigger();
     pdl_wait();   // x (and the output buffers) belong to the previous kernel until here
-    run_linear<kBf16, kNT, kScaleF32, kXSmem, false>(P, u_begin, u_end, smem, sbase, ring);
+    run_linear<kBf16, kNT, kScaleF32, kXSmem, false>(P, u_begin, u_end, smem, sbase, ring, uc);
 }
 
 // ---------------------------------------------------------------------------
@@ -940,33 +986,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (threadIdx.x == 0) atomicExch(&g_mma_wait_timeout, 1);
         return;
     }
-    const uint32_t bar_full = sbase;
-    const uint32_t bar_empty = bar_full + 8 * kStages;
-    int* cnt = reinterpret_cast<int*>(smem + 16 * kStages);
+    const Bars B(sbase);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; ++s) {
-            mbar_init(bar_full + 8 * s, 1);
-            mbar_init(bar_empty + 8 * s, kConsumerWarps);
-        }
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    if (threadIdx.x < kSlots) cnt[threadIdx.x] = 0;
+    if (threadIdx.x == 0) init_bars(B);
     __syncthreads();
 
-    uint32_t ring = 0;
+    uint32_t ring = 0, uc = 0;
     int u_begin, u_end;
-    if (warp == kConsumerWarps) {
+    if (warp == kProducerWarp) {
         for (int s = 0; s < n_steps; ++s) {
             if (steps[s].kind != kStepLinear) continue;
             unit_range(steps[s].lin.total_units, u_begin, u_end);
-            produce_linear<kScaleF32>(steps[s].lin, u_begin, u_end, bar_full, bar_empty, sbase + kBarBytes, lane,
-                                      ring);
+            produce_linear<kScaleF32>(steps[s].lin, u_begin, u_end, B.full, B.empty, sbase + kBarBytes, lane, ring);
+        }
+        return;
+    }
+    if (warp == kReducerWarp) {
+        // The consumers release a step's units only after the grid barrier before
+        // it, and wait for this warp's last release before they arrive at the next.
+        for (int s = 0; s < n_steps; ++s) {
+            if (steps[s].kind != kStepLinear) continue;
+            unit_range(steps[s].lin.total_units, u_begin, u_end);
+            reduce_linear<kBf16, 1, true>(steps[s].lin, u_begin, u_end, smem, sbase, uc);
         }
         return;
     }
     uint2* rep = reinterpret_cast<uint2*>(smem + (kRepWin - sbase));
-    uint2* cb_stage = reinterpret_cast<uint2*>(smem + (kHighWin - sbase));
+    uint2* cb_stage = reinterpret_cast<uint2*>(smem + kBarBytes + kStages * kStageBytes);
     float* scr = reinterpret_cast<float*>(smem + (scr_off - sbase));
     // the staged K / V rows follow the warp records (16-byte aligned)
     uint16_t* kst = reinterpret_cast<uint16_t*>(smem + (kv_off - sbase));
@@ -979,7 +1025,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (s > 0) grid_wait(&bars[s - 1], gridDim.x);
         if (T.kind == kStepLinear) {
             unit_range(T.lin.total_units, u_begin, u_end);
-            if (u_begin < u_end) run_linear<kBf16, 1, kScaleF32, true, true>(T.lin, u_begin, u_end, smem, sbase, ring);
+            if (u_begin < u_end) {
+                run_linear<kBf16, 1, kScaleF32, true, true>(T.lin, u_begin, u_end, smem, sbase, ring, uc);
+                // The step's outputs are complete once the reducer has released its
+                // last unit (units are reduced in order).
+                if (threadIdx.x == 0) mbar_wait(B.slot_free + 8 * ((uc - 1) % kSlots), ((uc - 1) / kSlots) & 1);
+            }
         } else if (T.attn.head_dim == 128) {
             prog_attention<4>(T.attn, scr, kst, kst + kAttnRows * 128, recs, attn_counters);
         } else {
