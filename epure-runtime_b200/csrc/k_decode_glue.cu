@@ -38,12 +38,16 @@ __device__ __forceinline__ void pdl_enter() {
 }
 
 template <typename... KArgs, typename... Args>
-int launch_pdl_cluster(void (*kern)(KArgs...), dim3 grid, dim3 block, unsigned cluster_x, cudaStream_t st,
-                       const char* what, Args... args) {
+int launch_pdl_cluster(void (*kern)(KArgs...), dim3 grid, dim3 block, unsigned cluster_x, size_t smem,
+                       cudaStream_t st, const char* what, Args... args) {
+    if (smem > 0) {
+        const int rc = set_smem_limit(reinterpret_cast<const void*>(kern), (int)smem, what);
+        if (rc != EPQ_OK) return rc;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
-    cfg.dynamicSmemBytes = 0;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -484,6 +488,32 @@ __device__ __forceinline__ float ld_cluster_f32(const float* local, uint32_t ran
     return v;
 }
 
+// Cached rows a CTA stages in shared memory per pass.
+constexpr int kClusterRows = 64;
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+    const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(gsrc) : "memory");
+}
+
+// Rows [base, base + cnt) of kv head kvh except position P into kst / vst, as
+// asynchronous 16-byte copies.
+template <int kDims>
+__device__ __forceinline__ void stage_rows(const __nv_bfloat16* k_cache, const __nv_bfloat16* v_cache, int KV,
+                                           int kvh, int64_t base, int cnt, int64_t P, __nv_bfloat16* kst,
+                                           __nv_bfloat16* vst) {
+    constexpr int hd = kDims * 32, pieces = hd / 8;
+    for (int i = threadIdx.x; i < cnt * pieces; i += kAttnWarps * 32) {
+        const int r = i / pieces, c = i - r * pieces;
+        const int64_t t = base + r;
+        if (t == P) continue;
+        const int64_t off = (t * KV + kvh) * hd + c * 8;
+        cp_async16(kst + r * hd + c * 8, k_cache + off);
+        cp_async16(vst + r * hd + c * 8, v_cache + off);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
 template <int kDims, int kGroup>
 __global__ void __launch_bounds__(kAttnWarps * 32) attn_rope_cluster_kernel(
     const __nv_bfloat16* __restrict__ q_in, const __nv_bfloat16* __restrict__ k_in,
@@ -491,16 +521,32 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_rope_cluster_kernel(
     __nv_bfloat16* __restrict__ v_cache, const int64_t* __restrict__ pos, int KV,
     const float* __restrict__ cos_t, const float* __restrict__ sin_t, int qk_norm, float eps, float scale,
     __nv_bfloat16* __restrict__ out, int64_t max_len) {
-    pdl_enter();
     constexpr int hd = kDims * 32;
     constexpr int kRec = hd + 2;                   // merged acc[hd], max, sum of one head
     __shared__ float wm[kAttnWarps][kGroup], wl[kAttnWarps][kGroup];
     __shared__ float wacc[kAttnWarps][kGroup][hd];
     __shared__ float rec[kGroup * kRec];            // this CTA's record, read by rank 0
+    extern __shared__ __align__(16) uint8_t dyn[];  // the staged K / V rows
+    __nv_bfloat16* kst = reinterpret_cast<__nv_bfloat16*>(dyn);
+    __nv_bfloat16* vst = kst + kClusterRows * hd;
     const int split = blockIdx.x, kvh = blockIdx.y;   // the cluster spans the splits of one kv head
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // The position and the cached rows before it were written by launches that
+    // completed before this grid's predecessor started (the previous token's
+    // position update and attention), so they are read before the dependency
+    // wait: the first pass of K / V rows streams in while the q / k / v
+    // projection that precedes this kernel is still finishing.
     const int64_t P = pos[0];
-    if (P < 0 || P >= max_len) {   // the same position for every CTA: the whole cluster returns here
+    const bool valid = P >= 0 && P < max_len;
+    const int64_t n = P + 1;
+    const int64_t chunk = (n + kClusterSplits - 1) / kClusterSplits;
+    const int64_t t0 = split * chunk, t1 = valid ? min(n, t0 + chunk) : t0;
+    int64_t base = t0;
+    int cnt = (int)min((int64_t)kClusterRows, t1 - base);
+    if (cnt > 0) stage_rows<kDims>(k_cache, v_cache, KV, kvh, base, cnt, P, kst, vst);
+    pdl_enter();
+    if (!valid) {   // the same position for every CTA: the whole cluster returns here
+        asm volatile("cp.async.wait_all;" ::: "memory");
         if (split == 0) {
             for (int e = threadIdx.x; e < kGroup * hd; e += kAttnWarps * 32)
                 out[(int64_t)kvh * kGroup * hd + e] = __float2bfloat16_rn(0.f);
@@ -508,21 +554,6 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_rope_cluster_kernel(
         }
         return;
     }
-    const int64_t n = P + 1;
-    const int64_t chunk = (n + kClusterSplits - 1) / kClusterSplits;
-    const int64_t t0 = split * chunk, t1 = min(n, t0 + chunk);
-    // the cached rows this warp will read first, issued before anything else
-    auto load_row = [&](int64_t t, float (&kr)[kDims], float (&vr)[kDims]) {
-        const int64_t kb = (t * KV + kvh) * hd + lane * kDims;
-#pragma unroll
-        for (int d = 0; d < kDims; ++d) {
-            kr[d] = __bfloat162float(k_cache[kb + d]);
-            vr[d] = __bfloat162float(v_cache[kb + d]);
-        }
-    };
-    float kn[kDims], vn[kDims];
-    int64_t t = t0 + warp;
-    if (t < t1 && t != P) load_row(t, kn, vn);
     float qv[kGroup][kDims], acc[kGroup][kDims], m[kGroup], l[kGroup];
 #pragma unroll
     for (int g = 0; g < kGroup; ++g) {
@@ -550,29 +581,58 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_rope_cluster_kernel(
             v_cache[cb + d] = __float2bfloat16_rn(vc[d]);
         }
     }
-    for (; t < t1; t += kAttnWarps) {
-        float kr[kDims], vr[kDims];
+    while (cnt > 0) {
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        if (warp == 0 && P >= base && P < base + cnt) {   // this position from registers
 #pragma unroll
-        for (int d = 0; d < kDims; ++d) {
-            kr[d] = t == P ? kc[d] : kn[d];
-            vr[d] = t == P ? vc[d] : vn[d];
+            for (int d = 0; d < kDims; ++d) {
+                kst[(P - base) * hd + lane * kDims + d] = __float2bfloat16_rn(kc[d]);
+                vst[(P - base) * hd + lane * kDims + d] = __float2bfloat16_rn(vc[d]);
+            }
         }
-        const int64_t tn = t + kAttnWarps;
-        if (tn < t1 && tn != P) load_row(tn, kn, vn);   // next row in flight while this one is scored
+        __syncthreads();
+        // each warp scores every kAttnWarps-th staged row, four at a time
+        for (int j0 = warp; j0 < cnt; j0 += 4 * kAttnWarps) {
+            float kr[4][kDims];
 #pragma unroll
-        for (int g = 0; g < kGroup; ++g) {
-            float sc = 0.f;
+            for (int u = 0; u < 4; ++u) {
+                const int j = min(j0 + u * kAttnWarps, cnt - 1);
 #pragma unroll
-            for (int d = 0; d < kDims; ++d) sc += qv[g][d] * kr[d];
-            for (int o = 16; o > 0; o >>= 1) sc += __shfl_xor_sync(0xffffffffu, sc, o);
-            sc *= scale;
-            const float mn = fmaxf(m[g], sc);
-            const float corr = expf(m[g] - mn), pw = expf(sc - mn);
-            l[g] = l[g] * corr + pw;
+                for (int d = 0; d < kDims; ++d) kr[u][d] = __bfloat162float(kst[j * hd + lane * kDims + d]);
+            }
 #pragma unroll
-            for (int d = 0; d < kDims; ++d) acc[g][d] = acc[g][d] * corr + pw * vr[d];
-            m[g] = mn;
+            for (int g = 0; g < kGroup; ++g) {
+                float sc[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    float a = 0.f;
+#pragma unroll
+                    for (int d = 0; d < kDims; ++d) a += qv[g][d] * kr[u][d];
+                    sc[u] = a;
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], o);
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int j = j0 + u * kAttnWarps;
+                    if (j >= cnt) break;
+                    const float s = sc[u] * scale;
+                    const float mn = fmaxf(m[g], s);
+                    const float corr = expf(m[g] - mn), pw = expf(s - mn);
+                    l[g] = l[g] * corr + pw;
+#pragma unroll
+                    for (int d = 0; d < kDims; ++d)
+                        acc[g][d] = acc[g][d] * corr + pw * __bfloat162float(vst[j * hd + lane * kDims + d]);
+                    m[g] = mn;
+                }
+            }
         }
+        base += cnt;
+        cnt = (int)min((int64_t)kClusterRows, t1 - base);
+        __syncthreads();   // every warp is done with the staged rows
+        if (cnt > 0) stage_rows<kDims>(k_cache, v_cache, KV, kvh, base, cnt, P, kst, vst);
     }
 #pragma unroll
     for (int g = 0; g < kGroup; ++g) {
@@ -887,7 +947,8 @@ int epq_attn_rope_decode(const void* q, const void* k, const void* v, const int6
     auto* ob = static_cast<__nv_bfloat16*>(out);
     const dim3 grid(kClusterSplits, kv_heads);
 #define EPQ_ATTN_ROPE(D, G)                                                                                     \
-    return launch_pdl_cluster(attn_rope_cluster_kernel<D, G>, grid, dim3(kAttnWarps * 32), kClusterSplits, st, \
+    return launch_pdl_cluster(attn_rope_cluster_kernel<D, G>, grid, dim3(kAttnWarps * 32), kClusterSplits,     \
+                              (size_t)(2 * kClusterRows * D * 32 * 2), st,                                     \
                               "epq_attn_rope_decode", qb, kb, vb, kcb, vcb, pos, (int)kv_heads, cos_tab, sin_tab,  \
                               (int)qk_norm, eps, scale, ob, max_len)
     if (head_dim == 128) {
