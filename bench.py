@@ -483,12 +483,12 @@ def run_finetune(args, rank, world, local_rank):
     for _ in range(args.warmup):
         step(ids)
     torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize(dev)
     stream = torch.cuda.current_stream(dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clocks:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
         ev0.record(stream)
         for _ in range(args.steps):
             step(ids)
@@ -658,14 +658,18 @@ def _max_over_ranks(vals, dev, world):
     return [float(v) for v in t]
 
 
-def _timed_replays(fn, steps, dev, stream, clocks_index=None):
-    """CUDA-event time (ms) of ``steps`` calls of fn() on ``stream``, bracketed by syncs."""
+def _timed_replays(fn, steps, dev, stream, clocks_index=None, barrier=None):
+    """CUDA-event time (ms) of ``steps`` calls of fn() on ``stream``, bracketed by syncs.
+    ``barrier`` (multi-rank) lines the ranks up after the clock sampler has started,
+    so that its start-up does not skew one rank against the others."""
     import torch
-    torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     sampler = ClockSampler(clocks_index) if clocks_index is not None else None
     if sampler:
         sampler.__enter__()
+    if barrier is not None:
+        barrier()
+    torch.cuda.synchronize(dev)
     e0.record(stream)
     for _ in range(steps):
         fn()
@@ -706,9 +710,8 @@ def run_model(args, rank, world, local_rank):
     for _ in range(args.warmup):
         dec._graph.replay()
     torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
-    ms, clocks = _timed_replays(dec._graph.replay, args.steps, dev, stream, local_rank)
+    ms, clocks = _timed_replays(dec._graph.replay, args.steps, dev, stream, local_rank,
+                                barrier=dist.barrier if world > 1 else None)
     if world > 1:
         dist.barrier()
 
@@ -919,12 +922,13 @@ def run_ours(args, rank, world, local_rank):
         runner.replay()
     torch.cuda.synchronize(dev)
 
-    # device-resident: K graph replays between two events on the replay stream
-    barrier()
-    torch.cuda.synchronize(dev)
+    # device-resident: K graph replays between two events on the replay stream;
+    # the clock sampler starts (NVML, first sample) before the ranks line up
     stream = torch.cuda.current_stream(dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clocks:
+        barrier()
+        torch.cuda.synchronize(dev)
         ev0.record(stream)
         for _ in range(args.steps):
             runner.replay()
