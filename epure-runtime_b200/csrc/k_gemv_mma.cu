@@ -806,6 +806,26 @@ __device__ __forceinline__ void stage_kv(const AttnStep& A, int kvh, int64_t bas
     asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
+// The first pass of an attention step's K / V rows, issued before the grid
+// barrier that precedes the step: the position and the cached rows before it
+// come from earlier launches, not from the step before (which only writes q /
+// k / v), so their HBM latency overlaps the wait.
+template <int kDims>
+__device__ void prestage_attention(const AttnStep& A, uint16_t* kst, uint16_t* vst) {
+    const int64_t P = A.pos[0];
+    if (P < 0 || P >= A.max_len) return;
+    const int64_t n = P + 1;
+    const int S = (int)min((int64_t)A.splits, (n + kAttnRows - 1) / kAttnRows);
+    const int blk = blockIdx.x;
+    if (blk >= A.kv_heads * S) return;
+    const int kvh = blk / S, split = blk - kvh * S;
+    const int64_t chunk = (n + S - 1) / S;
+    const int64_t t0 = split * chunk, t1 = min(n, t0 + chunk);
+    const int cnt = (int)min((int64_t)kAttnRows, t1 - t0);
+    if (cnt > 0) stage_kv<kDims>(A, kvh, t0, cnt, P, kst, vst);
+}
+
+
 // Attention step.  The positions 0..P are split over S CTAs per kv head, S the
 // fewest splits (at most A.splits) that keep a CTA's range within kAttnRows, so
 // a short context needs no cross-CTA merge.  A CTA stages its K / V rows in
@@ -817,9 +837,10 @@ __device__ __forceinline__ void stage_kv(const AttnStep& A, int kvh, int64_t bas
 // the CTA; with S > 1 one record per (split, head) goes to global memory and
 // the last CTA of the kv head merges them in split order.  Same arithmetic as
 // the epq_attn_rope_decode kernels (their split merge order aside).
+// `prestaged`: prestage_attention has issued the first pass already.
 template <int kDims>
 __device__ void prog_attention(const AttnStep& A, float* scr, uint16_t* kst, uint16_t* vst, float* recs,
-                               unsigned* counters) {
+                               unsigned* counters, bool prestaged) {
     constexpr int hd = kDims * 32, kRec = hd + 2;
     const int KV = A.kv_heads, group = A.heads / KV;
     const int blk = blockIdx.x;
@@ -842,7 +863,7 @@ __device__ void prog_attention(const AttnStep& A, float* scr, uint16_t* kst, uin
     const int64_t t0 = split * chunk, t1 = min(n, t0 + chunk);
     int64_t base = t0;
     int cnt = (int)min((int64_t)kAttnRows, t1 - base);
-    if (cnt > 0) stage_kv<kDims>(A, kvh, base, cnt, P, kst, vst);
+    if (cnt > 0 && !prestaged) stage_kv<kDims>(A, kvh, base, cnt, P, kst, vst);
 
     const int qh = kvh * group + g;
     float qv[kDims], acc[kDims], kc[kDims], vc[kDims];
@@ -1022,6 +1043,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int s = 0; s < n_steps; ++s) {
         const ProgStep& T = steps[s];
+        if (T.kind == kStepAttention) {
+            if (T.attn.head_dim == 128) prestage_attention<4>(T.attn, kst, kst + kAttnRows * 128);
+            else prestage_attention<2>(T.attn, kst, kst + kAttnRows * 64);
+        }
         if (s > 0) grid_wait(&bars[s - 1], gridDim.x);
         if (T.kind == kStepLinear) {
             unit_range(T.lin.total_units, u_begin, u_end);
@@ -1032,9 +1057,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (threadIdx.x == 0) mbar_wait(B.slot_free + 8 * ((uc - 1) % kSlots), ((uc - 1) / kSlots) & 1);
             }
         } else if (T.attn.head_dim == 128) {
-            prog_attention<4>(T.attn, scr, kst, kst + kAttnRows * 128, recs, attn_counters);
+            prog_attention<4>(T.attn, scr, kst, kst + kAttnRows * 128, recs, attn_counters, true);
         } else {
-            prog_attention<2>(T.attn, scr, kst, kst + kAttnRows * 64, recs, attn_counters);
+            prog_attention<2>(T.attn, scr, kst, kst + kAttnRows * 64, recs, attn_counters, true);
         }
         grid_arrive(&bars[s]);
         if (s + 1 < n_steps && steps[s + 1].kind == kStepLinear) {
