@@ -80,7 +80,7 @@ RMS_EPS = {"qwen3-1.7b": 1e-6, "llama3-8b": 1e-5, "llama3-70b": 1e-5}
 # (dram__bytes_read.sum + dram__bytes_write.sum over the launch's algorithmic
 # bytes); chain = chain_kernel on a 4-layer chain.
 NCU_TRAFFIC_RATIO = {"per-linear": 31249152 / 31264768,
-                     "chain": (232937728 + 24145664) / 232349696,
+                     "chain": (232708096 + 5034240) / 232349696,
                      "program": None}
 
 

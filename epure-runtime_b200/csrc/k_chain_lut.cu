@@ -183,6 +183,21 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
         "l"(src), "r"(bytes), "r"(bar)
         : "memory");
 }
+// The weight stream is read once per token: evict-first in L2, so that it does not
+// push the split-k partial sums (rewritten every token) out to DRAM.
+__device__ __forceinline__ uint64_t evict_first_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+__device__ __forceinline__ void bulk_g2s_stream(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar,
+                                                uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            dst),
+        "l"(src), "r"(bytes), "r"(bar), "l"(pol)
+        : "memory");
+}
 // Partial sums travel as 8-byte elements (fp32 value, 32-bit step tag); an aligned
 // 8-byte access is single-copy atomic, so a reader that sees the expected tag sees
 // the value written with it.
@@ -201,6 +216,16 @@ __device__ __forceinline__ uint64_t ldcg_u64(const uint64_t* p) {
 }
 __device__ __forceinline__ void stg_u64x2(uint64_t* p, uint64_t a, uint64_t b) {
     asm volatile("st.global.v2.u64 [%0], {%1,%2};" ::"l"(p), "l"(a), "l"(b) : "memory");
+}
+// Split-k partial sums are re-read by the next step and rewritten a few steps
+// later: evict-last in L2, so they stay there instead of being written back.
+__device__ __forceinline__ uint64_t evict_last_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+__device__ __forceinline__ void stg_u64x2_keep(uint64_t* p, uint64_t a, uint64_t b, uint64_t pol) {
+    asm volatile("st.global.L2::cache_hint.v2.u64 [%0], {%1,%2}, %3;" ::"l"(p), "l"(a), "l"(b), "l"(pol) : "memory");
 }
 __device__ __forceinline__ ulonglong2 ldsys_u64x2(const uint64_t* p) {   // peer or own memory, no caching
     ulonglong2 v;
@@ -310,6 +335,7 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
 
     if (warp == kConsumerWarps) {
         // ---------------- producer: stream every step's tiles into the ring ----------------
+        const uint64_t pol = evict_first_policy();
         int i = 0;
         for (int j = 0; j < n_steps; ++j) {
             const ChainStepD& S = steps[j];
@@ -325,10 +351,11 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
                 const uint32_t dst = stage_addr(stage);
                 if (lane == 0) {
                     mbar_expect_tx(bar_full + 8 * stage, nt * 512u + nt * 16u * esz);
-                    bulk_g2s(dst, C.idx + ((int64_t)g * C.rb + rb0) * 512, nt * 512u, bar_full + 8 * stage);
-                    bulk_g2s(dst + kStageIdx,
-                             static_cast<const char*>(C.scale) + ((int64_t)g * C.s_g + (int64_t)rb0 * 16) * esz,
-                             nt * 16u * esz, bar_full + 8 * stage);
+                    bulk_g2s_stream(dst, C.idx + ((int64_t)g * C.rb + rb0) * 512, nt * 512u, bar_full + 8 * stage,
+                                    pol);
+                    bulk_g2s_stream(dst + kStageIdx,
+                                    static_cast<const char*>(C.scale) + ((int64_t)g * C.s_g + (int64_t)rb0 * 16) * esz,
+                                    nt * 16u * esz, bar_full + 8 * stage, pol);
                 }
                 __syncwarp();
                 ++i;
@@ -338,6 +365,7 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
     }
 
     // ---------------- consumers ----------------
+    const uint64_t keep_pol = evict_last_policy();
     const int team = lane >> 3, tl = lane & 7;
     // Double-buffered staging (parity flips per change), so a new table's inputs
     // can be written while no warp still needs the previous ones.
@@ -660,8 +688,8 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const uint8_t* __res
                 const uint32_t sa = sdst + kStageIdx + tile * 16 * esz + 2 * tl * esz;
                 const float s0 = lds_scale(sa, f32), s1 = lds_scale(sa + esz, f32);
                 const int64_t row = (int64_t)(rb0 + tile) * 16 + 2 * tl;
-                stg_u64x2(pout + C.part_off + (int64_t)g * C.rb * 16 + row, tagged(a3[0] * s0, tag),
-                          tagged(a3[1] * s1, tag));
+                stg_u64x2_keep(pout + C.part_off + (int64_t)g * C.rb * 16 + row, tagged(a3[0] * s0, tag),
+                               tagged(a3[1] * s1, tag), keep_pol);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(bar_empty + 8 * stage);

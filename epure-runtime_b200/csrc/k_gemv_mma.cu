@@ -238,10 +238,27 @@ __device__ __forceinline__ void mbar_wait(uint32_t bar, uint32_t parity) {
         if (mbar_try_wait(bar, parity)) return;
     atomicExch(&g_mma_wait_timeout, 1);
 }
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+// The weight stream (index tiles and scales) is read once per call: evict-first in
+// L2, so that it does not push the KV rows, activations and codebooks out.
+__device__ __forceinline__ uint64_t evict_first_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar,
+                                         uint64_t pol) {
     asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-        "l"(src), "r"(bytes), "r"(bar)
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            dst),
+        "l"(src), "r"(bytes), "r"(bar), "l"(pol)
+        : "memory");
+}
+__device__ __forceinline__ void tma_load_2d_stream(uint32_t dst, const void* tmap, uint32_t bar, int c0, int c1,
+                                                   uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+        "l"(tmap), "r"(c0), "r"(c1), "r"(bar), "l"(pol)
         : "memory");
 }
 __device__ __forceinline__ void consumers_sync() {
@@ -423,6 +440,7 @@ template <bool kScaleF32>
 __device__ __forceinline__ void produce_linear(const MmaParams& P, int u_begin, int u_end, uint32_t bar_full,
                                                uint32_t bar_empty, uint32_t stage0, int lane, uint32_t& ring) {
     constexpr int kScaleBytes = kScaleF32 ? 4 : 2;
+    const uint64_t pol = evict_first_policy();
     const int cpu = P.chunks_per_unit, parts = P.parts, count = P.count;
     const int n_chunks = (u_end - u_begin) * cpu * parts;
     int si = parts == 2 ? 0 : store_of(P, u_begin);
@@ -451,8 +469,8 @@ __device__ __forceinline__ void produce_linear(const MmaParams& P, int u_begin, 
         // the store's last are zero-filled, and the full box is counted).
         if (lane == 0) {
             mbar_expect_tx(bar_full + 8 * stage, ngc * 512 + kChunkGroups * 16 * kScaleBytes);
-            bulk_g2s(dst, S.idx + ((int64_t)rb * S.ng + g0) * 512, ngc * 512, bar_full + 8 * stage);
-            sm100::tma_load_2d(dst + kStageIdx, &S.smap, bar_full + 8 * stage, rb * 16, g0);
+            bulk_g2s(dst, S.idx + ((int64_t)rb * S.ng + g0) * 512, ngc * 512, bar_full + 8 * stage, pol);
+            tma_load_2d_stream(dst + kStageIdx, &S.smap, bar_full + 8 * stage, rb * 16, g0, pol);
         }
         __syncwarp();
         if (++c == cpu) {
