@@ -79,6 +79,8 @@ constexpr int kThreads = kConsumers + 64;
 constexpr int kStages = 3;
 constexpr int kSlots = kStages + 1;             // unit reduction slots (see the ring argument below)
 constexpr int kChunkGroups = 32;                // groups per chunk
+constexpr int kTileSets = kChunkGroups / kConsumerWarps;   // tiles a consumer warp takes per chunk
+static_assert(kTileSets * kConsumerWarps == kChunkGroups, "consumer warps must divide a chunk");
 constexpr int kStageIdx = kChunkGroups * 512;   // 16 KB of index tiles
 constexpr int kStageBytes = kStageIdx + kChunkGroups * 64;
 constexpr int kBarBytes = 256;                  // ring and slot mbarriers
@@ -319,13 +321,13 @@ __device__ void build_replica(const MmaStore& S, uint2* rep, int part, uint2* st
     }
 }
 
-// kT (1 or 2) tiles of one chunk, interleaved so their gathers and MMAs overlap:
-// tile t is group gl0 + 16 t of the chunk (one 16-row block x 128 weights), its
-// products go to accumulator chain t.  Lanes whose B column is past the m
+// kT (1 .. kTileSets) tiles of one chunk, interleaved so their gathers and MMAs
+// overlap: tile t is group gl0 + kConsumerWarps t of the chunk (one 16-row block x
+// 128 weights), its products go to accumulator chain t.  Lanes whose B column is past the m
 // activation rows (xact0 / xact1 zero) load no activations: their columns of
 // the product are never stored, so they multiply zeros.
 template <bool kBf16, int kNT, bool kScaleF32, bool kXSmem, int kT>
-__device__ __forceinline__ void mma_tiles(float (&acc)[2][kNT][4], const uint32_t sdst, const int gl0, const int g0,
+__device__ __forceinline__ void mma_tiles(float (&acc)[kTileSets][kNT][4], const uint32_t sdst, const int gl0, const int g0,
                                           const uint32_t lanebase, const uint32_t xs0, const uint32_t xs1,
                                           const uint16_t* xg0, const uint16_t* xg1, const int k_lane,
                                           const int lane, const int xact0, const int xact1) {
@@ -334,7 +336,7 @@ __device__ __forceinline__ void mma_tiles(float (&acc)[2][kNT][4], const uint32_
     uint32_t wlo[kT][2], whi[kT][2], sc0[kT], sc1[kT];
 #pragma unroll
     for (int t = 0; t < kT; ++t) {
-        const int gl = gl0 + 16 * t;
+        const int gl = gl0 + kConsumerWarps * t;
         const uint4 w = lds128(sdst + gl * 512 + lane * 16);
         wlo[t][0] = w.x;
         wlo[t][1] = w.y;
@@ -351,7 +353,7 @@ __device__ __forceinline__ void mma_tiles(float (&acc)[2][kNT][4], const uint32_
         uint4 bx[kT], by[kT];
 #pragma unroll
         for (int t = 0; t < kT; ++t) {
-            const int gidx = g0 + gl0 + 16 * t;
+            const int gidx = g0 + gl0 + kConsumerWarps * t;
             if constexpr (kXSmem) {
                 bx[t] = lds128_if(xs0 + (gidx * 4 + p) * 64, xact0);
                 if constexpr (kNT == 2) by[t] = lds128_if(xs1 + (gidx * 4 + p) * 64, xact1);
@@ -575,9 +577,9 @@ __device__ __forceinline__ void run_linear(const MmaParams& P, int u_begin, int 
     const int xact0 = gq < M, xact1 = gq + 8 < M;   // this lane's B columns are activation rows
     const uint32_t lane16 = (kRepWin & 0xffff0000u) | ((uint32_t)(lane & 15) << 3);
     // Two accumulator chains (the two tiles a warp takes per chunk) keep dependent MMAs apart.
-    float acc[2][kNT][4];
+    float acc[kTileSets][kNT][4];
 #pragma unroll
-    for (int e = 0; e < 2; ++e)
+    for (int e = 0; e < kTileSets; ++e)
 #pragma unroll
         for (int h = 0; h < kNT; ++h) acc[e][h][0] = acc[e][h][1] = acc[e][h][2] = acc[e][h][3] = 0.f;
     int u = u_begin, part = 0, c = 0;
@@ -599,12 +601,23 @@ __device__ __forceinline__ void run_linear(const MmaParams& P, int u_begin, int 
         const int ngc = min(kChunkGroups, ng - g0);
         mbar_wait(B.full + 8 * stage, (ring / kStages) & 1);
         const uint32_t sdst = stage0 + stage * kStageBytes;
-        if (warp + kConsumerWarps < ngc)
-            mma_tiles<kBf16, kNT, kScaleF32, kXSmem, 2>(acc, sdst, warp, g0, lanebase, xs0, xs1, xg0, xg1, k_lane,
-                                                        lane, xact0, xact1);
-        else if (warp < ngc)
-            mma_tiles<kBf16, kNT, kScaleF32, kXSmem, 1>(acc, sdst, warp, g0, lanebase, xs0, xs1, xg0, xg1, k_lane,
-                                                        lane, xact0, xact1);
+        {
+            // this warp's tiles of the chunk: groups warp, warp + kConsumerWarps, ... < ngc
+            const int nt = warp < ngc ? min(kTileSets, (ngc - warp + kConsumerWarps - 1) / kConsumerWarps) : 0;
+#define EPQ_TILES(T)                                                                                            \
+    mma_tiles<kBf16, kNT, kScaleF32, kXSmem, T>(acc, sdst, warp, g0, lanebase, xs0, xs1, xg0, xg1, k_lane, lane, \
+                                                xact0, xact1)
+            if constexpr (kTileSets >= 4) {
+                if (nt == 4) EPQ_TILES(4);
+                else if (nt == 3) EPQ_TILES(3);
+                else if (nt == 2) EPQ_TILES(2);
+                else if (nt == 1) EPQ_TILES(1);
+            } else {
+                if (nt == 2) EPQ_TILES(2);
+                else if (nt == 1) EPQ_TILES(1);
+            }
+#undef EPQ_TILES
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive(B.empty + 8 * stage);   // this warp is done with the stage
         if (++c < cpu) continue;
@@ -619,16 +632,21 @@ __device__ __forceinline__ void run_linear(const MmaParams& P, int u_begin, int 
 #pragma unroll
             for (int h = 0; h < kNT; ++h) {
                 const int m0 = 8 * h + 2 * q;
+                float r[4] = {acc[0][h][0], acc[0][h][1], acc[0][h][2], acc[0][h][3]};
+#pragma unroll
+                for (int e = 1; e < kTileSets; ++e)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) r[j] += acc[e][h][j];
                 if (m0 < M) {
-                    mine[m0 * 16 + gq] = acc[0][h][0] + acc[1][h][0];
-                    mine[m0 * 16 + gq + 8] = acc[0][h][2] + acc[1][h][2];
+                    mine[m0 * 16 + gq] = r[0];
+                    mine[m0 * 16 + gq + 8] = r[2];
                 }
                 if (m0 + 1 < M) {
-                    mine[(m0 + 1) * 16 + gq] = acc[0][h][1] + acc[1][h][1];
-                    mine[(m0 + 1) * 16 + gq + 8] = acc[0][h][3] + acc[1][h][3];
+                    mine[(m0 + 1) * 16 + gq] = r[1];
+                    mine[(m0 + 1) * 16 + gq + 8] = r[3];
                 }
 #pragma unroll
-                for (int e = 0; e < 2; ++e) acc[e][h][0] = acc[e][h][1] = acc[e][h][2] = acc[e][h][3] = 0.f;
+                for (int e = 0; e < kTileSets; ++e) acc[e][h][0] = acc[e][h][1] = acc[e][h][2] = acc[e][h][3] = 0.f;
             }
         }
         if (++part < parts) continue;
