@@ -39,7 +39,8 @@
 //   ring guarded by mbarriers, two copies per chunk into this CTA's shared
 //   memory only: the index tiles (cp.async.bulk, one contiguous run) and the
 //   chunk's 16 x 32 scales (one 2-D cp.async.bulk.tensor box over the
-//   group-major scales).  16 consumer warps each take two tiles of a chunk,
+//   group-major scales), both with an evict-first L2 policy (the weights are
+//   read once per call).  16 consumer warps each take two tiles of a chunk,
 //   interleaved so their gathers and MMAs overlap.
 // * Full rows per CTA (no split over k between CTAs): one CTA per SM owns a
 //   contiguous range of 16-row blocks ("units").  At the end of a unit every
