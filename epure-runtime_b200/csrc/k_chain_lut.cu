@@ -177,12 +177,6 @@ __device__ __forceinline__ void mbar_wait(uint32_t bar, uint32_t parity) {
     }
     atomicExch(&g_chain_error, 1);
 }
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-        "l"(src), "r"(bytes), "r"(bar)
-        : "memory");
-}
 // The weight stream is read once per token: evict-first in L2, so that it does not
 // push the split-k partial sums (rewritten every token) out to DRAM.
 __device__ __forceinline__ uint64_t evict_first_policy() {

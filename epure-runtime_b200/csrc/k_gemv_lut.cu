@@ -20,9 +20,11 @@
 //   128-bit load.  The lookup address is one PRMT: the index byte becomes
 //   address bits 8..15, the lane's position and the table base fill the rest.
 // * Teams of 8 lanes.  Each team owns one 16-row tile; a lane covers 4 of
-//   the 32 positions (rotated per team so the 32 lanes of a warp always hit
-//   32 different banks), then a 3-step butterfly leaves every lane with the
-//   sums of 2 rows.
+//   the 32 positions (position blocks permuted per team, block i ^ team, so
+//   the 32 lanes of a warp always hit 32 different banks), then a 3-step
+//   butterfly leaves every lane with the sums of 2 rows.  The four blocks are
+//   added as (b0 + b1) + (b2 + b3) whatever the permutation, so a tile's sums
+//   are the same bits in every launch shape (fused stores, split grids).
 // * Split over k with a deterministic reduction.  The grid is one CTA per SM;
 //   CTA c streams a contiguous range of tiles in (store, group, row-block)
 //   order.  Each finished tile writes its 16 scaled group sums to
@@ -137,7 +139,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_lut_kernel(const __grid_cons
                 const uint8_t* tp = tile_base + (int64_t)(rb0 + tile) * 512;
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
-                    const int pos = tl + 8 * ((i + team) & 3);
+                    const int pos = tl + 8 * (i ^ team);
                     dst[i] = ldg_stream(tp + pos * 16);
                 }
             } else {
@@ -194,7 +196,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_lut_kernel(const __grid_cons
         uint32_t base[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i)
-            base[i] = kTBase | (uint32_t)(slot * 128 + 4 * (tl + 8 * ((i + team) & 3)));
+            base[i] = kTBase | (uint32_t)(slot * 128 + 4 * (tl + 8 * (i ^ team)));
 
         const int n16 = S.rb * 16;
         for (; q < n_quads; q += kWarps) {
@@ -202,11 +204,19 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_lut_kernel(const __grid_cons
             float ns0, ns1;
             load_quad(q + kWarps, nxt);
             load_scales(q + kWarps, ns0, ns1);
-            float acc[16];
+            // Position blocks {0, 1} and {2, 3} are summed apart and then added: the
+            // blocks a lane holds are permuted by team (i ^ team), but the pairs are
+            // the same sets for every team, so a tile's sums do not depend on which
+            // team (and so which launch shape) processed it.
+            float acc[16], acc2[16];
 #pragma unroll
-            for (int r = 0; r < 16; ++r) acc[r] = 0.f;
+            for (int r = 0; r < 16; ++r) acc[r] = acc2[r] = 0.f;
+            lookup16(cur[0], base[0], acc);
+            lookup16(cur[1], base[1], acc);
+            lookup16(cur[2], base[2], acc2);
+            lookup16(cur[3], base[3], acc2);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) lookup16(cur[i], base[i], acc);
+            for (int r = 0; r < 16; ++r) acc[r] += acc2[r];
 
             // Butterfly over the 8 lanes of the team: lane tl ends with rows 2tl, 2tl+1.
             const bool b2 = tl & 4, b1 = tl & 2, b0 = tl & 1;

@@ -177,17 +177,15 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
                  : "r"(addr));
     return v;
 }
-// A 128-bit shared load done only by lanes with `p` set; the others get zeros
-// without issuing a request (so a warp whose upper lanes are idle costs one
+// A 128-bit shared load into `v` done only by lanes with `p` set; the others keep
+// `v` without issuing a request (so a warp whose upper lanes are idle costs one
 // shared-memory wavefront instead of four).
-__device__ __forceinline__ uint4 lds128_if(uint32_t addr, int p) {
-    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+__device__ __forceinline__ void lds128_if(uint4& v, uint32_t addr, int p) {
     asm volatile(
         "{\n .reg .pred q;\n setp.ne.b32 q, %5, 0;\n"
         " @q ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n}\n"
         : "+r"(v.x), "+r"(v.y), "+r"(v.z), "+r"(v.w)
         : "r"(addr), "r"(p));
-    return v;
 }
 template <bool kF32>
 __device__ __forceinline__ float lds_scale(uint32_t addr) {
@@ -349,15 +347,20 @@ __device__ __forceinline__ void mma_tiles(float (&acc)[kTileSets][kNT][4], const
         sc0[t] = cvt_pair<kBf16>(s0, s0);
         sc1[t] = cvt_pair<kBf16>(s1, s1);
     }
+    // The B fragments keep their registers across the four k-step pairs: a lane that
+    // loads no activations keeps the zeros set here once per tile (its product columns
+    // are never stored).
+    uint4 bx[kT], by[kT];
+#pragma unroll
+    for (int t = 0; t < kT; ++t) bx[t] = by[t] = make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
-        uint4 bx[kT], by[kT];
 #pragma unroll
         for (int t = 0; t < kT; ++t) {
             const int gidx = g0 + gl0 + kConsumerWarps * t;
             if constexpr (kXSmem) {
-                bx[t] = lds128_if(xs0 + (gidx * 4 + p) * 64, xact0);
-                if constexpr (kNT == 2) by[t] = lds128_if(xs1 + (gidx * 4 + p) * 64, xact1);
+                lds128_if(bx[t], xs0 + (gidx * 4 + p) * 64, xact0);
+                if constexpr (kNT == 2) lds128_if(by[t], xs1 + (gidx * 4 + p) * 64, xact1);
             } else {
                 // Global loads: lanes past m read row m - 1 (their columns are never stored).
                 const int col = gidx * 128 + 32 * p;
@@ -449,9 +452,13 @@ __device__ __forceinline__ void produce_linear(const MmaParams& P, int u_begin, 
     int si = parts == 2 ? 0 : store_of(P, u_begin);
     int s_next = (parts == 1 && si + 1 < count) ? P.st[si + 1].unit0 : INT_MAX;
     int u = u_begin, part = 0, c = 0;
-    for (int j = 0; j < n_chunks; ++j, ++ring) {
-        const uint32_t stage = ring % kStages;
-        if (ring >= (uint32_t)kStages) mbar_wait(bar_empty + 8 * stage, ((ring / kStages) - 1) & 1);
+    // Ring position `ring` as (stage, phase); a stage is refilled once the consumers
+    // have released its previous use (phase - 1), nothing to wait for on the first lap.
+    uint32_t stage = ring % kStages, phase = (ring / kStages) & 1;
+    bool lapped = ring >= (uint32_t)kStages;
+    ring += (uint32_t)n_chunks;
+    for (int j = 0; j < n_chunks; ++j) {
+        if (lapped) mbar_wait(bar_empty + 8 * stage, phase ^ 1);
         int rb;
         if (parts == 2) {
             si = part;
@@ -476,6 +483,11 @@ __device__ __forceinline__ void produce_linear(const MmaParams& P, int u_begin, 
             tma_load_2d_stream(dst + kStageIdx, &S.smap, bar_full + 8 * stage, rb * 16, g0, pol);
         }
         __syncwarp();
+        if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1;
+            lapped = true;
+        }
         if (++c == cpu) {
             c = 0;
             if (++part == parts) {
@@ -584,8 +596,10 @@ __device__ __forceinline__ void run_linear(const MmaParams& P, int u_begin, int 
 #pragma unroll
         for (int h = 0; h < kNT; ++h) acc[e][h][0] = acc[e][h][1] = acc[e][h][2] = acc[e][h][3] = 0.f;
     int u = u_begin, part = 0, c = 0;
-    for (int j = 0; j < n_chunks; ++j, ++ring) {
-        const uint32_t stage = ring % kStages;
+    // Ring position `ring` as (stage, phase), advanced incrementally per chunk.
+    uint32_t stage = ring % kStages, phase = (ring / kStages) & 1;
+    ring += (uint32_t)n_chunks;
+    for (int j = 0; j < n_chunks; ++j, stage = stage + 1 == kStages ? 0 : stage + 1, phase ^= stage == 0) {
         if (parts == 1 && c == 0 && u >= c_next) {
             // New store (CTA-uniform): rebuild the codebook replica once every warp
             // is past the previous store's gathers.
@@ -600,7 +614,7 @@ __device__ __forceinline__ void run_linear(const MmaParams& P, int u_begin, int 
         const uint32_t lanebase = lane16 | (uint32_t)((parts == 2 ? part : 0) << 7);
         const int g0 = c * kChunkGroups;
         const int ngc = min(kChunkGroups, ng - g0);
-        mbar_wait(B.full + 8 * stage, (ring / kStages) & 1);
+        mbar_wait(B.full + 8 * stage, phase);
         const uint32_t sdst = stage0 + stage * kStageBytes;
         {
             // this warp's tiles of the chunk: groups warp, warp + kConsumerWarps, ... < ngc
