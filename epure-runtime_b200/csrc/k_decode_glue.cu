@@ -470,7 +470,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_rope_split_kernel(
 
 // Decode attention as thread-block clusters: the kClusterSplits CTAs of one
 // cluster split the positions of one kv head, and their partial softmax
-// records are merged over distributed shared memory by the cluster's rank 0
+// records are merged over distributed shared memory, each CTA merging one slice
+// of the kv head's outputs
 // (no workspace round trip, fence or completion counter).  Otherwise as
 // attn_rope_split_kernel: (q/k RMSNorm and) RoPE inside, this position's k / v
 // from registers and written into the caches by rank 0; each warp prefetches
@@ -525,7 +526,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_rope_cluster_kernel(
     constexpr int kRec = hd + 2;                   // merged acc[hd], max, sum of one head
     __shared__ float wm[kAttnWarps][kGroup], wl[kAttnWarps][kGroup];
     __shared__ float wacc[kAttnWarps][kGroup][hd];
-    __shared__ float rec[kGroup * kRec];            // this CTA's record, read by rank 0
+    __shared__ float rec[kGroup * kRec];            // this CTA's record, read by the whole cluster
     extern __shared__ __align__(16) uint8_t dyn[];  // the staged K / V rows
     __nv_bfloat16* kst = reinterpret_cast<__nv_bfloat16*>(dyn);
     __nv_bfloat16* vst = kst + kClusterRows * hd;
@@ -662,8 +663,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_rope_cluster_kernel(
         }
     }
     cluster_sync_all();   // every split's record is in its shared memory
-    if (split == 0) {
-        for (int e = threadIdx.x; e < kGroup * hd; e += kAttnWarps * 32) {
+    {
+        // Every CTA of the cluster merges one slice of the kv head's outputs, so the
+        // merge's dependent remote loads run once per thread (rank 0 alone took two turns).
+        constexpr int kSlice = (kGroup * hd + kClusterSplits - 1) / kClusterSplits;
+        const int e_end = min(kGroup * hd, (split + 1) * kSlice);
+        for (int e = split * kSlice + threadIdx.x; e < e_end; e += kAttnWarps * 32) {
             const int g = e / hd, d = e - g * hd;
             float mxs[kClusterSplits];
             float mx = -INFINITY;
@@ -683,7 +688,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_rope_cluster_kernel(
             out[(int64_t)(kvh * kGroup + g) * hd + d] = __float2bfloat16_rn(num / den);
         }
     }
-    cluster_sync_all();   // no CTA leaves while rank 0 still reads its record
+    cluster_sync_all();   // no CTA leaves while another still reads its record
 }
 
 // Arg-max of n floats (first index of the maximum, as torch.argmax): every CTA
